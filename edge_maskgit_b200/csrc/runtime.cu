@@ -1,0 +1,729 @@
+// runtime.cu -- the C ABI of libmgcuda.so: kernel-level entry points, the GGUF-backed
+// transformer runtime (the CUDA counterpart of mg::OpenCLRuntime, include/mg-opencl.hpp),
+// and the decode loop of src/mg-generate.cpp.
+#include "../../include/mgc.h"
+#include "kernels.h"
+#include "pack.h"
+#include "ptx.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <memory>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <unordered_map>
+#include <vector>
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+namespace mgc {
+__device__ int g_dev_error = 0;
+}
+
+using namespace mgc;
+
+namespace {
+
+thread_local std::string g_err;
+
+struct Err : std::runtime_error { using std::runtime_error::runtime_error; };
+
+#define CK(call)                                                                        \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            throw Err(std::string(#call) + ": " + cudaGetErrorString(e_));              \
+    } while (0)
+
+template <class F>
+int guard(F&& f) {
+    try { f(); return 0; }
+    catch (const std::exception& e) { g_err = e.what(); return -1; }
+}
+
+template <class T>
+T* dalloc(size_t n) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    return (T*)p;
+}
+template <class T>
+T* dupload(const T* h, size_t n) {
+    T* d = dalloc<T>(n);
+    CK(cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyHostToDevice));
+    return d;
+}
+
+// ----------------------------------------------------------------------- GGUF (v3) reader
+// Format of Model::load (mg-model.cpp:139-201): header, metadata KVs, tensor infos, data
+// aligned to general.alignment.  Tensors are referenced in the read-only mapping.
+struct GgufTensor { uint32_t type = 0; int64_t ne[4] = {1, 1, 1, 1}; const uint8_t* data = nullptr; size_t bytes = 0; };
+
+struct Gguf {
+    void* base = MAP_FAILED; size_t size = 0;
+    std::unordered_map<std::string, GgufTensor> tensors;
+    std::unordered_map<std::string, int64_t> ints;
+    std::unordered_map<std::string, float> floats;
+
+    ~Gguf() { if (base != MAP_FAILED) munmap(base, size); }
+
+    void open(const char* path) {
+        int fd = ::open(path, O_RDONLY);
+        if (fd < 0) throw Err(std::string("cannot open ") + path);
+        struct stat st{};
+        fstat(fd, &st);
+        size = (size_t)st.st_size;
+        base = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+        ::close(fd);
+        if (base == MAP_FAILED) throw Err("mmap failed");
+        const uint8_t* b = (const uint8_t*)base;
+        size_t p = 0;
+        auto need = [&](size_t n) { if (p + n > size) throw Err("gguf: unexpected EOF"); };
+        auto u32 = [&]() { need(4); uint32_t v; std::memcpy(&v, b + p, 4); p += 4; return v; };
+        auto u64 = [&]() { need(8); uint64_t v; std::memcpy(&v, b + p, 8); p += 8; return v; };
+        auto str = [&]() { uint64_t n = u64(); need(n); std::string s((const char*)b + p, n); p += n; return s; };
+        auto scalar_size = [](uint32_t t) -> size_t {
+            switch (t) { case 0: case 1: case 7: return 1; case 2: case 3: return 2;
+                         case 4: case 5: case 6: return 4; case 10: case 11: case 12: return 8; }
+            throw Err("gguf: unsupported metadata type");
+        };
+        if (u32() != 0x46554747u) throw Err("not a GGUF file");
+        if (u32() != 3) throw Err("unsupported GGUF version");
+        const uint64_t nt = u64(), nkv = u64();
+        for (uint64_t i = 0; i < nkv; i++) {
+            const std::string key = str();
+            const uint32_t t = u32();
+            if (t == 8) { str(); continue; }
+            if (t == 9) {
+                const uint32_t sub = u32(); const uint64_t n = u64();
+                for (uint64_t j = 0; j < n; j++) { if (sub == 8) str(); else { need(scalar_size(sub)); p += scalar_size(sub); } }
+                continue;
+            }
+            const size_t sz = scalar_size(t);
+            need(sz);
+            if (t == 6) { float f; std::memcpy(&f, b + p, 4); floats[key] = f; }
+            else if (t == 12) { double f; std::memcpy(&f, b + p, 8); floats[key] = (float)f; }
+            else {
+                int64_t v = 0;
+                switch (t) {
+                    case 0: case 7: v = b[p]; break; case 1: v = (int8_t)b[p]; break;
+                    case 2: { uint16_t x; std::memcpy(&x, b + p, 2); v = x; } break;
+                    case 3: { int16_t x; std::memcpy(&x, b + p, 2); v = x; } break;
+                    case 4: { uint32_t x; std::memcpy(&x, b + p, 4); v = x; } break;
+                    case 5: { int32_t x; std::memcpy(&x, b + p, 4); v = x; } break;
+                    case 10: { uint64_t x; std::memcpy(&x, b + p, 8); v = (int64_t)x; } break;
+                    case 11: { int64_t x; std::memcpy(&x, b + p, 8); v = x; } break;
+                }
+                ints[key] = v;
+            }
+            p += sz;
+        }
+        struct Info { std::string name; GgufTensor t; uint64_t off; };
+        std::vector<Info> infos(nt);
+        for (auto& in : infos) {
+            in.name = str();
+            const uint32_t nd = u32();
+            if (nd > 4) throw Err("gguf: too many dims on " + in.name);
+            for (uint32_t d = 0; d < nd; d++) in.t.ne[d] = (int64_t)u64();
+            in.t.type = u32();
+            in.off = u64();
+        }
+        const uint64_t align = ints.count("general.alignment") ? (uint64_t)ints["general.alignment"] : 32;
+        const size_t data0 = (p + align - 1) / align * align;
+        for (auto& in : infos) {
+            const int64_t n = in.t.ne[0] * in.t.ne[1] * in.t.ne[2] * in.t.ne[3];
+            switch (in.t.type) {
+                case 0: in.t.bytes = (size_t)n * 4; break;
+                case 8: in.t.bytes = (size_t)n / 32 * 34; break;
+                case 12: in.t.bytes = (size_t)n / 256 * 144; break;
+                default: in.t.bytes = 0; break;   // other types are not used by the transformer
+            }
+            in.t.data = b + data0 + in.off;
+            if (data0 + in.off + in.t.bytes > size) throw Err("gguf: tensor '" + in.name + "' past EOF");
+            tensors[in.name] = in.t;
+        }
+    }
+    const GgufTensor& req(const std::string& n) const {
+        auto it = tensors.find(n);
+        if (it == tensors.end()) throw Err("gguf: missing required tensor '" + n + "'");
+        return it->second;
+    }
+    int geti(const std::string& k, int dflt) const { auto it = ints.find(k); return it == ints.end() ? dflt : (int)it->second; }
+    float getf(const std::string& k, float dflt) const { auto it = floats.find(k); return it == floats.end() ? dflt : it->second; }
+};
+
+// Upload an [N][K] weight given as GGUF bytes (Q8_0 / Q4_K blocks, or row-major F32).
+QWeight upload_weight(int wtype, const void* host, int N, int K) {
+    QWeight w;
+    w.wtype = wtype; w.N = N; w.K = K;
+    if (wtype == 0) { w.f32 = dupload((const float*)host, (size_t)N * K); return w; }
+    if (wtype != 8 && wtype != 12) throw Err("unsupported weight type " + std::to_string(wtype));
+    if (K % 128 != 0 || (wtype == 12 && K % 256 != 0)) throw Err("qweight: K must be a multiple of 128 (256 for Q4_K)");
+    w.Npad = round_up(N, 128);
+    std::vector<int8_t> q; std::vector<float> sa, sb;
+    repack(wtype, (const uint8_t*)host, N, K, w.Npad, q, sa, sb);
+    w.q = dupload(q.data(), q.size());
+    w.sa = dupload(sa.data(), sa.size());
+    if (wtype == 12) w.sb = dupload(sb.data(), sb.size());
+    return w;
+}
+void free_weight(QWeight& w) {
+    cudaFree(w.q); cudaFree(w.sa); cudaFree(w.sb); cudaFree(w.f32);
+    w = QWeight{};
+}
+
+// Quantized-activation buffers for up to Mpad rows and K columns.
+ActQ alloc_actq(int Mpad, int K) {
+    ActQ a;
+    a.Mpad = Mpad;
+    a.q = dalloc<int8_t>((size_t)K * Mpad);
+    a.d = dalloc<float>((size_t)(K / 32) * Mpad);
+    a.c = dalloc<float>((size_t)(K / 32) * Mpad);
+    CK(cudaMemset(a.q, 0, (size_t)K * Mpad));
+    CK(cudaMemset(a.d, 0, sizeof(float) * (K / 32) * Mpad));
+    CK(cudaMemset(a.c, 0, sizeof(float) * (K / 32) * Mpad));
+    return a;
+}
+void free_actq(ActQ& a) { cudaFree(a.q); cudaFree(a.d); cudaFree(a.c); a = ActQ{}; }
+
+// Library scratch used by the standalone mgc_qgemm entry point (grown on demand, per device).
+struct Scratch { ActQ a; int Mpad = 0, K = 0; };
+std::map<int, Scratch> g_scratch;
+std::mutex g_scratch_mu;
+
+}  // namespace
+
+struct mgc_qweight { QWeight w; };
+
+extern "C" {
+
+const char* mgc_last_error(void) { return g_err.c_str(); }
+
+int mgc_device_error(void) {
+    int v = 0;
+    int rc = guard([&] {
+        CK(cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)));
+        const int zero = 0;
+        CK(cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int)));
+    });
+    return rc != 0 ? rc : v;
+}
+
+int mgc_pack_q8_0(const float* w, int64_t N, int64_t K, uint8_t* out) {
+    if (!w || !out || N <= 0 || K <= 0 || K % 32) { g_err = "mgc_pack_q8_0: K must be a positive multiple of 32"; return -1; }
+    pack_q8_0(w, N, K, out);
+    return 0;
+}
+int mgc_pack_q4_k(const float* w, int64_t N, int64_t K, uint8_t* out) {
+    if (!w || !out || N <= 0 || K <= 0 || K % 256) { g_err = "mgc_pack_q4_k: K must be a positive multiple of 256"; return -1; }
+    pack_q4_k(w, N, K, out);
+    return 0;
+}
+int mgc_dequant(int wtype, const uint8_t* w, int64_t N, int64_t K, float* out) {
+    if (!(wtype == 8 && K % 32 == 0) && !(wtype == 12 && K % 256 == 0)) { g_err = "mgc_dequant: bad type or K"; return -1; }
+    dequant(wtype, w, N, K, out);
+    return 0;
+}
+
+int mgc_quantize_act(const float* x, int M, int K, int8_t* qx, float* dx, int32_t* sumx, void* stream) {
+    if (M <= 0 || K <= 0 || K % 32) { g_err = "mgc_quantize_act: K must be a positive multiple of 32"; return -1; }
+    return guard([&] {
+        launch_quant_act_plain(x, M, K, qx, dx, sumx, (cudaStream_t)stream);
+        CK(cudaPeekAtLastError());
+    });
+}
+
+int mgc_qweight_create(int wtype, const void* w_host, int N, int K, mgc_qweight** out) {
+    return guard([&] {
+        if (!w_host || !out || N <= 0 || K <= 0) throw Err("mgc_qweight_create: bad arguments");
+        auto* q = new mgc_qweight();
+        try { q->w = upload_weight(wtype, w_host, N, K); }
+        catch (...) { delete q; throw; }
+        int dev; CK(cudaGetDevice(&dev));
+        CK(cudaSetDevice(dev));
+        if (qgemm_prepare() != 0) throw Err("qgemm: cannot set shared-memory limit");
+        *out = q;
+    });
+}
+void mgc_qweight_destroy(mgc_qweight* w) {
+    if (!w) return;
+    free_weight(w->w);
+    delete w;
+}
+
+int mgc_qgemm(const mgc_qweight* wq, const float* x, int M, const float* bias, int act, const float* resid,
+              float* y, void* stream) {
+    return guard([&] {
+        if (!wq || !x || !y || M <= 0) throw Err("mgc_qgemm: bad arguments");
+        const QWeight& w = wq->w;
+        cudaStream_t st = (cudaStream_t)stream;
+        if (w.wtype == 0) {
+            launch_gemm_f32(w.f32, x, M, w.N, w.K, bias, act, resid, y, st);
+            CK(cudaPeekAtLastError());
+            return;
+        }
+        int dev; CK(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        Scratch& s = g_scratch[dev];
+        const int Mpad = round_up(M, 128);
+        if (s.Mpad < Mpad || s.K < w.K) {
+            CK(cudaStreamSynchronize(st));
+            free_actq(s.a);
+            s.Mpad = std::max(s.Mpad, Mpad);
+            s.K = std::max(s.K, w.K);
+            s.a = alloc_actq(s.Mpad, s.K);
+        }
+        launch_quant_act_tiled(x, M, w.K, s.a, w.wtype == 12, st);
+        if (launch_qgemm(w, s.a, M, bias, act, resid, y, st) != 0)
+            throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+    });
+}
+
+int mgc_gemm_f32(const float* w, const float* x, int M, int N, int K, const float* bias, int act,
+                 const float* resid, float* y, void* stream) {
+    return guard([&] {
+        if (M <= 0 || N <= 0 || K <= 0) throw Err("mgc_gemm_f32: bad sizes");
+        launch_gemm_f32(w, x, M, N, K, bias, act, resid, y, (cudaStream_t)stream);
+        CK(cudaPeekAtLastError());
+    });
+}
+
+int mgc_layernorm_affine(const float* x, const float* gamma, const float* beta, int rows, int D, float eps,
+                         float* y, void* stream) {
+    return guard([&] {
+        if (rows <= 0 || D % 64 || D > 2048 || D <= 0) throw Err("mgc_layernorm_affine: D must be a multiple of 64, <= 2048");
+        launch_ln(x, gamma, beta, rows, D, eps, y, nullptr, false, (cudaStream_t)stream);
+        CK(cudaPeekAtLastError());
+    });
+}
+
+int mgc_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, void* stream) {
+    return guard([&] {
+        if (B <= 0 || S <= 0 || H <= 0) throw Err("mgc_flash_attn: bad sizes");
+        if (launch_flash_attn(qkv, B, S, H, Dh, scale, out, (cudaStream_t)stream) != 0)
+            throw Err("mgc_flash_attn: head_dim must be 48");
+    });
+}
+
+int mgc_embed(const float* tok, int vocab, const float* pos, int E, const int32_t* tokens, int B, int S,
+              float* out, void* stream) {
+    return guard([&] {
+        if (E % 64 || E > 2048 || B <= 0 || S <= 0) throw Err("mgc_embed: E must be a multiple of 64, <= 2048");
+        launch_embed(tok, vocab, pos, E, tokens, B, S, out, (cudaStream_t)stream);
+        CK(cudaPeekAtLastError());
+    });
+}
+
+}  // extern "C"
+
+// ============================================================================ runtime
+struct LayerW {
+    QWeight qkv, o, up, down;
+    float *bqkv = nullptr, *bo = nullptr, *bup = nullptr, *bdown = nullptr;
+    float *g1 = nullptr, *b1 = nullptr, *g2 = nullptr, *b2 = nullptr;
+};
+
+struct ProfRow { double ms = 0; int n = 0; };
+
+struct mgc_runtime {
+    int device = 0;
+    std::string dev_name;
+    cudaStream_t st = nullptr;
+    // hparams
+    int n_layer = 0, n_head = 0, E = 0, F = 0, Dh = 0, V = 0, n_tokens = 0, mask_id = -1, codebook = 0;
+    int n_pos = 0, wtype = 0;
+    float eps = 1e-12f, choice_temp = 4.5f;
+    // weights
+    float *tok = nullptr, *pos = nullptr, *g0 = nullptr, *b0 = nullptr;
+    std::vector<LayerW> layers;
+    QWeight proj;
+    float *bproj = nullptr, *gout = nullptr, *bout = nullptr, *obias = nullptr;
+    bool any_q4k = false;
+    std::vector<float*> f32_allocs;
+    // activations
+    int max_rows = 0, Mpad = 0;
+    float *x = nullptr, *t = nullptr, *qkv = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr;
+    int32_t* tokens = nullptr;
+    ActQ aE, aF;
+    // host staging (pinned)
+    int32_t* h_tokens = nullptr;
+    float* h_logits = nullptr;
+    // CUDA graphs keyed by (B, S, tokens ptr, logits ptr)
+    std::map<std::tuple<int, int, const void*, const void*>, cudaGraphExec_t> graphs;
+    // profiling
+    bool prof = false;
+    std::map<std::string, ProfRow> prof_rows;
+
+    float* up_f32(const GgufTensor& t, size_t n) {
+        if (t.type != 0) throw Err("expected an F32 tensor");
+        float* d = dupload((const float*)t.data, n);
+        f32_allocs.push_back(d);
+        return d;
+    }
+};
+
+namespace {
+
+QWeight load_linear(const Gguf& g, const std::vector<std::string>& names, int K, bool& any_q4k) {
+    // several [N_i][K] weights of one type stacked along N (q|k|v): rows are independent,
+    // so concatenating the GGUF bytes is the same as one [sum N_i][K] weight.
+    std::vector<uint8_t> bytes;
+    int N = 0; uint32_t type = 0;
+    for (size_t i = 0; i < names.size(); i++) {
+        const GgufTensor& t = g.req(names[i]);
+        if (t.ne[0] != K) throw Err("tensor '" + names[i] + "' has unexpected K");
+        if (i == 0) type = t.type;
+        else if (t.type != type) throw Err("fused weights of different types");
+        bytes.insert(bytes.end(), t.data, t.data + t.bytes);
+        N += (int)t.ne[1];
+    }
+    if (type == 12) any_q4k = true;
+    return upload_weight((int)type, bytes.data(), N, K);
+}
+
+// One linear layer: quantized path reads the tiled activation `a`, F32 path the f32 `xin`.
+void linear(mgc_runtime* rt, const QWeight& w, const float* xin, const ActQ& a, int M, const float* bias,
+            int act, const float* resid, float* y) {
+    if (w.wtype == 0) { launch_gemm_f32(w.f32, xin, M, w.N, w.K, bias, act, resid, y, rt->st); return; }
+    if (launch_qgemm(w, a, M, bias, act, resid, y, rt->st) != 0)
+        throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+}
+
+// Enqueue one transformer forward (build_transformer, mg-transformer.cpp:32-111) on rt->st.
+// dump (device, optional) receives the 51 named tensors back to back.
+void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits, float* dump) {
+    const int R = B * S, E = rt->E, F = rt->F;
+    if (R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
+    if (S > rt->n_pos) throw Err("forward: S exceeds n_positions");
+    cudaStream_t st = rt->st;
+    size_t doff = 0;
+    auto put = [&](const float* src, int w) {
+        if (!dump) return;
+        CK(cudaMemcpyAsync(dump + doff, src, sizeof(float) * (size_t)R * w, cudaMemcpyDeviceToDevice, st));
+        doff += (size_t)R * w;
+    };
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (rt->prof) { CK(cudaEventCreate(&e0)); CK(cudaEventCreate(&e1)); }
+    auto op = [&](const char* name, auto&& fn) {
+        if (!rt->prof) { fn(); return; }
+        CK(cudaEventRecord(e0, st));
+        fn();
+        CK(cudaEventRecord(e1, st));
+        CK(cudaEventSynchronize(e1));
+        float ms = 0; CK(cudaEventElapsedTime(&ms, e0, e1));
+        ProfRow& r = rt->prof_rows[name]; r.ms += ms; r.n++;
+    };
+    const bool qc = rt->any_q4k;
+    const char* mm = rt->wtype == 0 ? "MulMat(f32)" : "MulMat(q)";
+    op("GetRows+Norm", [&] { launch_embed_ln(rt->tok, rt->V, rt->pos, E, tokens, B, S, rt->g0, rt->b0, rt->eps,
+                                              rt->x, &rt->aE, qc, st); });
+    put(rt->x, E);
+    const float scale = 1.0f / std::sqrt((float)rt->Dh);
+    for (int l = 0; l < rt->n_layer; l++) {
+        const LayerW& L = rt->layers[l];
+        op(mm, [&] { linear(rt, L.qkv, rt->x, rt->aE, R, L.bqkv, 0, nullptr, rt->qkv); });
+        op("FlashAttention", [&] {
+            if (launch_flash_attn(rt->qkv, B, S, rt->n_head, rt->Dh, scale, rt->att, st) != 0)
+                throw Err("flash attention launch failed");
+        });
+        if (L.o.wtype != 0) op("Quantize", [&] { launch_quant_act_tiled(rt->att, R, E, rt->aE, qc, st); });
+        op(mm, [&] { linear(rt, L.o, rt->att, rt->aE, R, L.bo, 0, rt->x, rt->t); });
+        op("Norm", [&] { launch_ln(rt->t, L.g1, L.b1, R, E, rt->eps, rt->x, &rt->aE, qc, st); });
+        put(rt->x, E);
+        op(mm, [&] { linear(rt, L.up, rt->x, rt->aE, R, L.bup, 1, nullptr, rt->ff); });
+        if (L.down.wtype != 0) op("Quantize", [&] { launch_quant_act_tiled(rt->ff, R, F, rt->aF, qc, st); });
+        op(mm, [&] { linear(rt, L.down, rt->ff, rt->aF, R, L.bdown, 0, rt->x, rt->t); });
+        op("Norm", [&] { launch_ln(rt->t, L.g2, L.b2, R, E, rt->eps, rt->x, &rt->aE, qc, st); });
+        put(rt->x, E);
+    }
+    op(mm, [&] { linear(rt, rt->proj, rt->x, rt->aE, R, rt->bproj, 1, nullptr, rt->t); });
+    op("Norm", [&] { launch_ln(rt->t, rt->gout, rt->bout, R, E, rt->eps, rt->x, nullptr, false, st); });
+    put(rt->x, E);
+    op("MulMat(f32)", [&] { launch_gemm_f32(rt->tok, rt->x, R, rt->V, E, rt->obias, 0, nullptr, logits, st); });
+    put(logits, rt->V);
+    CK(cudaPeekAtLastError());
+    if (e0) { cudaEventDestroy(e0); cudaEventDestroy(e1); }
+}
+
+// Forward through a cached CUDA graph (captured on the first call for this key).
+void run_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits) {
+    if (rt->prof) { enqueue_forward(rt, tokens, B, S, logits, nullptr); return; }
+    auto key = std::make_tuple(B, S, (const void*)tokens, (const void*)logits);
+    auto it = rt->graphs.find(key);
+    if (it == rt->graphs.end()) {
+        cudaGraph_t g;
+        CK(cudaStreamBeginCapture(rt->st, cudaStreamCaptureModeThreadLocal));
+        try { enqueue_forward(rt, tokens, B, S, logits, nullptr); }
+        catch (...) { cudaStreamEndCapture(rt->st, &g); if (g) cudaGraphDestroy(g); throw; }
+        CK(cudaStreamEndCapture(rt->st, &g));
+        cudaGraphExec_t ex;
+        CK(cudaGraphInstantiate(&ex, g, 0));
+        cudaGraphDestroy(g);
+        it = rt->graphs.emplace(key, ex).first;
+    }
+    CK(cudaGraphLaunch(it->second, rt->st));
+}
+
+void check_dev_error() {
+    int v = 0;
+    CK(cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)));
+    if (v != 0) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int));
+        throw Err("a kernel gave up waiting (device error code " + std::to_string(v) + ")");
+    }
+}
+
+void destroy_runtime(mgc_runtime* rt) {
+    if (!rt) return;
+    cudaSetDevice(rt->device);
+    if (rt->st) cudaStreamSynchronize(rt->st);
+    for (auto& kv : rt->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& L : rt->layers) { free_weight(L.qkv); free_weight(L.o); free_weight(L.up); free_weight(L.down); }
+    free_weight(rt->proj);
+    for (float* p : rt->f32_allocs) cudaFree(p);
+    cudaFree(rt->x); cudaFree(rt->t); cudaFree(rt->qkv); cudaFree(rt->att); cudaFree(rt->ff);
+    cudaFree(rt->logits); cudaFree(rt->tokens);
+    free_actq(rt->aE); free_actq(rt->aF);
+    if (rt->h_tokens) cudaFreeHost(rt->h_tokens);
+    if (rt->h_logits) cudaFreeHost(rt->h_logits);
+    if (rt->st) cudaStreamDestroy(rt->st);
+    delete rt;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime** out) {
+    return guard([&] {
+        if (!path || !out || max_rows <= 0) throw Err("mgc_runtime_create: bad arguments");
+        std::unique_ptr<mgc_runtime, void (*)(mgc_runtime*)> rt(new mgc_runtime(), destroy_runtime);
+        rt->device = device;
+        CK(cudaSetDevice(device));
+        cudaDeviceProp prop;
+        CK(cudaGetDeviceProperties(&prop, device));
+        rt->dev_name = prop.name;
+        if (prop.major != 10) throw Err(std::string("libmgcuda needs an sm_100 GPU, found ") + prop.name);
+        CK(cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking));
+        if (qgemm_prepare() != 0) throw Err("qgemm: cannot set shared-memory limit");
+        Gguf g;
+        g.open(path);
+        rt->n_layer = g.geti("maskgit.n_layer", 0); rt->n_head = g.geti("maskgit.n_head", 0);
+        rt->E = g.geti("maskgit.n_embd", 0); rt->F = g.geti("maskgit.n_ffn", 0);
+        rt->Dh = g.geti("maskgit.head_dim", 0); rt->V = g.geti("maskgit.vocab_size", 0);
+        rt->n_tokens = g.geti("maskgit.n_tokens", 0); rt->mask_id = g.geti("maskgit.mask_token_id", -1);
+        rt->codebook = g.geti("maskgit.vqgan.codebook_size", 0);
+        rt->eps = g.getf("maskgit.layernorm_eps", 1e-12f);
+        rt->choice_temp = g.getf("maskgit.sampling.choice_temperature", 4.5f);
+        const int E = rt->E, F = rt->F;
+        if (E <= 0 || F <= 0 || rt->n_head * rt->Dh != E || E % 128 || F % 128)
+            throw Err("unsupported hyper-parameters (n_embd / n_ffn must be multiples of 128)");
+        const GgufTensor& tok = g.req("token_embd.weight");
+        const GgufTensor& pos = g.req("pos_embd.weight");
+        if (tok.ne[0] != E || tok.ne[1] != rt->V || pos.ne[0] != E) throw Err("embedding shapes do not match hparams");
+        rt->n_pos = (int)pos.ne[1];
+        rt->tok = rt->up_f32(tok, (size_t)E * rt->V);
+        rt->pos = rt->up_f32(pos, (size_t)E * rt->n_pos);
+        rt->g0 = rt->up_f32(g.req("token_embd_norm.weight"), E);
+        rt->b0 = rt->up_f32(g.req("token_embd_norm.bias"), E);
+        bool q4 = false;
+        for (int l = 0; l < rt->n_layer; l++) {
+            const std::string p = "blk." + std::to_string(l) + ".";
+            LayerW L;
+            L.qkv = load_linear(g, {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, E, q4);
+            L.o = load_linear(g, {p + "attn_o.weight"}, E, q4);
+            L.up = load_linear(g, {p + "ffn_up.weight"}, E, q4);
+            L.down = load_linear(g, {p + "ffn_down.weight"}, F, q4);
+            std::vector<float> bqkv;
+            for (const char* nm : {"attn_q.bias", "attn_k.bias", "attn_v.bias"}) {
+                const GgufTensor& t = g.req(p + nm);
+                bqkv.insert(bqkv.end(), (const float*)t.data, (const float*)t.data + E);
+            }
+            L.bqkv = dupload(bqkv.data(), bqkv.size());
+            rt->f32_allocs.push_back(L.bqkv);
+            L.bo = rt->up_f32(g.req(p + "attn_o.bias"), E);
+            L.bup = rt->up_f32(g.req(p + "ffn_up.bias"), F);
+            L.bdown = rt->up_f32(g.req(p + "ffn_down.bias"), E);
+            L.g1 = rt->up_f32(g.req(p + "attn_norm.weight"), E);
+            L.b1 = rt->up_f32(g.req(p + "attn_norm.bias"), E);
+            L.g2 = rt->up_f32(g.req(p + "ffn_norm.weight"), E);
+            L.b2 = rt->up_f32(g.req(p + "ffn_norm.bias"), E);
+            rt->layers.push_back(L);
+        }
+        rt->proj = load_linear(g, {"output_proj.weight"}, E, q4);
+        rt->bproj = rt->up_f32(g.req("output_proj.bias"), E);
+        rt->gout = rt->up_f32(g.req("output_norm.weight"), E);
+        rt->bout = rt->up_f32(g.req("output_norm.bias"), E);
+        rt->obias = rt->up_f32(g.req("output.bias"), rt->V);
+        rt->any_q4k = q4;
+        rt->wtype = rt->n_layer > 0 ? rt->layers[0].qkv.wtype : rt->proj.wtype;
+        // activations
+        rt->max_rows = max_rows;
+        rt->Mpad = round_up(max_rows, 128);
+        const size_t R = (size_t)rt->Mpad;
+        rt->x = dalloc<float>(R * E); rt->t = dalloc<float>(R * E); rt->qkv = dalloc<float>(R * 3 * E);
+        rt->att = dalloc<float>(R * E); rt->ff = dalloc<float>(R * F); rt->logits = dalloc<float>(R * rt->V);
+        rt->tokens = dalloc<int32_t>(R);
+        rt->aE = alloc_actq(rt->Mpad, E);
+        rt->aF = alloc_actq(rt->Mpad, F);
+        CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
+        CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
+        CK(cudaDeviceSynchronize());
+        *out = rt.release();
+    });
+}
+
+void mgc_runtime_destroy(mgc_runtime* rt) { destroy_runtime(rt); }
+
+int mgc_runtime_hparams(const mgc_runtime* rt, int32_t o[10]) {
+    if (!rt) return -1;
+    const int32_t v[10] = {rt->n_layer, rt->n_head, rt->E, rt->F, rt->Dh, rt->V, rt->n_tokens, rt->mask_id,
+                           rt->codebook, rt->wtype};
+    std::memcpy(o, v, sizeof(v));
+    return 0;
+}
+const char* mgc_runtime_device_name(const mgc_runtime* rt) { return rt ? rt->dev_name.c_str() : ""; }
+void* mgc_runtime_stream(mgc_runtime* rt) { return rt ? (void*)rt->st : nullptr; }
+
+int mgc_runtime_sync(mgc_runtime* rt) {
+    return guard([&] {
+        CK(cudaSetDevice(rt->device));
+        CK(cudaStreamSynchronize(rt->st));
+        check_dev_error();
+    });
+}
+
+int mgc_transformer_forward_dev(mgc_runtime* rt, const int32_t* tokens_dev, int B, int S, float* logits_dev) {
+    return guard([&] {
+        if (!rt || B <= 0 || S <= 0) throw Err("mgc_transformer_forward_dev: bad arguments");
+        CK(cudaSetDevice(rt->device));
+        run_forward(rt, tokens_dev, B, S, logits_dev);
+    });
+}
+
+int mgc_transformer_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits) {
+    return guard([&] {
+        if (!rt || !tokens || !logits || B <= 0 || S <= 0) throw Err("mgc_transformer_forward: bad arguments");
+        const size_t R = (size_t)B * S, nl = R * rt->V;
+        if ((int)R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
+        CK(cudaSetDevice(rt->device));
+        std::memcpy(rt->h_tokens, tokens, sizeof(int32_t) * R);
+        CK(cudaMemcpyAsync(rt->tokens, rt->h_tokens, sizeof(int32_t) * R, cudaMemcpyHostToDevice, rt->st));
+        run_forward(rt, rt->tokens, B, S, rt->logits);
+        CK(cudaMemcpyAsync(rt->h_logits, rt->logits, sizeof(float) * nl, cudaMemcpyDeviceToHost, rt->st));
+        CK(cudaStreamSynchronize(rt->st));
+        check_dev_error();
+        std::memcpy(logits, rt->h_logits, sizeof(float) * nl);
+    });
+}
+
+int mgc_transformer_forward_dump(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits,
+                                 float* dump_host) {
+    return guard([&] {
+        if (!rt || !tokens || !logits || !dump_host) throw Err("mgc_transformer_forward_dump: bad arguments");
+        const size_t R = (size_t)B * S;
+        if ((int)R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
+        const size_t ndump = R * ((size_t)rt->E * (2 * rt->n_layer + 2) + rt->V);
+        CK(cudaSetDevice(rt->device));
+        float* d_dump = dalloc<float>(ndump);
+        try {
+            CK(cudaMemcpyAsync(rt->tokens, tokens, sizeof(int32_t) * R, cudaMemcpyHostToDevice, rt->st));
+            enqueue_forward(rt, rt->tokens, B, S, rt->logits, d_dump);
+            CK(cudaMemcpyAsync(logits, rt->logits, sizeof(float) * R * rt->V, cudaMemcpyDeviceToHost, rt->st));
+            CK(cudaMemcpyAsync(dump_host, d_dump, sizeof(float) * ndump, cudaMemcpyDeviceToHost, rt->st));
+            CK(cudaStreamSynchronize(rt->st));
+            check_dev_error();
+        } catch (...) { cudaFree(d_dump); throw; }
+        cudaFree(d_dump);
+    });
+}
+
+// generate() sampling (mg-generate.cpp:24-35 helpers, :53-123 loop) for B independent
+// images; the same libstdc++ mt19937_64 / uniform_real_distribution<double> streams.
+int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_t* seeds, int steps,
+                 float temperature, int32_t* tokens_out) {
+    return guard([&] {
+        if (!rt || B <= 0 || !class_ids || !seeds || !tokens_out || steps <= 0) throw Err("mgc_generate: bad arguments");
+        const int CB = rt->codebook, MASK = rt->mask_id, S = rt->n_tokens + 1;
+        const size_t vocab = (size_t)rt->V;
+        if (B * S > rt->max_rows) throw Err("mgc_generate: B*S exceeds max_rows");
+        if (CB <= 0 || CB > rt->V) throw Err("mgc_generate: bad codebook size");
+        const float ct = temperature < 0 ? rt->choice_temp : temperature;
+        std::vector<std::mt19937_64> rng;
+        for (int i = 0; i < B; i++) rng.emplace_back(seeds[i]);
+        std::vector<int32_t> tokens((size_t)B * S, MASK), sampled(S), result((size_t)B * S);
+        for (int i = 0; i < B; i++) tokens[(size_t)i * S] = class_ids[i] + CB;
+        std::vector<float> L((size_t)B * S * vocab), selp(S), conf(S), probs(CB);
+        for (int step = 0; step < steps; step++) {
+            if (mgc_transformer_forward(rt, tokens.data(), B, S, L.data()) != 0) throw Err(g_err);
+            for (int i = 0; i < B; i++) {
+                std::mt19937_64& r = rng[i];
+                int32_t* tk = tokens.data() + (size_t)i * S;
+                for (int s = 0; s < S; s++) {
+                    const float* row = L.data() + ((size_t)i * S + s) * vocab;
+                    float mx = -INFINITY;
+                    for (int v = 0; v < CB; v++) mx = std::fmax(mx, row[v]);
+                    float sum = 0.f;
+                    for (int v = 0; v < CB; v++) { const float e = std::exp(row[v] - mx); probs[v] = e; sum += e; }
+                    const float inv = 1.f / sum;
+                    for (int v = 0; v < CB; v++) probs[v] *= inv;
+                    std::uniform_real_distribution<double> u(0.0, 1.0);
+                    const double rr = u(r);
+                    double acc = 0.0;
+                    int sid = CB - 1;
+                    for (int v = 0; v < CB; v++) { acc += probs[v]; if (rr <= acc) { sid = v; break; } }
+                    const bool unknown = tk[s] == MASK;
+                    sampled[s] = unknown ? sid : tk[s];
+                    selp[s] = unknown ? probs[sid] : INFINITY;
+                }
+                std::copy(sampled.begin(), sampled.end(), result.begin() + (size_t)i * S);
+                const float ratio = (float)(step + 1) / steps;
+                const float mask_ratio = std::cos((float)M_PI / 2.f * ratio);
+                int n_unknown = 0;
+                for (int s = 0; s < S; s++) n_unknown += tk[s] == MASK;
+                int mask_len = (int)std::floor(rt->n_tokens * mask_ratio);
+                mask_len = std::max(1, std::min(mask_len, n_unknown - 1));
+                const float temp = ct * (1.f - ratio);
+                for (int s = 0; s < S; s++) {
+                    std::uniform_real_distribution<double> u(1e-12, 1.0);
+                    const float gm = (float)(-std::log(-std::log(u(r))));
+                    conf[s] = std::log(selp[s]) + temp * gm;
+                }
+                std::vector<float> sorted(conf);
+                std::nth_element(sorted.begin(), sorted.begin() + mask_len, sorted.end());
+                const float cutoff = sorted[mask_len];
+                for (int s = 0; s < S; s++) tk[s] = conf[s] < cutoff ? MASK : sampled[s];
+            }
+        }
+        std::memcpy(tokens_out, result.data(), sizeof(int32_t) * B * S);
+    });
+}
+
+int mgc_profile_enable(mgc_runtime* rt, int on) { if (!rt) return -1; rt->prof = on != 0; return 0; }
+int mgc_profile_reset(mgc_runtime* rt) { if (!rt) return -1; rt->prof_rows.clear(); return 0; }
+int mgc_profile_report(mgc_runtime* rt, char* buf, size_t len) {
+    if (!rt || !buf || len == 0) return -1;
+    std::vector<std::pair<std::string, ProfRow>> rows(rt->prof_rows.begin(), rt->prof_rows.end());
+    std::sort(rows.begin(), rows.end(), [](auto& a, auto& b) { return a.second.ms > b.second.ms; });
+    std::string s;
+    for (auto& r : rows) {
+        char line[128];
+        std::snprintf(line, sizeof line, "%s %d %.4f\n", r.first.c_str(), r.second.n, r.second.ms);
+        s += line;
+    }
+    std::snprintf(buf, len, "%s", s.c_str());
+    return 0;
+}
+
+}  // extern "C"

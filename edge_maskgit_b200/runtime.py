@@ -1,0 +1,284 @@
+"""Host-side mirror of edge_maskgit's backend interface over libmgcuda.so.
+
+``CudaRuntime`` mirrors ``mg::OpenCLRuntime`` (include/mg-opencl.hpp:23-58) for the MaskGIT
+transformer graph: construct once per device, call ``forward`` (the ``TransformerFwd``
+callback of include/mg-generate.hpp:15) once per decode step, optionally profile per op type.
+The kernel-level functions (``quantize_act``, ``QWeight.qgemm``, ``layernorm_affine``,
+``flash_attn``, ``embed``, ``gemm_f32``) take CUDA torch tensors and call the C ABI directly;
+torch is only used for device memory and streams.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import MgcError, check, lib
+
+__all__ = ["CudaRuntime", "QWeight", "MgcError", "pack_q8_0", "pack_q4_k", "dequant",
+           "quantize_act", "gemm_f32", "layernorm_affine", "flash_attn", "embed", "device_error",
+           "F32", "Q8_0", "Q4_K"]
+
+F32, Q8_0, Q4_K = 0, 8, 12
+
+
+def _ptr(a) -> C.c_void_p:
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return C.c_void_p(a.ctypes.data)
+    return C.c_void_p(a.data_ptr())
+
+
+def _stream():
+    import torch
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda_f32(t, name):
+    import torch
+    if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()):
+        raise MgcError(f"{name} must be a contiguous float32 CUDA tensor")
+    return t
+
+
+# ----------------------------------------------------------------- block formats (host)
+def pack_q8_0(w: np.ndarray) -> np.ndarray:
+    """[N][K] f32 -> GGUF Q8_0 bytes (tools/convert_to_gguf.py:109-124)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    out = np.empty(N * K // 32 * 34, np.uint8)
+    check(lib.mgc_pack_q8_0(_ptr(w), N, K, _ptr(out)), "pack_q8_0")
+    return out
+
+
+def pack_q4_k(w: np.ndarray) -> np.ndarray:
+    """[N][K] f32 -> GGUF Q4_K bytes (tools/convert_to_gguf.py:68-106)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    N, K = w.shape
+    out = np.empty(N * K // 256 * 144, np.uint8)
+    check(lib.mgc_pack_q4_k(_ptr(w), N, K, _ptr(out)), "pack_q4_k")
+    return out
+
+
+def dequant(wtype: int, blocks: np.ndarray, N: int, K: int) -> np.ndarray:
+    """GGUF blocks -> [N][K] f32 (DEQ_Q8 / deq_q4k_elem of mg-opencl.cpp)."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((N, K), np.float32)
+    check(lib.mgc_dequant(wtype, _ptr(blocks), N, K, _ptr(out)), "dequant")
+    return out
+
+
+def device_error() -> int:
+    """Read and clear the device error word set by kernels whose bounded waits expired."""
+    return int(lib.mgc_device_error())
+
+
+# ----------------------------------------------------------------- kernel-level ops
+def quantize_act(x, want_sum: bool = False):
+    """k_quantize_q8: x [M][K] -> (qx int8 [M][K], dx f32 [M][K/32], sumx int32 | None)."""
+    import torch
+    _cuda_f32(x, "x")
+    M, K = x.shape
+    qx = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    dx = torch.empty((M, K // 32), dtype=torch.float32, device=x.device)
+    sx = torch.empty((M, K // 32), dtype=torch.int32, device=x.device) if want_sum else None
+    check(lib.mgc_quantize_act(_ptr(x), M, K, _ptr(qx), _ptr(dx), _ptr(sx), _stream()), "quantize_act")
+    return qx, dx, sx
+
+
+class QWeight:
+    """A Q8_0 / Q4_K (or F32) [N][K] weight resident on the current CUDA device."""
+
+    def __init__(self, wtype: int, data: np.ndarray, N: int, K: int):
+        data = np.ascontiguousarray(data)
+        h = C.c_void_p()
+        check(lib.mgc_qweight_create(wtype, _ptr(data), N, K, C.byref(h)), "qweight_create")
+        self._h, self.wtype, self.N, self.K = h, wtype, N, K
+
+    def qgemm(self, x, bias=None, act: int = 0, resid=None, out=None):
+        """y = act(W.x + bias) + resid, the MulMat(q) dispatch of mg-opencl.cpp:1381-1399."""
+        import torch
+        _cuda_f32(x, "x")
+        M = x.shape[0]
+        if x.shape[1] != self.K:
+            raise MgcError(f"x has {x.shape[1]} columns, weight K = {self.K}")
+        y = out if out is not None else torch.empty((M, self.N), dtype=torch.float32, device=x.device)
+        check(lib.mgc_qgemm(self._h, _ptr(x), M, _ptr(bias), act, _ptr(resid), _ptr(y), _stream()), "qgemm")
+        return y
+
+    def close(self):
+        if self._h:
+            lib.mgc_qweight_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def gemm_f32(w, x, bias=None, act: int = 0, resid=None):
+    import torch
+    N, K = w.shape
+    M = x.shape[0]
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    check(lib.mgc_gemm_f32(_ptr(w), _ptr(x), M, N, K, _ptr(bias), act, _ptr(resid), _ptr(y), _stream()),
+          "gemm_f32")
+    return y
+
+
+def layernorm_affine(x, gamma, beta, eps: float = 1e-12):
+    import torch
+    rows, D = x.shape
+    y = torch.empty_like(x)
+    check(lib.mgc_layernorm_affine(_ptr(x), _ptr(gamma), _ptr(beta), rows, D, eps, _ptr(y), _stream()),
+          "layernorm_affine")
+    return y
+
+
+def flash_attn(qkv, B: int, S: int, H: int, Dh: int, scale: float):
+    import torch
+    y = torch.empty((B * S, H * Dh), dtype=torch.float32, device=qkv.device)
+    check(lib.mgc_flash_attn(_ptr(qkv), B, S, H, Dh, scale, _ptr(y), _stream()), "flash_attn")
+    return y
+
+
+def embed(tok, pos, tokens, B: int, S: int):
+    import torch
+    V, E = tok.shape
+    y = torch.empty((B * S, E), dtype=torch.float32, device=tok.device)
+    check(lib.mgc_embed(_ptr(tok), V, _ptr(pos), E, _ptr(tokens), B, S, _ptr(y), _stream()), "embed")
+    return y
+
+
+# ----------------------------------------------------------------- runtime
+@dataclass
+class HParams:
+    n_layer: int
+    n_head: int
+    n_embd: int
+    n_ffn: int
+    head_dim: int
+    vocab_size: int
+    n_tokens: int
+    mask_token_id: int
+    codebook_size: int
+    wtype: int
+
+
+@dataclass
+class OpProfile:   # include/mg-opencl.hpp:17-21
+    op: str
+    count: int
+    ms: float
+
+
+class CudaRuntime:
+    """mg::OpenCLRuntime's counterpart for the MaskGIT transformer on one B200."""
+
+    def __init__(self, gguf_path: str, max_rows: int = 257, device: int = 0):
+        h = C.c_void_p()
+        check(lib.mgc_runtime_create(str(gguf_path).encode(), max_rows, device, C.byref(h)), "runtime_create")
+        self._h = h
+        hp = np.zeros(10, np.int32)
+        check(lib.mgc_runtime_hparams(h, _ptr(hp)))
+        self.hparams = HParams(*[int(v) for v in hp])
+        self.max_rows = max_rows
+
+    # --- OpenCLRuntime API
+    def device_name(self) -> str:
+        return lib.mgc_runtime_device_name(self._h).decode()
+
+    def invalidate(self, _tensor=None) -> None:
+        """Token inputs are uploaded on every forward, so nothing is cached to drop."""
+
+    def profile_enable(self, on: bool) -> None:
+        check(lib.mgc_profile_enable(self._h, int(on)))
+
+    def profile_reset(self) -> None:
+        check(lib.mgc_profile_reset(self._h))
+
+    def profile_report(self) -> list[OpProfile]:
+        buf = C.create_string_buffer(1 << 14)
+        check(lib.mgc_profile_report(self._h, buf, len(buf)))
+        rows = []
+        for line in buf.value.decode().splitlines():
+            name, n, ms = line.rsplit(" ", 2)
+            rows.append(OpProfile(name, int(n), float(ms)))
+        return rows
+
+    # --- TransformerFwd
+    def forward(self, tokens: np.ndarray, B: int | None = None) -> np.ndarray:
+        """tokens [B][S] int32 (host) -> logits [B*S][vocab] f32 (host)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        if tokens.ndim == 1:
+            tokens = tokens[None]
+        B, S = tokens.shape
+        out = np.empty((B * S, self.hparams.vocab_size), np.float32)
+        check(lib.mgc_transformer_forward(self._h, _ptr(tokens), B, S, _ptr(out)), "forward")
+        return out
+
+    def forward_dev(self, tokens_dev, logits_dev, B: int, S: int) -> None:
+        """Device-resident forward on the runtime's stream (graph replay); not synchronised."""
+        check(lib.mgc_transformer_forward_dev(self._h, _ptr(tokens_dev), B, S, _ptr(logits_dev)), "forward_dev")
+
+    def forward_dump(self, tokens: np.ndarray):
+        """Forward that also returns the 51 named verification tensors (MG_DUMP_NAMED)."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        if tokens.ndim == 1:
+            tokens = tokens[None]
+        B, S = tokens.shape
+        hp = self.hparams
+        R = B * S
+        logits = np.empty((R, hp.vocab_size), np.float32)
+        dump = np.empty(R * (hp.n_embd * (2 * hp.n_layer + 2) + hp.vocab_size), np.float32)
+        check(lib.mgc_transformer_forward_dump(self._h, _ptr(tokens), B, S, _ptr(logits), _ptr(dump)),
+              "forward_dump")
+        return logits, split_named(dump, R, hp.n_layer, hp.n_embd, hp.vocab_size)
+
+    def sync(self) -> None:
+        check(lib.mgc_runtime_sync(self._h), "sync")
+
+    @property
+    def stream_handle(self) -> int:
+        return int(lib.mgc_runtime_stream(self._h) or 0)
+
+    def generate(self, class_ids, seeds, steps: int = 8, temperature: float = 4.5) -> np.ndarray:
+        """generate() (src/mg-generate.cpp:53-123) for len(class_ids) images -> tokens [B][S]."""
+        cls = np.ascontiguousarray(class_ids, dtype=np.int32)
+        sd = np.ascontiguousarray(seeds, dtype=np.uint64)
+        B = cls.shape[0]
+        out = np.empty((B, self.hparams.n_tokens + 1), np.int32)
+        check(lib.mgc_generate(self._h, B, _ptr(cls), _ptr(sd), steps, temperature, _ptr(out)), "generate")
+        return out
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib.mgc_runtime_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def named_tensor_names(n_layer: int) -> list[str]:
+    """The 51 verification names of mg-transformer.cpp:48,91,98,105,109 in dump order."""
+    names = ["embd_post_norm"]
+    for i in range(n_layer):
+        names += [f"blk.{i}.attn_post", f"blk.{i}.ffn_post"]
+    return names + ["output_norm", "output_logits"]
+
+
+def split_named(dump: np.ndarray, R: int, n_layer: int, E: int, V: int) -> dict:
+    out, off = {}, 0
+    for name in named_tensor_names(n_layer):
+        w = V if name == "output_logits" else E
+        out[name] = dump[off:off + R * w].reshape(R, w)
+        off += R * w
+    return out

@@ -1,0 +1,178 @@
+"""Synthetic MaskGIT GGUF models (the stand-in for the reference's real checkpoints).
+
+Writes GGUF v3 in the layout the reference loader reads (mg-model.cpp:139-201) with the
+tensor names and shapes of reference/export_weights.py:51-80 and the metadata keys of
+tools/convert_to_gguf.py:188-210.  Every tensor is ``0.02 * N(0, 1)`` drawn from one
+``numpy.random.default_rng(seed)`` stream in export order.  Linear weights (attn_q/k/v/o,
+ffn_up/down, output_proj) are packed Q8_0 ("gq8") or Q4_K ("gq4") by the library's packer,
+or kept F32 ("f32"); token_embd / pos_embd / LayerNorm / biases stay F32, as the reference
+converter does (convert_to_gguf.py:213-246).
+
+``dequant_twin`` writes the same model with every packed weight dequantised back to F32 --
+the input the reference's scalar CPU executor needs (it reads weights as float only).
+"""
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from . import runtime as rt
+
+ALIGN = 32
+_LINEAR = ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_o.weight",
+           "ffn_up.weight", "ffn_down.weight")
+
+
+@dataclass
+class ModelSpec:
+    n_layer: int = 24
+    n_embd: int = 768
+    n_head: int = 16
+    n_ffn: int = 3072
+    vocab_size: int = 2025
+    n_tokens: int = 256
+    codebook: int = 1024
+    quant: str = "gq8"        # gq8 | gq4 | f32
+    seed: int = 42
+
+    @property
+    def head_dim(self) -> int:
+        return self.n_embd // self.n_head
+
+
+def tensor_list(s: ModelSpec):
+    """(name, numpy shape) in export order (export_weights.py:51-80)."""
+    E, F, V, P = s.n_embd, s.n_ffn, s.vocab_size, s.n_tokens + 1
+    out = [("token_embd.weight", (V, E)), ("pos_embd.weight", (P, E)),
+           ("token_embd_norm.weight", (E,)), ("token_embd_norm.bias", (E,))]
+    for i in range(s.n_layer):
+        p = f"blk.{i}."
+        for nm in ("q", "k", "v"):
+            out += [(p + f"attn_{nm}.weight", (E, E)), (p + f"attn_{nm}.bias", (E,))]
+        out += [(p + "attn_o.weight", (E, E)), (p + "attn_o.bias", (E,)),
+                (p + "attn_norm.weight", (E,)), (p + "attn_norm.bias", (E,)),
+                (p + "ffn_up.weight", (F, E)), (p + "ffn_up.bias", (F,)),
+                (p + "ffn_down.weight", (E, F)), (p + "ffn_down.bias", (E,)),
+                (p + "ffn_norm.weight", (E,)), (p + "ffn_norm.bias", (E,))]
+    out += [("output_proj.weight", (E, E)), ("output_proj.bias", (E,)),
+            ("output_norm.weight", (E,)), ("output_norm.bias", (E,)), ("output.bias", (V,))]
+    return out
+
+
+def _is_linear(name: str) -> bool:
+    return name.endswith(_LINEAR) or name == "output_proj.weight"
+
+
+class _Buf:
+    def __init__(self):
+        self.b = bytearray()
+
+    def u32(self, v): self.b += struct.pack("<I", v)
+    def i32(self, v): self.b += struct.pack("<i", v)
+    def u64(self, v): self.b += struct.pack("<Q", v)
+    def f32(self, v): self.b += struct.pack("<f", v)
+
+    def s(self, text: str):
+        raw = text.encode()
+        self.u64(len(raw))
+        self.b += raw
+
+
+def _metadata(s: ModelSpec, quant_label: str) -> tuple[bytes, int]:
+    kv = _Buf()
+    n = 0
+
+    def put(key, typ, val):
+        nonlocal n
+        kv.s(key)
+        kv.u32(typ)
+        {4: kv.u32, 5: kv.i32, 6: kv.f32, 8: kv.s}[typ](val)
+        n += 1
+
+    put("general.architecture", 8, "maskgit")
+    put("general.name", 8, f"synthetic maskgit (seed {s.seed})")
+    put("general.alignment", 4, ALIGN)
+    put("general.file_type", 4, 0)
+    put("maskgit.resolution", 4, 256)
+    put("maskgit.n_layer", 4, s.n_layer)
+    put("maskgit.n_head", 4, s.n_head)
+    put("maskgit.n_embd", 4, s.n_embd)
+    put("maskgit.n_ffn", 4, s.n_ffn)
+    put("maskgit.head_dim", 4, s.head_dim)
+    put("maskgit.vocab_size", 4, s.vocab_size)
+    put("maskgit.n_tokens", 4, s.n_tokens)
+    put("maskgit.n_positions", 4, s.n_tokens + 1)
+    put("maskgit.mask_token_id", 5, s.vocab_size - 1)
+    put("maskgit.layernorm_eps", 6, 1e-12)
+    put("maskgit.vqgan.codebook_size", 4, s.codebook)
+    put("maskgit.sampling.choice_temperature", 6, 4.5)
+    put("maskgit.quant", 8, quant_label)
+    return bytes(kv.b), n
+
+
+def _write(path: Path, s: ModelSpec, quant_label: str, tensors) -> None:
+    """tensors: iterable of (name, ne innermost-first, ggml type, bytes)."""
+    tensors = list(tensors)
+    kv, nkv = _metadata(s, quant_label)
+    info = _Buf()
+    offs, cur = [], 0
+    for name, ne, typ, data in tensors:
+        info.s(name)
+        info.u32(len(ne))
+        for d in ne:
+            info.u64(int(d))
+        info.u32(typ)
+        info.u64(cur)
+        offs.append(cur)
+        cur = (cur + len(data) + ALIGN - 1) // ALIGN * ALIGN
+    head = struct.pack("<IIQQ", 0x46554747, 3, len(tensors), nkv) + kv + bytes(info.b)
+    pad = (-len(head)) % ALIGN
+    path.parent.mkdir(parents=True, exist_ok=True)
+    with open(path, "wb") as f:
+        f.write(head + b"\0" * pad)
+        pos = 0
+        for (name, ne, typ, data), off in zip(tensors, offs):
+            if off > pos:
+                f.write(b"\0" * (off - pos))
+                pos = off
+            f.write(data)
+            pos += len(data)
+
+
+def make_model(path, spec: ModelSpec | None = None, dequant_twin=None) -> Path:
+    """Write a synthetic GGUF (and optionally its dequantised F32 twin)."""
+    s = spec or ModelSpec()
+    rng = np.random.default_rng(s.seed)
+    packed, twin = [], []
+    for name, shape in tensor_list(s):
+        a = (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        ne = list(reversed(shape))
+        if _is_linear(name) and s.quant in ("gq8", "gq4"):
+            N, K = shape
+            if s.quant == "gq8":
+                blob, typ = rt.pack_q8_0(a), rt.Q8_0
+            else:
+                blob, typ = rt.pack_q4_k(a), rt.Q4_K
+            packed.append((name, ne, typ, blob.tobytes()))
+            if dequant_twin is not None:
+                twin.append((name, ne, 0, rt.dequant(typ, blob, N, K).tobytes()))
+        else:
+            packed.append((name, ne, 0, a.tobytes()))
+            if dequant_twin is not None:
+                twin.append((name, ne, 0, a.tobytes()))
+    path = Path(path)
+    _write(path, s, s.quant, packed)
+    if dequant_twin is not None:
+        _write(Path(dequant_twin), s, "f32", twin)
+    return path
+
+
+def config1_tokens(spec: ModelSpec | None = None, class_id: int = 207) -> np.ndarray:
+    """Step-1 input: class token (class + codebook) then n_tokens mask ids (mg-generate.cpp:58-59)."""
+    s = spec or ModelSpec()
+    t = np.full(s.n_tokens + 1, s.vocab_size - 1, np.int32)
+    t[0] = class_id + s.codebook
+    return t

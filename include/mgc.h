@@ -1,0 +1,130 @@
+/* mgc.h -- C ABI of libmgcuda.so, the B200 (sm_100a) backend for edge_maskgit's quantized
+ * MaskGIT transformer.
+ *
+ * Conventions
+ *   - Every entry point returns int: 0 on success, <0 on error; mgc_last_error() then
+ *     returns a message (thread-local, valid until the next call on that thread).
+ *   - "dev" pointers are CUDA device pointers; "host" pointers are ordinary host memory.
+ *   - stream is a cudaStream_t passed as void* (NULL = the legacy default stream).
+ *   - Layouts follow the reference's row-major activation convention x[m*K + k]
+ *     (ggml ne = {K, M}); weight bytes are the GGUF Q8_0 / Q4_K blocks unchanged.
+ *   - wtype codes are GGML's: 0 = F32, 8 = Q8_0, 12 = Q4_K.
+ */
+#ifndef MGC_H
+#define MGC_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MGC_F32 0
+#define MGC_Q8_0 8
+#define MGC_Q4_K 12
+
+const char* mgc_last_error(void);
+/* Reads and clears the device-side error word written by bounded waits inside kernels
+ * (0 = none).  A non-zero value means a kernel gave up waiting and returned early. */
+int mgc_device_error(void);
+
+/* ------------------------------------------------------------------ weight packing (host)
+ * Replaces tools/convert_to_gguf.py quant_q8_0 (:109-124) and quant_q4_k (:68-106):
+ * w [N][K] f32 row-major -> GGUF block bytes (N*K/32*34 or N*K/256*144 bytes). */
+int mgc_pack_q8_0(const float* w_host, int64_t N, int64_t K, uint8_t* out_host);
+int mgc_pack_q4_k(const float* w_host, int64_t N, int64_t K, uint8_t* out_host);
+/* Dequantise GGUF blocks to f32 with the reference formulas DEQ_Q8 / deq_q4k_elem
+ * (src/mg-opencl/mg-opencl.cpp:386-387, :252-262). */
+int mgc_dequant(int wtype, const uint8_t* w_host, int64_t N, int64_t K, float* out_host);
+
+/* ------------------------------------------------------------------ kernel-level ops
+ * Replaces k_quantize_q8 (mg-opencl.cpp:424-434, dispatched at :1386-1389):
+ * x dev [M][K] f32 -> qx dev [M][K] int8, dx dev [M][K/32] f32, sumx dev [M][K/32] int32
+ * (sumx may be NULL). */
+int mgc_quantize_act(const float* x_dev, int M, int K, int8_t* qx_dev, float* dx_dev,
+                     int32_t* sumx_dev, void* stream);
+
+/* A quantized weight resident on the device in the GEMM's streaming layout. */
+typedef struct mgc_qweight mgc_qweight;
+/* Upload GGUF blocks (host) of an [N][K] weight; wtype 8 or 12 (0 = F32 row-major).
+ * K must be a multiple of 128 (256 for Q4_K). */
+int mgc_qweight_create(int wtype, const void* w_host, int N, int K, mgc_qweight** out);
+void mgc_qweight_destroy(mgc_qweight* w);
+
+/* Quantized linear layer, the MulMat(Q8_0 | Q4_K) dispatch of mg-opencl.cpp:1381-1399
+ * (k_quantize_q8 + k_mul_mat_q8_i8 / k_mul_mat_q4k_i8):
+ *   y[m*N+n] = act(sum_b dw*dx*idot_b + bias[n]) + resid[m*N+n]
+ * x, bias, resid, y are device f32; bias / resid may be NULL; act 0 none, 1 erf-GELU,
+ * 2 SiLU.  Uses a per-library scratch for the quantized activation. */
+int mgc_qgemm(const mgc_qweight* w, const float* x_dev, int M, const float* bias_dev,
+              int act, const float* resid_dev, float* y_dev, void* stream);
+
+/* F32 linear with the same epilogue (k_mul_mat_t, mg-opencl.cpp:57-98; the MLM head at
+ * mg-transformer.cpp:107-108).  w dev [N][K] f32 row-major. */
+int mgc_gemm_f32(const float* w_dev, const float* x_dev, int M, int N, int K,
+                 const float* bias_dev, int act, const float* resid_dev, float* y_dev,
+                 void* stream);
+
+/* LayerNorm + affine over D (k_norm_affine, mg-opencl.cpp:705-727; dispatch :1450-1465).
+ * D must be a multiple of 64 and <= 2048. */
+int mgc_layernorm_affine(const float* x_dev, const float* gamma_dev, const float* beta_dev,
+                         int rows, int D, float eps, float* y_dev, void* stream);
+
+/* fp16-K/V flash attention (k_flash_attention_h, mg-opencl.cpp:859-937; dispatch
+ * :1483-1511).  qkv dev [B*S][3*H*Dh] f32 holds the q | k | v projections side by side;
+ * out dev [B*S][H*Dh] f32 is the head-merged result (mg-transformer.cpp:84-85).
+ * Dh must be 48. */
+int mgc_flash_attn(const float* qkv_dev, int B, int S, int H, int Dh, float scale,
+                   float* out_dev, void* stream);
+
+/* Token + position embedding (k_get_rows mg-opencl.cpp:667-672 and k_add :947-953). */
+int mgc_embed(const float* tok_embd_dev, int vocab, const float* pos_embd_dev, int E,
+              const int32_t* tokens_dev, int B, int S, float* out_dev, void* stream);
+
+/* ------------------------------------------------------------------ runtime
+ * The CUDA counterpart of mg::OpenCLRuntime (include/mg-opencl.hpp:23-58) specialised to
+ * the MaskGIT transformer graph of src/mg-transformer.cpp:32-111. */
+typedef struct mgc_runtime mgc_runtime;
+/* Load a GGUF (mg-model.cpp:139-201 format), upload and repack every weight.
+ * max_rows = largest B*S a forward will see. device = CUDA ordinal. */
+int mgc_runtime_create(const char* gguf_path, int max_rows, int device, mgc_runtime** out);
+void mgc_runtime_destroy(mgc_runtime* rt);
+/* n_layer n_head n_embd n_ffn head_dim vocab n_tokens mask_id codebook wtype */
+int mgc_runtime_hparams(const mgc_runtime* rt, int32_t out[10]);
+const char* mgc_runtime_device_name(const mgc_runtime* rt);
+
+/* The TransformerFwd callback (include/mg-generate.hpp:15): tokens host [B*S] int32 ->
+ * logits host [B*S*vocab] f32, row-major s-outer / v-inner; synchronous. */
+int mgc_transformer_forward(mgc_runtime* rt, const int32_t* tokens_host, int B, int S,
+                            float* logits_host);
+/* Same forward with device buffers, enqueued on the runtime's stream (replayed from a
+ * CUDA graph captured on first use for each (B, S)).  Not synchronised on return. */
+int mgc_transformer_forward_dev(mgc_runtime* rt, const int32_t* tokens_dev, int B, int S,
+                                float* logits_dev);
+/* Forward that also copies the 51 named verification tensors (the MG_DUMP_NAMED hook of
+ * mg-opencl.cpp:1631-1641): embd_post_norm, blk.i.attn_post, blk.i.ffn_post, output_norm,
+ * output_logits, each [B*S][width] f32, concatenated into dump_host. */
+int mgc_transformer_forward_dump(mgc_runtime* rt, const int32_t* tokens_host, int B, int S,
+                                 float* logits_host, float* dump_host);
+/* Synchronise the runtime's stream. */
+int mgc_runtime_sync(mgc_runtime* rt);
+/* Raw cudaStream_t of the runtime. */
+void* mgc_runtime_stream(mgc_runtime* rt);
+
+/* Decode loop (generate(), src/mg-generate.cpp:53-123, without the VQGAN): B independent
+ * images, image i with class_ids[i] and std::mt19937_64(seeds[i]); forwards are batched.
+ * tokens_out host [B][S] = the final sampled sequence (class token first). */
+int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_t* seeds,
+                 int steps, float temperature, int32_t* tokens_out);
+
+/* Per-op-type profile (OpenCLRuntime::profile_enable/reset/report, mg-opencl.hpp:50-53).
+ * When enabled, forwards run eagerly with CUDA events around each kernel. */
+int mgc_profile_enable(mgc_runtime* rt, int on);
+int mgc_profile_reset(mgc_runtime* rt);
+/* Writes "name count ms\n" lines (descending by ms) into buf (NUL-terminated). */
+int mgc_profile_report(mgc_runtime* rt, char* buf, size_t buflen);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,30 @@
+"""CPU: the C-ABI library loads and exports every symbol include/mgc.h declares."""
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared():
+    src = (ROOT / "include" / "mgc.h").read_text()
+    return sorted(set(re.findall(r"\b(mgc_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from edge_maskgit_b200 import _lib
+    names = declared()
+    assert len(names) >= 20
+    for n in names:
+        assert hasattr(_lib.lib, n), n
+    assert set(names) == set(_lib.EXPORTED)
+
+
+def test_errors_are_reported_without_a_gpu():
+    import numpy as np
+    from edge_maskgit_b200 import runtime as rt
+    try:
+        rt.pack_q8_0(np.zeros((2, 33), np.float32))
+    except rt.MgcError as e:
+        assert "multiple of 32" in str(e)
+    else:
+        raise AssertionError("expected MgcError")

@@ -1,0 +1,142 @@
+"""GPU: every kernel through the C ABI against the CPU oracle on the same inputs.
+
+Integer outputs (qx, block dots via act=0 GEMM results) and every pure-IEEE path are
+bit-exact; paths through erf / exp (GELU epilogue, attention softmax) use CUDA's erff /
+expf against the C library's, so they are held to a few ulp (rtol 1e-5)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _x(M, K, seed=0):
+    return np.random.default_rng(seed).standard_normal((M, K), dtype=np.float32)
+
+
+@pytest.mark.parametrize("M,K", [(1, 32), (31, 768), (257, 768), (300, 3072)])
+def test_quantize_act_bit_exact(dev, oracle_mod, M, K):
+    from edge_maskgit_b200 import runtime as rt
+    x = _x(M, K, 3)
+    x[0, :32] = 0.0
+    x[-1, 5] = 1e4
+    qx, dx, sx = rt.quantize_act(_t(x, dev), want_sum=True)
+    oq, od, os_ = oracle_mod.quantize_act(x)
+    assert np.array_equal(qx.cpu().numpy(), oq)
+    assert np.array_equal(dx.cpu().numpy(), od)
+    assert np.array_equal(sx.cpu().numpy(), os_)
+
+
+SHAPES = [(768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 2025)]
+
+
+@pytest.mark.parametrize("wtype", [8, 12])
+@pytest.mark.parametrize("M", [1, 31, 257])
+@pytest.mark.parametrize("K,N", SHAPES)
+def test_qgemm_bit_exact(dev, oracle_mod, wtype, M, K, N):
+    from edge_maskgit_b200 import runtime as rt
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
+    blocks = rt.pack_q8_0(w) if wtype == 8 else rt.pack_q4_k(w)
+    qw = rt.QWeight(wtype, blocks, N, K)
+    y = qw.qgemm(_t(x, dev)).cpu().numpy()
+    ref = oracle_mod.qgemm(wtype, blocks, x, N)
+    assert np.array_equal(y, ref), f"max diff {np.abs(y - ref).max()}"
+
+
+@pytest.mark.parametrize("wtype", [8, 12])
+@pytest.mark.parametrize("act", [0, 1])
+def test_qgemm_epilogue(dev, oracle_mod, wtype, act):
+    from edge_maskgit_b200 import runtime as rt
+    rng = np.random.default_rng(5)
+    M, K, N = 257, 768, 3072
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
+    b = rng.standard_normal(N, dtype=np.float32)
+    r = rng.standard_normal((M, N), dtype=np.float32)
+    blocks = rt.pack_q8_0(w) if wtype == 8 else rt.pack_q4_k(w)
+    qw = rt.QWeight(wtype, blocks, N, K)
+    y = qw.qgemm(_t(x, dev), bias=_t(b, dev), act=act, resid=_t(r, dev)).cpu().numpy()
+    ref = oracle_mod.qgemm(wtype, blocks, x, N, bias=b, act=act, resid=r)
+    if act == 0:
+        assert np.array_equal(y, ref)
+    else:
+        np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_qgemm_large_m(dev, oracle_mod):
+    """M=4097 (config 5 row count): compare a row sample against the oracle."""
+    from edge_maskgit_b200 import runtime as rt
+    rng = np.random.default_rng(9)
+    M, K, N = 4097, 3072, 768
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
+    blocks = rt.pack_q8_0(w)
+    y = rt.QWeight(8, blocks, N, K).qgemm(_t(x, dev)).cpu().numpy()
+    rows = np.r_[0:3, 127:130, 2048:2050, 4094:4097]
+    ref = oracle_mod.qgemm(8, blocks, x[rows], N)
+    assert np.array_equal(y[rows], ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(17, 2025, 768), (257, 2025, 768), (5, 70, 48)])
+def test_gemm_f32_bit_exact(dev, oracle_mod, M, N, K):
+    from edge_maskgit_b200 import runtime as rt
+    rng = np.random.default_rng(1)
+    w = rng.standard_normal((N, K), dtype=np.float32)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    b = rng.standard_normal(N, dtype=np.float32)
+    y = rt.gemm_f32(_t(w, dev), _t(x, dev), bias=_t(b, dev)).cpu().numpy()
+    assert np.array_equal(y, oracle_mod.gemm_f32(w, x, bias=b))
+
+
+@pytest.mark.parametrize("rows,D", [(1, 768), (257, 768), (33, 64)])
+def test_layernorm_bit_exact(dev, oracle_mod, rows, D):
+    from edge_maskgit_b200 import runtime as rt
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((rows, D), dtype=np.float32) * 3 + 1
+    g = rng.standard_normal(D, dtype=np.float32)
+    b = rng.standard_normal(D, dtype=np.float32)
+    y = rt.layernorm_affine(_t(x, dev), _t(g, dev), _t(b, dev), 1e-12).cpu().numpy()
+    assert np.array_equal(y, oracle_mod.layernorm_affine(x, g, b, 1e-12))
+
+
+@pytest.mark.parametrize("B,S", [(1, 257), (2, 17), (1, 1), (1, 33)])
+def test_flash_attn(dev, oracle_mod, B, S):
+    from edge_maskgit_b200 import runtime as rt
+    H, Dh = 16, 48
+    rng = np.random.default_rng(4)
+    qkv = rng.standard_normal((B * S, 3 * H * Dh), dtype=np.float32)
+    scale = 1.0 / np.sqrt(np.float32(Dh))
+    y = rt.flash_attn(_t(qkv, dev), B, S, H, Dh, float(scale)).cpu().numpy()
+    ref = oracle_mod.flash_attn(qkv, B, S, H, Dh, float(scale))
+    np.testing.assert_allclose(y, ref, rtol=2e-5, atol=2e-6)
+
+
+def test_embed_bit_exact(dev, oracle_mod):
+    from edge_maskgit_b200 import runtime as rt
+    rng = np.random.default_rng(6)
+    V, E, B, S = 2025, 768, 2, 257
+    tok = rng.standard_normal((V, E), dtype=np.float32)
+    pos = rng.standard_normal((S, E), dtype=np.float32)
+    ids = rng.integers(-1, V, (B, S)).astype(np.int32)   # -1 wraps to the last row (mask)
+    y = rt.embed(_t(tok, dev), _t(pos, dev), _t(ids, dev), B, S).cpu().numpy()
+    assert np.array_equal(y, oracle_mod.embed(tok, pos, ids, B, S))
+
+
+def test_no_device_error_left(dev):
+    from edge_maskgit_b200 import runtime as rt
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0

@@ -1,0 +1,89 @@
+"""GPU: the whole transformer runtime (mgc_runtime_*) against the oracle and the reference."""
+import numpy as np
+import pytest
+
+from conftest import TIERS, cosine
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+@pytest.mark.parametrize("q,tier", [("gq8", "q8"), ("gq4", "q4")])
+def test_named_tensors_vs_oracle_and_reference(oracle_mod, golden, small_models, q, tier):
+    from edge_maskgit_b200 import runtime as rt, synth
+    path, spec = small_models[q]
+    tok = synth.config1_tokens(spec)
+    r = rt.CudaRuntime(path, max_rows=2 * (spec.n_tokens + 1))
+    logits, named = r.forward_dump(tok)
+    o_logits, o_named = oracle_mod.OracleModel(path).forward(tok, dump=True)
+    max_tol, cos_tol = TIERS[tier]
+    for name in oracle_mod.named_tensor_names(spec.n_layer):
+        # vs the oracle: only the attention's exp differs, so nearly identical
+        assert cosine(named[name], o_named[name]) > 0.999999, name
+        assert np.abs(named[name] - o_named[name]).max() < 1e-3, name
+        # vs the reference's own CPU path: the tier gate
+        ref = golden[f"ref_{q}_{name}"]
+        assert np.abs(named[name] - ref).max() <= max_tol, name
+        assert cosine(named[name], ref) >= cos_tol, name
+    assert np.array_equal(logits, named["output_logits"])
+    # graph-replayed forward equals the eager dump forward
+    assert np.array_equal(r.forward(tok), logits)
+    r.close()
+
+
+def test_batched_forward_rows_match_single(small_models):
+    from edge_maskgit_b200 import runtime as rt, synth
+    path, spec = small_models["gq8"]
+    S = spec.n_tokens + 1
+    r = rt.CudaRuntime(path, max_rows=3 * S)
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, spec.vocab_size, (3, S)).astype(np.int32)
+    both = r.forward(toks)
+    for i in range(3):
+        assert np.array_equal(both[i * S:(i + 1) * S], r.forward(toks[i]))
+    r.close()
+
+
+def test_generate_tokens_identical(oracle_mod, golden, small_models):
+    """Sampled tokens of the CUDA runtime's decode loop vs the reference's generate()."""
+    from edge_maskgit_b200 import runtime as rt
+    path, spec = small_models["gq8"]
+    r = rt.CudaRuntime(path, max_rows=2 * (spec.n_tokens + 1))
+    toks = r.generate([207], [42], steps=8)
+    assert np.array_equal(toks[0, 1:], golden["ref_grid_gq8"])
+    om = oracle_mod.OracleModel(path)
+    both = r.generate([207, 11], [42, 8], steps=8)
+    assert np.array_equal(both, om.generate([207, 11], [42, 8], steps=8))
+    r.close()
+
+
+def test_config1_full_model(oracle_mod, tmp_path):
+    """Config 1 at full size (24 layers, M=257, Q8_0): logits vs the oracle."""
+    from edge_maskgit_b200 import runtime as rt, synth
+    spec = synth.ModelSpec()
+    path = synth.make_model(tmp_path / "c1.gguf", spec)
+    tok = synth.config1_tokens(spec)
+    r = rt.CudaRuntime(path, max_rows=257)
+    logits = r.forward(tok)
+    ref = oracle_mod.OracleModel(path).forward(tok)
+    assert cosine(logits, ref) > 0.99999
+    assert np.abs(logits - ref).max() < 1e-2
+    r.close()
+
+
+def test_profile_report(small_models):
+    from edge_maskgit_b200 import runtime as rt, synth
+    path, spec = small_models["gq8"]
+    r = rt.CudaRuntime(path, max_rows=spec.n_tokens + 1)
+    r.profile_enable(True)
+    r.forward(synth.config1_tokens(spec))
+    rows = {p.op: p for p in r.profile_report()}
+    assert rows["MulMat(q)"].count == spec.n_layer * 4 + 1
+    assert rows["FlashAttention"].count == spec.n_layer
+    r.close()
