@@ -31,6 +31,7 @@ _SIGS = {
     "mgc_qweight_create": (I, [I, P, I, I, C.POINTER(P)]),
     "mgc_qweight_destroy": (None, [P]),
     "mgc_qgemm": (I, [P, P, I, P, I, P, P, P]),
+    "mgc_qgemm_noalloc": (I, [P, P, I, P, I, P, P, P]),
     "mgc_gemm_f32": (I, [P, P, I, I, I, P, I, P, P, P]),
     "mgc_layernorm_affine": (I, [P, P, P, I, I, F, P, P]),
     "mgc_flash_attn": (I, [P, I, I, I, I, F, P, P]),

@@ -64,3 +64,11 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
                       cudaStream_t st);
 
 }  // namespace mgc
+
+namespace mgc {
+// Set the message mgc_last_error() returns on this thread.
+void set_last_error(const char* msg);
+}  // namespace mgc
+
+// Handle behind the C ABI's opaque mgc_qweight (include/mgc.h).
+struct mgc_qweight { mgc::QWeight w; };

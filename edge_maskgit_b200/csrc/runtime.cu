@@ -203,7 +203,8 @@ std::mutex g_scratch_mu;
 
 }  // namespace
 
-struct mgc_qweight { QWeight w; };
+
+void mgc::set_last_error(const char* msg) { g_err = msg; }
 
 extern "C" {
 

@@ -59,6 +59,24 @@ void mgc_qweight_destroy(mgc_qweight* w);
 int mgc_qgemm(const mgc_qweight* w, const float* x_dev, int M, const float* bias_dev,
               int act, const float* resid_dev, float* y_dev, void* stream);
 
+/* Upper bound on round_up(M, 128) * K for mgc_qgemm_noalloc: 6 Mi elements, i.e. a fixed
+ * 7.5 MiB device array (int8 codes plus two f32 per 32-block) held by every GPU that loads
+ * the library, for as long as the process lives. */
+#define MGC_NOALLOC_MAX_ELEMS 6291456
+
+/* No counterpart in the reference.  mgc_qgemm for callers that are not allowed to allocate
+ * device memory (a host whose pool allocator owns all GPU memory, or code that may not
+ * allocate after start-up): same inputs, outputs and results as mgc_qgemm, but the
+ * quantized-activation scratch is a fixed array compiled into the library, so the call
+ * makes no cudaMalloc / cudaFree.  Returns <0 with a clear message if
+ * round_up(M,128) * K > MGC_NOALLOC_MAX_ELEMS, or for an F32 weight.  The first call on
+ * each device looks up the array's device address; make that first call before any
+ * stream capture.  All calls share the one array and it keeps the previous call's
+ * contents (nothing in it needs to start at zero), so calls that can overlap on the GPU --
+ * different streams, or different host threads -- race on it: serialise them. */
+int mgc_qgemm_noalloc(const mgc_qweight* w, const float* x_dev, int M, const float* bias_dev,
+                      int act, const float* resid_dev, float* y_dev, void* stream);
+
 /* F32 linear with the same epilogue (k_mul_mat_t, mg-opencl.cpp:57-98; the MLM head at
  * mg-transformer.cpp:107-108).  w dev [N][K] f32 row-major. */
 int mgc_gemm_f32(const float* w_dev, const float* x_dev, int M, int N, int K,
