@@ -20,7 +20,8 @@ ROOT = PKG.parent
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC",
-                  "-I", str(ROOT / "include"), "--expt-relaxed-constexpr"]
+                  "-I", str(ROOT / "include"), "--expt-relaxed-constexpr"] + \
+    os.environ.get("MGC_EXTRA_NVFLAGS", "").split()
 
 
 def _headers() -> list[Path]:

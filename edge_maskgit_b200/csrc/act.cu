@@ -66,11 +66,6 @@ __global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, int8
     }
 }
 
-void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st) {
-    const long n = (long)M * (K / 32);
-    quant_act_kernel<true><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, M, K, a.q, a.d,
-                                                                         want_c ? a.c : nullptr, nullptr, a.Mpad);
-}
 void launch_quant_act_plain(const float* x, int M, int K, int8_t* qx, float* dx, int32_t* sumx,
                             cudaStream_t st) {
     const long n = (long)M * (K / 32);
@@ -176,6 +171,165 @@ __global__ void embed_ln_kernel(const float* __restrict__ tok, int vocab, const 
     if (quant) quant_row_warp<NV>(v, warp, a, want_c != 0, lane);
 }
 
+// ---------------------------------------------------------------- chunked row kernels
+// Faster layout for D % 256 == 0: lane l of a row's warp holds, for chunk i, the 8
+// contiguous elements 256 i + 8 l .. +7 (two 16-byte loads, a fully coalesced warp access),
+// so one 32-element quant block is 4 adjacent lanes and its 32 codes leave as four 8-byte
+// stores.  LayerNorm keeps the reference's summation order exactly: the row is staged in
+// shared memory and lane l forms the partial sums of work-items t = l and t = l + 32 over
+// d = t, t+64, ... before the same shuffle tree as above.
+template <int NC>
+__device__ __forceinline__ void quant_chunks(const float (&v)[NC][8], int m, const ActQ& a, bool want_c, int lane) {
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(v[i][e]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        uint32_t lo = 0, hi = 0;
+        int sum = 0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int q = (int)roundf(__fmul_rn(v[i][e], id));
+            sum += q;
+            const uint32_t byte = (uint32_t)(q & 0xFF);
+            if (e < 4) lo |= byte << (8 * e); else hi |= byte << (8 * (e - 4));
+        }
+        const int b = 8 * i + (lane >> 2), kc = b >> 2, j = b & 3;
+        const uint32_t kb = (uint32_t)(j * 32 + (lane & 3) * 8);
+        int8_t* row = a.q + ((size_t)kc * a.Mpad + m) * 128;
+        *reinterpret_cast<uint2*>(row + ((((kb >> 4) ^ (uint32_t)(m & 7)) << 4) | (kb & 15))) = make_uint2(lo, hi);
+        if (want_c) {
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        }
+        if ((lane & 3) == 0) {
+            a.d[((size_t)kc * a.Mpad + m) * 4 + j] = d;
+            if (want_c) a.c[((size_t)kc * a.Mpad + m) * 4 + j] = __fmul_rn(d, (float)sum);
+        }
+    }
+}
+
+template <int NC>
+__device__ __forceinline__ void load_chunks(const float* r, float (&v)[NC][8], int lane) {
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        const float4* p = reinterpret_cast<const float4*>(r + 256 * i + 8 * lane);
+        const float4 a = p[0], b = p[1];
+        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+    }
+}
+
+// LayerNorm of a row held as chunks; sm = this warp's D-float staging row.
+template <int NC>
+__device__ __forceinline__ void ln_chunks(float (&v)[NC][8], float* sm, const float* gamma, const float* beta,
+                                          float eps, int lane) {
+    constexpr int D = NC * 256;
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        float4* p = reinterpret_cast<float4*>(sm + 256 * i + 8 * lane);
+        p[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        p[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+    }
+    __syncwarp();
+    float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+    for (int d = 0; d < D; d += 64) { s0 = __fadd_rn(s0, sm[d + lane]); s1 = __fadd_rn(s1, sm[d + lane + 32]); }
+    float s = __fadd_rn(s0, s1);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) s = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, k));
+    s = __shfl_sync(0xffffffffu, s, 0);
+    const float mean = __fdiv_rn(s, (float)D);
+    float w0 = 0.0f, w1 = 0.0f;
+#pragma unroll
+    for (int d = 0; d < D; d += 64) {
+        const float u0 = __fsub_rn(sm[d + lane], mean), u1 = __fsub_rn(sm[d + lane + 32], mean);
+        w0 = __fmaf_rn(u0, u0, w0);
+        w1 = __fmaf_rn(u1, u1, w1);
+    }
+    float w = __fadd_rn(w0, w1);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) w = __fadd_rn(w, __shfl_down_sync(0xffffffffu, w, k));
+    w = __shfl_sync(0xffffffffu, w, 0);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(w, (float)D), eps)));
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        const float4* gp = reinterpret_cast<const float4*>(gamma + 256 * i + 8 * lane);
+        const float4* bp = reinterpret_cast<const float4*>(beta + 256 * i + 8 * lane);
+        const float4 g0 = __ldg(gp), g1 = __ldg(gp + 1), b0 = __ldg(bp), b1 = __ldg(bp + 1);
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[i][e] = __fmaf_rn(__fmul_rn(__fsub_rn(v[i][e], mean), inv), g[e], bb[e]);
+    }
+}
+
+template <int NC>
+__device__ __forceinline__ void store_chunks(float* r, const float (&v)[NC][8], int lane) {
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        float4* p = reinterpret_cast<float4*>(r + 256 * i + 8 * lane);
+        p[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        p[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+    }
+}
+
+// MODE 0: y = LN(x);  MODE 1: y = LN(tok[id] + pos[s]);  MODE 2: quantize x only.
+template <int NC, int MODE>
+__global__ void __launch_bounds__(128) rows_kernel(const float* __restrict__ x, const float* __restrict__ tok,
+                                                   int vocab, const float* __restrict__ pos,
+                                                   const int32_t* __restrict__ tokens, int S, int rows,
+                                                   const float* __restrict__ gamma, const float* __restrict__ beta,
+                                                   float eps, float* y, ActQ a, int quant, int want_c) {
+    extern __shared__ float stage[];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m = blockIdx.x * 4 + w;
+    if (m >= rows) return;
+    constexpr int D = NC * 256;
+    float v[NC][8];
+    if (MODE == 1) {
+        int id = tokens[m];
+        if (id < 0) id += vocab;   // negative ids wrap (mask token), mg-opencl.cpp:670
+        float p[NC][8];
+        load_chunks<NC>(tok + (size_t)id * D, v, lane);
+        load_chunks<NC>(pos + (size_t)(m % S) * D, p, lane);
+#pragma unroll
+        for (int i = 0; i < NC; i++)
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[i][e] = __fadd_rn(v[i][e], p[i][e]);
+    } else {
+        load_chunks<NC>(x + (size_t)m * D, v, lane);
+    }
+    if (MODE != 2) {
+        ln_chunks<NC>(v, stage + w * D, gamma, beta, eps, lane);
+        store_chunks<NC>(y + (size_t)m * D, v, lane);
+    }
+    if (quant) quant_chunks<NC>(v, m, a, want_c != 0, lane);
+}
+
+template <int MODE>
+static bool launch_rows(int D, const float* x, const float* tok, int vocab, const float* pos, const int32_t* tokens,
+                        int S, int rows, const float* gamma, const float* beta, float eps, float* y, const ActQ* a,
+                        bool want_c, cudaStream_t st) {
+    const ActQ aa = a ? *a : ActQ{};
+    const unsigned blocks = (unsigned)((rows + 3) / 4);
+    const size_t sm = MODE == 2 ? 0 : (size_t)4 * D * sizeof(float);
+#define MGC_ROWS(NC)                                                                                       \
+    case NC:                                                                                               \
+        rows_kernel<NC, MODE><<<blocks, 128, sm, st>>>(x, tok, vocab, pos, tokens, S, rows, gamma, beta, eps, y, \
+                                                       aa, a != nullptr, want_c);                          \
+        return true;
+    switch (D % 256 == 0 ? D / 256 : 0) {
+        MGC_ROWS(1) MGC_ROWS(2) MGC_ROWS(3) MGC_ROWS(4) MGC_ROWS(6) MGC_ROWS(8) MGC_ROWS(12)
+        default: return false;
+    }
+#undef MGC_ROWS
+}
+
 #define MGC_NV_SWITCH(D, CALL)           \
     switch ((D) / 32) {                  \
         case 2: { constexpr int NV = 2; CALL; } break;   \
@@ -192,6 +346,8 @@ __global__ void embed_ln_kernel(const float* __restrict__ tok, int vocab, const 
 
 void launch_ln(const float* x, const float* gamma, const float* beta, int rows, int D, float eps,
                float* y, const ActQ* a, bool want_c, cudaStream_t st) {
+    if (D <= 2048 && launch_rows<0>(D, x, nullptr, 0, nullptr, nullptr, 1, rows, gamma, beta, eps, y, a, want_c, st))
+        return;
     const ActQ aa = a ? *a : ActQ{};
     const unsigned blocks = (unsigned)((rows + 7) / 8);
     MGC_NV_SWITCH(D, (ln_kernel<NV><<<blocks, 256, 0, st>>>(x, gamma, beta, rows, eps, y, aa, a != nullptr,
@@ -209,11 +365,21 @@ void launch_embed(const float* tok, int vocab, const float* pos, int E, const in
 void launch_embed_ln(const float* tok, int vocab, const float* pos, int E, const int32_t* tokens, int B,
                      int S, const float* gamma, const float* beta, float eps, float* y, const ActQ* a,
                      bool want_c, cudaStream_t st) {
+    if (E <= 2048 && launch_rows<1>(E, nullptr, tok, vocab, pos, tokens, S, B * S, gamma, beta, eps, y, a, want_c, st))
+        return;
     const int rows = B * S;
     const ActQ aa = a ? *a : ActQ{};
     const unsigned blocks = (unsigned)((rows + 7) / 8);
     MGC_NV_SWITCH(E, (embed_ln_kernel<NV><<<blocks, 256, 0, st>>>(tok, vocab, pos, tokens, S, rows, gamma,
                                                                   beta, eps, y, aa, 1, a != nullptr, want_c)));
+}
+
+void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st) {
+    if (launch_rows<2>(K, x, nullptr, 0, nullptr, nullptr, 1, M, nullptr, nullptr, 0.0f, nullptr, &a, want_c, st))
+        return;
+    const long n = (long)M * (K / 32);
+    quant_act_kernel<true><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, M, K, a.q, a.d,
+                                                                         want_c ? a.c : nullptr, nullptr, a.Mpad);
 }
 
 }  // namespace mgc

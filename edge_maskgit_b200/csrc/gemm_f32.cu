@@ -2,15 +2,15 @@
 // mg-opencl.cpp:57-98).  Used for the MLM head (token_embd, kept F32 by
 // tools/convert_to_gguf.py:213-216) and for linears a GGUF stores unquantized.
 //
-// 128x64 output tile per CTA of 256 threads, 8x4 register micro-tile per thread, K staged
-// 16 at a time in shared memory.  Every output accumulates k = 0..K-1 in order with one
+// 64x64 output tile per CTA of 256 threads, 4x4 register micro-tile per thread, K staged
+// 32 at a time in shared memory.  Every output accumulates k = 0..K-1 in order with one
 // FMA per term, so results equal the sequential reference sum fma by fma.
 #include "kernels.h"
 #include "ptx.cuh"
 
 namespace mgc {
 
-constexpr int GF_BM = 128, GF_BN = 64, GF_BK = 16, GF_TM = 8, GF_TN = 4;
+constexpr int GF_BM = 64, GF_BN = 64, GF_BK = 32;   // 256 threads, 4 x 4 outputs each
 
 __device__ __forceinline__ float act_f32(float v, int a) {
     if (a == 1) return 0.5f * v * (1.0f + erff(v * 0.70710678f));
@@ -22,46 +22,59 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
                                                        int M, int N, int K, const float* __restrict__ bias,
                                                        int act, const float* __restrict__ resid,
                                                        float* __restrict__ y) {
-    __shared__ float As[GF_BK][GF_BM + 4];   // x slab, As[k][m]
-    __shared__ float Bs[GF_BK][GF_BN + 4];   // w slab, Bs[k][n]
-    const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;   // 16 x 16 threads
+    __shared__ __align__(16) float As[GF_BK][GF_BM + 4];   // x slab, As[k][m]
+    __shared__ __align__(16) float Bs[GF_BK][GF_BN + 4];   // w slab, Bs[k][n]
+    const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;   // 16 x 16 threads, 4 x 4 each
     const int m0 = blockIdx.y * GF_BM, n0 = blockIdx.x * GF_BN;
-    float acc[GF_TM][GF_TN];
+    const bool vec = (K % 4) == 0;
+    float acc[4][4];
 #pragma unroll
-    for (int i = 0; i < GF_TM; i++)
+    for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < GF_TN; j++) acc[i][j] = 0.0f;
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
     for (int k0 = 0; k0 < K; k0 += GF_BK) {
-        for (int l = tid; l < GF_BM * GF_BK; l += 256) {
-            const int r = l / GF_BK, kk = l % GF_BK, gm = m0 + r, gk = k0 + kk;
-            As[kk][r] = (gm < M && gk < K) ? x[(size_t)gm * K + gk] : 0.0f;
-        }
-        for (int l = tid; l < GF_BN * GF_BK; l += 256) {
-            const int r = l / GF_BK, kk = l % GF_BK, gn = n0 + r, gk = k0 + kk;
-            Bs[kk][r] = (gn < N && gk < K) ? w[(size_t)gn * K + gk] : 0.0f;
+        // 64 rows x 32 k per operand: 2 float4 per thread, transposed into [k][row]
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int l = tid + 256 * h, r = l / 8, kq = (l % 8) * 4, gk = k0 + kq;
+            float4 xa = make_float4(0, 0, 0, 0), wb = make_float4(0, 0, 0, 0);
+            const int gm = m0 + r, gn = n0 + r;
+            if (vec && gk + 3 < K) {
+                if (gm < M) xa = *reinterpret_cast<const float4*>(x + (size_t)gm * K + gk);
+                if (gn < N) wb = *reinterpret_cast<const float4*>(w + (size_t)gn * K + gk);
+            } else {
+                float t[4], u[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    t[e] = (gm < M && gk + e < K) ? x[(size_t)gm * K + gk + e] : 0.0f;
+                    u[e] = (gn < N && gk + e < K) ? w[(size_t)gn * K + gk + e] : 0.0f;
+                }
+                xa = make_float4(t[0], t[1], t[2], t[3]);
+                wb = make_float4(u[0], u[1], u[2], u[3]);
+            }
+            As[kq][r] = xa.x; As[kq + 1][r] = xa.y; As[kq + 2][r] = xa.z; As[kq + 3][r] = xa.w;
+            Bs[kq][r] = wb.x; Bs[kq + 1][r] = wb.y; Bs[kq + 2][r] = wb.z; Bs[kq + 3][r] = wb.w;
         }
         __syncthreads();
         const int kn = min(GF_BK, K - k0);
-        for (int kk = 0; kk < kn; kk++) {
-            float a[GF_TM], bb[GF_TN];
+        for (int kk = 0; kk < kn; kk++) {   // k ascending: each output is a sequential fma chain
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][tm * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tn * 4]);
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-            for (int i = 0; i < GF_TM; i++) a[i] = As[kk][tm + 16 * i];
+            for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < GF_TN; j++) bb[j] = Bs[kk][tn + 16 * j];
-#pragma unroll
-            for (int i = 0; i < GF_TM; i++)
-#pragma unroll
-                for (int j = 0; j < GF_TN; j++) acc[i][j] = __fmaf_rn(bb[j], a[i], acc[i][j]);
+                for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(bb[j], a[i], acc[i][j]);
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < GF_TM; i++) {
-        const int m = m0 + tm + 16 * i;
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + tm * 4 + i;
         if (m >= M) continue;
 #pragma unroll
-        for (int j = 0; j < GF_TN; j++) {
-            const int n = n0 + tn + 16 * j;
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tn * 4 + j;
             if (n >= N) continue;
             float v = acc[i][j];
             if (bias) v = __fadd_rn(v, bias[n]);

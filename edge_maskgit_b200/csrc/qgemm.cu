@@ -33,10 +33,25 @@ struct QGemmArgs {
     const float* bias; const float* resid; float* y; int act;
 };
 
-// exact int32 -> f32 for |v| < 2^22: place v in the mantissa of 1.5 * 2^23 and subtract.
-__device__ __forceinline__ float i2f_exact(uint32_t v) {
-    return __int_as_float((int)(v + 0x4B400000u)) - 12582912.0f;
+// Packed f32x2 arithmetic (sm_100): each lane is an IEEE round-to-nearest op, bit-identical
+// to the scalar fma / mul / add.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r; asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b)); return r;
 }
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d; asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c)); return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d; asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b)); return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b)); return d;
+}
+// (-1.5 * 2^23, -1.5 * 2^23): |v| < 2^22 always holds (32 * 127 * 128 < 2^22)
+constexpr uint64_t kMagicNeg2 = 0xCB400000CB400000ull;
 
 __device__ __forceinline__ float act_apply(float v, int a) {
     if (a == 1) return 0.5f * v * (1.0f + erff(v * 0.70710678f));
@@ -44,9 +59,30 @@ __device__ __forceinline__ float act_apply(float v, int a) {
     return v;
 }
 
+// Development trace (compile with -DMGC_QGEMM_TRACE): CTA (0,0) stores globaltimer stamps
+// into its own output tile instead of its outputs.  Per 4-block chunk: [0,128) producer
+// issue, [128,256) MMA start, [256,768) MMA committed, [768,1280) warp 2 sees the dot
+// tiles, [1280,1792) warp 2 done.
+#ifdef MGC_QGEMM_TRACE
+__device__ __forceinline__ void trace(const QGemmArgs& p, int idx, long long t0) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1792) {
+        long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        p.y[(size_t)(idx / 32) * p.N + (idx % 32)] = (float)(t - t0);   // inside this CTA's tile
+    }
+}
+#define TRACE(i) trace(p, (i), t_start)
+#else
+#define TRACE(i) ((void)0)
+#endif
+
 template <int BN, int CG, bool Q4K>
 struct QGemmCfg {
-    static constexpr int NST = 4, NBUF = 4, NPW = 4 * CG, CW = BN / CG;
+    // NGRP: TMEM ring of 4-block groups (4 * BN columns each) within 512 columns
+    static constexpr int NPW = 4 * CG, CW = BN / CG;
+    // TMEM ring of 4-block groups (4 * BN columns each), at most 256 columns so two CTAs
+    // can share an SM; shared-memory ring as deep as ~200 KB allows (stage size grows with BN)
+    static constexpr int NGRP = 256 / (4 * BN) >= 2 ? 2 : 1;
+    static constexpr int NST = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
     static constexpr int THREADS = 64 + 32 * NPW;
     static constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = BN * 128, DX_BYTES = 128 * 16,
                               DW_BYTES = 16 * BN;
@@ -57,30 +93,33 @@ struct QGemmCfg {
     static constexpr uint32_t TX_BYTES = A_BYTES + B_BYTES + DX_BYTES + DW_BYTES +
                                          (Q4K ? DW_BYTES + DX_BYTES : 0);
     static constexpr uint32_t SMEM = 1024 + NST * STAGE + 256;
-    static constexpr uint32_t TMEM_COLS = BN * NBUF;
+    static constexpr uint32_t TMEM_COLS = 4 * BN * NGRP;
 };
 
 template <int BN, int CG, bool Q4K>
 __global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K>::THREADS, 1)
 qgemm_kernel(const QGemmArgs p) {
     using C = QGemmCfg<BN, CG, Q4K>;
-    constexpr int NST = C::NST, NBUF = C::NBUF, CW = C::CW;
+    constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= 64 ? 1 : 64 / CW > 4 ? 4 : 64 / CW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* full = (uint64_t*)(smem + NST * C::STAGE);
     uint64_t* empty = full + NST;
     uint64_t* tfull = empty + NST;
-    uint64_t* tempty = tfull + NBUF;
-    uint32_t* tmem_slot = (uint32_t*)(tempty + NBUF);
+    uint64_t* tempty = tfull + NGRP;
+    uint32_t* tmem_slot = (uint32_t*)(tempty + NGRP);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128;
-    const int nb = p.K / 32, nkc = p.K / 128;
+#ifdef MGC_QGEMM_TRACE
+    long long t_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
+#endif
+    const int nkc = p.K / 128;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NST; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + C::NPW); }
-        for (int b = 0; b < NBUF; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], C::NPW); }
+        for (int g = 0; g < NGRP; g++) { mbar_init(&tfull[g], 1); mbar_init(&tempty[g], C::NPW); }
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -92,16 +131,21 @@ qgemm_kernel(const QGemmArgs p) {
 
     if (warp == 0) {
         if (lane == 0) {
+            // a partial last m-tile streams only its valid rows (rounded up to the 8-row
+            // swizzle atom); the MMA rows beyond read stale shared memory and are discarded
+            const uint32_t rows8 = (uint32_t)min(128, (p.M - m0 + 7) & ~7);
+            const uint32_t tx_bytes = C::TX_BYTES - (128 - rows8) * (128 + 16 + (Q4K ? 16 : 0));
             int last_it[NST];
             for (int s = 0; s < NST; s++) last_it[s] = -1;
             for (int kc = 0; kc < nkc; kc++) {
                 const int s = kc % NST, it = kc / NST;
                 if (!mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1)) break;
                 uint8_t* st = smem + s * C::STAGE;
-                mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
-                bulk_g2s(st, p.aq + ((size_t)kc * p.Mpad + m0) * 128, C::A_BYTES, &full[s]);
+                TRACE(kc);
+                mbar_arrive_expect_tx(&full[s], tx_bytes);
+                bulk_g2s(st, p.aq + ((size_t)kc * p.Mpad + m0) * 128, rows8 * 128, &full[s]);
                 bulk_g2s(st + C::OFF_B, p.wq + ((size_t)kc * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
-                bulk_g2s(st + C::OFF_DX, p.adx + ((size_t)kc * p.Mpad + m0) * 4, C::DX_BYTES, &full[s]);
+                bulk_g2s(st + C::OFF_DX, p.adx + ((size_t)kc * p.Mpad + m0) * 4, rows8 * 16, &full[s]);
 #pragma unroll
                 for (int j = 0; j < 4; j++)
                     bulk_g2s(st + C::OFF_DW + j * BN * 4, p.wsa + (size_t)(kc * 4 + j) * p.Npad + n0,
@@ -111,7 +155,7 @@ qgemm_kernel(const QGemmArgs p) {
                     for (int j = 0; j < 4; j++)
                         bulk_g2s(st + C::OFF_MN + j * BN * 4, p.wsb + (size_t)(kc * 4 + j) * p.Npad + n0,
                                  BN * 4, &full[s]);
-                    bulk_g2s(st + C::OFF_CX, p.acx + ((size_t)kc * p.Mpad + m0) * 4, C::DX_BYTES, &full[s]);
+                    bulk_g2s(st + C::OFF_CX, p.acx + ((size_t)kc * p.Mpad + m0) * 4, rows8 * 16, &full[s]);
                 }
                 last_it[s] = it;
             }
@@ -124,85 +168,135 @@ qgemm_kernel(const QGemmArgs p) {
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_make(2, 1, Q4K ? 0 : 1, 128, BN);
-            bool ok = true;
-            for (int kc = 0; kc < nkc && ok; kc++) {
-                const int s = kc % NST, it = kc / NST;
+            for (int kc = 0; kc < nkc; kc++) {
+                const int s = kc % NST, it = kc / NST, g = kc % NGRP, ug = kc / NGRP;
                 if (!mbar_wait(&full[s], it & 1, abort_flag, 2)) break;
+                if (!mbar_wait(&tempty[g], (ug & 1) ^ 1, abort_flag, 3)) break;
                 tc_fence_after();
+                TRACE(128 + kc);
                 const uint32_t a_base = smem_u32(smem + s * C::STAGE), b_base = a_base + C::OFF_B;
+                // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int b = kc * 4 + j, buf = b % NBUF, u = b / NBUF;
-                    if (!mbar_wait(&tempty[buf], (u & 1) ^ 1, abort_flag, 3)) { ok = false; break; }
-                    tc_fence_after();
-                    mma_i8(tmem + buf * BN, sdesc_sw128(a_base + 32 * j), sdesc_sw128(b_base + 32 * j),
+                for (int j = 0; j < 4; j++)
+                    mma_i8(tmem + (g * 4 + j) * BN, sdesc_sw128(a_base + 32 * j), sdesc_sw128(b_base + 32 * j),
                            idesc, 0);
-                    mma_commit(&tfull[buf]);
-                }
-                if (ok) mma_commit(&empty[s]);
+                mma_commit(&tfull[g]);   // the chunk's 4 dot tiles are ready
+                mma_commit(&empty[s]);   // its shared-memory operands may be overwritten
+                TRACE(256 + kc);
             }
         }
     } else {
         const int pw = warp - 2, q = warp & 3, cg = pw >> 2;
         const int row = q * 32 + lane, m = m0 + row, c0 = cg * CW;
         const bool active = (m0 + q * 32) < p.M;   // warp-uniform
-        float acc[CW];
+        uint64_t acc2[CW / 2];   // column pairs (2c, 2c+1), packed for f32x2 math
 #pragma unroll
-        for (int c = 0; c < CW; c++) acc[c] = 0.0f;
-        float4 dxv = make_float4(0, 0, 0, 0), cxv = make_float4(0, 0, 0, 0);
+        for (int c = 0; c < CW / 2; c++) acc2[c] = 0;
         const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16) + c0;
-        for (int b = 0; b < nb; b++) {
-            const int kc = b >> 2, j = b & 3, s = kc % NST;
-            const uint8_t* st = smem + s * C::STAGE;
-            if (j == 0) {
-                bool ok = mbar_wait(&full[s], (kc / NST) & 1, abort_flag, 4);
-                if (!__all_sync(0xffffffffu, ok)) break;
-                dxv = reinterpret_cast<const float4*>(st + C::OFF_DX)[row];
-                if constexpr (Q4K) cxv = reinterpret_cast<const float4*>(st + C::OFF_CX)[row];
+        // Work unit = a batch of BATCH blocks (BATCH*CW int32 per thread, one TMEM-load wait
+        // per batch); BPC batches per 4-block chunk.  (Overlapping batch t+1's loads with batch
+        // t's math measured slower: it forces smaller batches, and the waits dominate.)
+        constexpr int BPC = 4 / BATCH;
+        const int nbatch = nkc * BPC;
+        bool ok = true;
+        // wait for a chunk's operands + dot tiles, then issue the batch's TMEM loads
+        auto issue = [&](uint32_t (&I)[BATCH][CW], int t) {
+            const int kc = t / BPC, jb = t % BPC, g = kc % NGRP;
+            if (jb == 0) {
+                bool w = mbar_wait(&full[kc % NST], (kc / NST) & 1, abort_flag, 4) &&
+                         mbar_wait(&tfull[g], (kc / NGRP) & 1, abort_flag, 5);
+                ok = __all_sync(0xffffffffu, w);
+                if (!ok) return;
+                tc_fence_after();
+                if (warp == 2 && lane == 0) TRACE(768 + kc);
             }
-            const int buf = b % NBUF, u = b / NBUF;
-            bool ok = mbar_wait(&tfull[buf], u & 1, abort_flag, 5);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            tc_fence_after();
-            uint32_t I[CW];
 #pragma unroll
-            for (int t = 0; t < CW / 32; t++)
-                tmem_ld32(t_lane + buf * BN + t * 32, *reinterpret_cast<uint32_t(*)[32]>(&I[t * 32]));
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
-            if (active) {
-                const float dxj = j == 0 ? dxv.x : j == 1 ? dxv.y : j == 2 ? dxv.z : dxv.w;
-                const float* dw = reinterpret_cast<const float*>(st + C::OFF_DW) + j * BN + c0;
+            for (int jj = 0; jj < BATCH; jj++) {
+                const uint32_t ta = t_lane + (g * 4 + jb * BATCH + jj) * BN;
+                if constexpr (CW % 32 == 0) {
 #pragma unroll
-                for (int c = 0; c < CW; c += 4) {
-                    const float4 w4 = *reinterpret_cast<const float4*>(dw + c);
-                    acc[c + 0] = __fmaf_rn(__fmul_rn(w4.x, dxj), i2f_exact(I[c + 0]), acc[c + 0]);
-                    acc[c + 1] = __fmaf_rn(__fmul_rn(w4.y, dxj), i2f_exact(I[c + 1]), acc[c + 1]);
-                    acc[c + 2] = __fmaf_rn(__fmul_rn(w4.z, dxj), i2f_exact(I[c + 2]), acc[c + 2]);
-                    acc[c + 3] = __fmaf_rn(__fmul_rn(w4.w, dxj), i2f_exact(I[c + 3]), acc[c + 3]);
+                    for (int u = 0; u < CW / 32; u++)
+                        tmem_ld32(ta + u * 32, *reinterpret_cast<uint32_t(*)[32]>(&I[jj][u * 32]));
+                } else {
+                    tmem_ld16(ta, I[jj]);
                 }
+            }
+        };
+        // wait for batch t's loads, pin the registers after the wait, release the TMEM group
+        auto landed = [&](uint32_t (&I)[BATCH][CW], int t) {
+            tmem_ld_wait();
+#pragma unroll
+            for (int jj = 0; jj < BATCH; jj++)
+#pragma unroll
+                for (int c = 0; c < CW; c++) asm volatile("" : "+r"(I[jj][c]));
+            if (t % BPC == BPC - 1) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[(t / BPC) % NGRP]);
+            }
+        };
+        auto promote = [&](const uint32_t (&I)[BATCH][CW], int t) {
+            const int kc = t / BPC, jb = t % BPC, s = kc % NST;
+            const uint8_t* st = smem + s * C::STAGE;
+            if (active) {
+                const float4 dxv = reinterpret_cast<const float4*>(st + C::OFF_DX)[row];
+                const float dxa[4] = {dxv.x, dxv.y, dxv.z, dxv.w};
+                float cxa[4] = {0, 0, 0, 0};
                 if constexpr (Q4K) {
-                    const float cxj = j == 0 ? cxv.x : j == 1 ? cxv.y : j == 2 ? cxv.z : cxv.w;
-                    const float* mn = reinterpret_cast<const float*>(st + C::OFF_MN) + j * BN + c0;
+                    const float4 cxv = reinterpret_cast<const float4*>(st + C::OFF_CX)[row];
+                    cxa[0] = cxv.x; cxa[1] = cxv.y; cxa[2] = cxv.z; cxa[3] = cxv.w;
+                }
+#pragma unroll
+                for (int jj = 0; jj < BATCH; jj++) {   // blocks in ascending order: b = 4 kc + j
+                    const int j = jb * BATCH + jj;
+                    const uint64_t dx2 = pack2(dxa[j], dxa[j]);
+                    const float* dw = reinterpret_cast<const float*>(st + C::OFF_DW) + j * BN + c0;
 #pragma unroll
                     for (int c = 0; c < CW; c += 4) {
-                        const float4 n4 = *reinterpret_cast<const float4*>(mn + c);
-                        acc[c + 0] = __fmaf_rn(-n4.x, cxj, acc[c + 0]);
-                        acc[c + 1] = __fmaf_rn(-n4.y, cxj, acc[c + 1]);
-                        acc[c + 2] = __fmaf_rn(-n4.z, cxj, acc[c + 2]);
-                        acc[c + 3] = __fmaf_rn(-n4.w, cxj, acc[c + 3]);
+                        const float4 w4 = *reinterpret_cast<const float4*>(dw + c);
+                        // exact int32 -> f32: bits(v + 0x4B400000) = 1.5*2^23 + v, minus 1.5*2^23
+                        const uint64_t f01 = add2(pack2(__uint_as_float(I[jj][c] + 0x4B400000u),
+                                                        __uint_as_float(I[jj][c + 1] + 0x4B400000u)), kMagicNeg2);
+                        const uint64_t f23 = add2(pack2(__uint_as_float(I[jj][c + 2] + 0x4B400000u),
+                                                        __uint_as_float(I[jj][c + 3] + 0x4B400000u)), kMagicNeg2);
+                        acc2[c / 2] = fma2(mul2(pack2(w4.x, w4.y), dx2), f01, acc2[c / 2]);
+                        acc2[c / 2 + 1] = fma2(mul2(pack2(w4.z, w4.w), dx2), f23, acc2[c / 2 + 1]);
+                    }
+                    if constexpr (Q4K) {
+                        const uint64_t cx2 = pack2(cxa[j], cxa[j]);
+                        const float* mn = reinterpret_cast<const float*>(st + C::OFF_MN) + j * BN + c0;
+#pragma unroll
+                        for (int c = 0; c < CW; c += 4) {
+                            const float4 n4 = *reinterpret_cast<const float4*>(mn + c);
+                            acc2[c / 2] = fma2(pack2(-n4.x, -n4.y), cx2, acc2[c / 2]);
+                            acc2[c / 2 + 1] = fma2(pack2(-n4.z, -n4.w), cx2, acc2[c / 2 + 1]);
+                        }
                     }
                 }
             }
-            if (j == 3) {
+            if (jb == BPC - 1) {   // chunk done: its shared-memory stage may be refilled
+                if (warp == 2 && lane == 0) TRACE(1280 + kc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
+        };
+        for (int t = 0; ok && t < nbatch; t++) {
+            uint32_t I[BATCH][CW];
+            issue(I, t);
+            if (!ok) break;
+            landed(I, t);
+            promote(I, t);
         }
         // epilogue: bias -> act -> residual (mg-opencl.cpp:481-493)
-        if (m < p.M && !*abort_flag) {
+        float acc[CW];
+#pragma unroll
+        for (int c = 0; c < CW / 2; c++) unpack2(acc2[c], acc[2 * c], acc[2 * c + 1]);
+#ifdef MGC_QGEMM_TRACE
+        const bool keep_stamps = blockIdx.x == 0 && blockIdx.y == 0;   // trace build: no stores
+#else
+        constexpr bool keep_stamps = false;
+#endif
+        if (m < p.M && !*abort_flag && !keep_stamps) {
             const int nbase = n0 + c0;
             const bool vec = (p.N % 4) == 0;
 #pragma unroll
@@ -257,11 +351,13 @@ static int set_smem_attr() {
 // Sets the dynamic shared-memory limit of every instantiation on the current device.  Must
 // run once per device before the first launch (the runtime does it at creation, outside any
 // stream capture).
+#define MGC_QGEMM_CONFIGS(X) X(32, 1) X(32, 2) X(64, 2) X(64, 4) X(128, 4)
+
 int qgemm_prepare() {
     int rc = 0;
-    rc |= set_smem_attr<128, 2, false>(); rc |= set_smem_attr<128, 2, true>();
-    rc |= set_smem_attr<64, 2, false>();  rc |= set_smem_attr<64, 2, true>();
-    rc |= set_smem_attr<32, 1, false>();  rc |= set_smem_attr<32, 1, true>();
+#define X(BN, CG) rc |= set_smem_attr<BN, CG, false>(); rc |= set_smem_attr<BN, CG, true>();
+    MGC_QGEMM_CONFIGS(X)
+#undef X
     return rc;
 }
 
@@ -273,28 +369,35 @@ static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
-// Tile width: the widest BN that still gives >= ~one CTA per SM; MGC_QGEMM_BN overrides.
-static int pick_bn(int M, int N) {
-    static int forced = -1;
-    if (forced < 0) {
-        const char* e = std::getenv("MGC_QGEMM_BN");
-        forced = e ? std::atoi(e) : 0;
+// Tile shape (BN columns, CG column groups of promotion warps).  MGC_QGEMM_CFG="BN,CG"
+// overrides the heuristic (used to sweep shapes).
+static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
+    static int fbn = -1, fcg = 0;
+    if (fbn < 0) {
+        fbn = 0;
+        if (const char* e = std::getenv("MGC_QGEMM_CFG")) std::sscanf(e, "%d,%d", &fbn, &fcg);
     }
-    if (forced == 32 || forced == 64 || forced == 128) return forced;
-    const int mt = (M + 127) / 128;
-    for (int bn : {128, 64}) if ((long)mt * ((N + bn - 1) / bn) >= 140) return bn;
-    return 32;
+    if (fbn) { bn = fbn; cg = fcg; return; }
+    (void)K;
+    // measured (ncu, cold L2) over the config-2 sweep: 32 columns x 2 warp groups wins at
+    // M <= ~512, 64 x 2 above
+    bn = M <= 512 ? 32 : 64;
+    cg = 2;
+    (void)N;
 }
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
                  const float* resid, float* y, cudaStream_t st) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
     QGemmArgs p{a.q, a.d, a.c, a.Mpad, w.q, w.sa, w.sb, w.Npad, M, w.N, w.K, bias, resid, y, act};
-    const int bn = pick_bn(M, w.N);
+    int bn, cg;
+    pick_cfg(M, w.N, w.K, bn, cg);
     const bool q4 = w.wtype == 12;
-    if (bn == 128) return q4 ? run_qgemm<128, 2, true>(p, st) : run_qgemm<128, 2, false>(p, st);
-    if (bn == 64) return q4 ? run_qgemm<64, 2, true>(p, st) : run_qgemm<64, 2, false>(p, st);
-    return q4 ? run_qgemm<32, 1, true>(p, st) : run_qgemm<32, 1, false>(p, st);
+#define X(BN, CG) \
+    if (bn == BN && cg == CG) return q4 ? run_qgemm<BN, CG, true>(p, st) : run_qgemm<BN, CG, false>(p, st);
+    MGC_QGEMM_CONFIGS(X)
+#undef X
+    return -2;
 }
 
 }  // namespace mgc
