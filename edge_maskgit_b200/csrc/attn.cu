@@ -45,7 +45,8 @@ __device__ __forceinline__ void st_half(uint8_t* blk, int r, int k, __half v) {
 }
 
 __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ qkv, int S, int H, float scale,
-                                                     float* __restrict__ out) {
+                                                     float* __restrict__ out, int nsplit, int tiles_per,
+                                                     float* __restrict__ opart, float* __restrict__ mlpart) {
     using namespace fa;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -55,7 +56,7 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.y, b = blockIdx.z, q0 = blockIdx.x * BM;
+    const int h = blockIdx.y, b = blockIdx.z / nsplit, split = blockIdx.z % nsplit, q0 = blockIdx.x * BM;
     const int E = H * D, W = 3 * E;
     const float* base = qkv + (size_t)b * S * W + h * D;
 
@@ -90,7 +91,6 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
     const uint32_t tmem = *tmem_slot;
     const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);
 
-    constexpr uint32_t idesc_s = idesc_make(1, 0, 0, BM, BC);
     constexpr uint32_t idesc_o = idesc_make(1, 0, 0, BM, D);
     const uint32_t sQ = smem_u32(sm + OFF_Q), sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_VT),
                    sPh = smem_u32(sm + OFF_PH), sPl = smem_u32(sm + OFF_PL);
@@ -100,10 +100,14 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
     for (int d = 0; d < D; d++) o[d] = 0.0f;
     float m_i = -INFINITY, l_i = 0.0f;
     const int ntiles = (S + BC - 1) / BC;
+    const int kt0 = split * tiles_per, kt1 = min(ntiles, kt0 + tiles_per);
+    const bool wact = q0 + warp * 32 < S;   // warp-uniform: this warp owns at least one real query row
     bool ok = true;
 
-    for (int kt = 0; kt < ntiles && ok; kt++) {
-        const int kb = kt * BC;
+    for (int kt = kt0; kt < kt1 && ok; kt++) {
+        const int kb = kt * BC, ph = (kt - kt0) & 1;
+        // a short last tile runs the MMAs at N (and K for P.V) = valid keys rounded up to 16
+        const int nvalid = min(BC, S - kb), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
         // ---- 1. stage K and V^T (f16)
         {
             const int t = kb + tid;
@@ -139,20 +143,22 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
         if (tid == 0) {
             tc_fence_after();
 #pragma unroll
+            const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
             for (int k = 0; k < D / 16; k++)
                 mma_f16(tmem, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idesc_s, k > 0);
             mma_commit(bar_s);
         }
-        ok = mbar_wait(bar_s, kt & 1, abort_flag, 21);
+        ok = mbar_wait(bar_s, ph, abort_flag, 21);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; }
         ok = __syncthreads_and(ok);
         if (!ok) break;
         tc_fence_after();
         // ---- 3. softmax row update, P = hi + lo
-        const int nvalid = min(BC, S - kb);
-        float m_new = m_i;
+        float m_new = m_i, alpha = 1.0f;
+        if (wact) {
 #pragma unroll
         for (int ch = 0; ch < BC / 32; ch++) {
+            if (ch >= nch) break;
             uint32_t r[32];
             tmem_ld32(t_row + ch * 32, r);
             tmem_ld_wait();
@@ -160,11 +166,12 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
             for (int j = 0; j < 32; j++)
                 if (ch * 32 + j < nvalid) m_new = fmaxf(m_new, __fmul_rn(__uint_as_float(r[j]), scale));
         }
-        const float alpha = expf(m_i - m_new);
+        alpha = expf(m_i - m_new);
         float l_new = __fmul_rn(alpha, l_i);
         const int row = warp * 32 + lane;
 #pragma unroll
         for (int ch = 0; ch < BC / 32; ch++) {
+            if (ch >= nch) break;
             uint32_t r[32];
             tmem_ld32(t_row + ch * 32, r);
             tmem_ld_wait();
@@ -194,6 +201,7 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
         }
         m_i = m_new;
         l_i = l_new;
+        }
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -204,7 +212,7 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
             for (int part = 0; part < 2; part++) {
                 const uint32_t sP = part == 0 ? sPh : sPl;
 #pragma unroll
-                for (int j = 0; j < BC / 16; j++) {
+                for (int j = 0; j < nmma / 16; j++) {
                     const uint32_t a = sP + (j >> 2) * P_BLK + (j & 3) * 32;
                     const uint32_t bv = sV + (j >> 2) * VT_BLK + (j & 3) * 32;
                     mma_f16(tmem + BC, sdesc_sw128(a), sdesc_sw128(bv), idesc_o, (part | j) != 0);
@@ -212,13 +220,13 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
             }
             mma_commit(bar_o);
         }
-        ok = mbar_wait(bar_o, kt & 1, abort_flag, 22);
+        ok = mbar_wait(bar_o, ph, abort_flag, 22);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; }
         ok = __syncthreads_and(ok);
         if (!ok) break;
         tc_fence_after();
         // ---- 5. o = alpha * o + O_tile
-        {
+        if (wact) {
             uint32_t r[32], r2[16];
             tmem_ld32(t_row + BC, r);
             tmem_ld16(t_row + BC + 32, r2);
@@ -233,7 +241,13 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
     }
 
     const int qr = q0 + warp * 32 + lane;
-    if (ok && qr < S) {
+    if (ok && qr < S && nsplit > 1) {   // partial result of this key range, merged by attn_combine
+        const size_t R = (size_t)(gridDim.z / nsplit) * S, r = (size_t)split * R + (size_t)b * S + qr;
+        float4* dst = reinterpret_cast<float4*>(opart + r * E + h * D);
+#pragma unroll
+        for (int d = 0; d < D; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        reinterpret_cast<float2*>(mlpart)[r * H + h] = make_float2(m_i, l_i);
+    } else if (ok && qr < S) {
         const float inv = __fdiv_rn(1.0f, l_i);
         float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D);
 #pragma unroll
@@ -249,6 +263,35 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
     }
 }
 
+// Merge the key-range partials: m = max m_s, l = sum l_s e^(m_s - m), o = sum o_s e^(m_s - m) / l.
+__global__ void attn_combine(const float* __restrict__ opart, const float* __restrict__ mlpart, int nsplit,
+                             int R, int H, float* __restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;   // (row, head, 4-dim group)
+    constexpr int G = fa::D / 4;
+    if (i >= R * H * G) return;
+    const int rh = i / G, d = (i % G) * 4, r = rh / H, h = rh % H, E = H * fa::D;
+    const float2* ml = reinterpret_cast<const float2*>(mlpart);
+    float m = -INFINITY;
+    for (int s = 0; s < nsplit; s++) m = fmaxf(m, ml[(size_t)s * R * H + rh].x);
+    float l = 0.0f;
+    float4 acc = make_float4(0, 0, 0, 0);
+    for (int s = 0; s < nsplit; s++) {
+        const float2 v2 = ml[(size_t)s * R * H + rh];
+        const float wgt = expf(v2.x - m);
+        l = __fmaf_rn(v2.y, wgt, l);
+        const float4 v = *reinterpret_cast<const float4*>(opart + ((size_t)s * R + r) * E + h * fa::D + d);
+        acc.x = __fmaf_rn(v.x, wgt, acc.x); acc.y = __fmaf_rn(v.y, wgt, acc.y);
+        acc.z = __fmaf_rn(v.z, wgt, acc.z); acc.w = __fmaf_rn(v.w, wgt, acc.w);
+    }
+    const float inv = __fdiv_rn(1.0f, l);
+    *reinterpret_cast<float4*>(out + (size_t)r * E + h * fa::D + d) =
+        make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
+}
+
+size_t attn_scratch_floats(int B, int S, int H) {
+    return (size_t)kAttnMaxSplit * B * S * H * (fa::D + 2);
+}
+
 static bool g_attn_ready[64] = {};
 
 int attn_prepare() {
@@ -260,14 +303,27 @@ int attn_prepare() {
     return 0;
 }
 
-int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, cudaStream_t st) {
+int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
+                      size_t scratch_floats, cudaStream_t st) {
     if (Dh != fa::D) return -2;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return -1;
     if (!g_attn_ready[dev] && attn_prepare() != 0) return -1;   // runtimes prepare at creation
-    dim3 grid((S + fa::BM - 1) / fa::BM, H, B);
-    flash_attn_tc<<<grid, 128, fa::SMEM, st>>>(qkv, S, H, scale, out);
+    // Split the key range over CTAs when (query tiles x heads x images) leaves SMs idle.
+    const int qt = (S + fa::BM - 1) / fa::BM, ntiles = (S + fa::BC - 1) / fa::BC;
+    const long ctas = (long)qt * H * B;
+    int nsplit = 1;
+    if (scratch && scratch_floats >= attn_scratch_floats(B, S, H))
+        while (nsplit < kAttnMaxSplit && nsplit < ntiles && ctas * (nsplit + 1) <= 2 * 148) nsplit++;
+    const int tiles_per = (ntiles + nsplit - 1) / nsplit;
+    nsplit = (ntiles + tiles_per - 1) / tiles_per;   // no empty split
+    const int R = B * S;
+    float* opart = scratch;
+    float* mlpart = scratch ? scratch + (size_t)nsplit * R * H * fa::D : nullptr;
+    dim3 grid(qt, H, B * nsplit);
+    flash_attn_tc<<<grid, 128, fa::SMEM, st>>>(qkv, S, H, scale, out, nsplit, tiles_per, opart, mlpart);
+    if (nsplit > 1) attn_combine<<<(R * H * (fa::D / 4) + 255) / 256, 256, 0, st>>>(opart, mlpart, nsplit, R, H, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -61,8 +61,11 @@ int attn_prepare();
 void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const float* bias, int act,
                      const float* resid, float* y, cudaStream_t st);
 // fp16-K/V flash attention, qkv [B*S][3E] -> out [B*S][E]
-int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out,
-                      cudaStream_t st);
+// scratch (optional) holds the key-split partials: attn_scratch_floats() floats.
+constexpr int kAttnMaxSplit = 4;
+size_t attn_scratch_floats(int B, int S, int H);
+int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
+                      size_t scratch_floats, cudaStream_t st);
 
 }  // namespace mgc
 

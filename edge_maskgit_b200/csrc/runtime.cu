@@ -197,7 +197,7 @@ ActQ alloc_actq(int Mpad, int K) {
 void free_actq(ActQ& a) { cudaFree(a.q); cudaFree(a.d); cudaFree(a.c); a = ActQ{}; }
 
 // Library scratch used by the standalone mgc_qgemm entry point (grown on demand, per device).
-struct Scratch { ActQ a; int Mpad = 0, K = 0; };
+struct Scratch { ActQ a; int Mpad = 0, K = 0; float* attn = nullptr; size_t attn_n = 0; };
 std::map<int, Scratch> g_scratch;
 std::mutex g_scratch_mu;
 
@@ -311,8 +311,19 @@ int mgc_layernorm_affine(const float* x, const float* gamma, const float* beta, 
 int mgc_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, void* stream) {
     return guard([&] {
         if (B <= 0 || S <= 0 || H <= 0) throw Err("mgc_flash_attn: bad sizes");
-        if (launch_flash_attn(qkv, B, S, H, Dh, scale, out, (cudaStream_t)stream) != 0)
-            throw Err("mgc_flash_attn: head_dim must be 48");
+        if (Dh != 48) throw Err("mgc_flash_attn: head_dim must be 48");
+        int dev; CK(cudaGetDevice(&dev));
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        Scratch& sc = g_scratch[dev];
+        const size_t need = attn_scratch_floats(B, S, H);
+        if (sc.attn_n < need) {
+            CK(cudaStreamSynchronize((cudaStream_t)stream));
+            cudaFree(sc.attn);
+            sc.attn = dalloc<float>(need);
+            sc.attn_n = need;
+        }
+        if (launch_flash_attn(qkv, B, S, H, Dh, scale, out, sc.attn, sc.attn_n, (cudaStream_t)stream) != 0)
+            throw Err(std::string("mgc_flash_attn: launch failed: ") + cudaGetErrorString(cudaGetLastError()));
     });
 }
 
@@ -356,6 +367,8 @@ struct mgc_runtime {
     float *x = nullptr, *t = nullptr, *qkv = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr;
     int32_t* tokens = nullptr;
     ActQ aE, aF;
+    float* attn_scratch = nullptr;   // key-split partials of the attention
+    size_t attn_scratch_n = 0;
     // host staging (pinned)
     int32_t* h_tokens = nullptr;
     float* h_logits = nullptr;
@@ -434,7 +447,8 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
         const LayerW& L = rt->layers[l];
         op(mm, [&] { linear(rt, L.qkv, rt->x, rt->aE, R, L.bqkv, 0, nullptr, rt->qkv); });
         op("FlashAttention", [&] {
-            if (launch_flash_attn(rt->qkv, B, S, rt->n_head, rt->Dh, scale, rt->att, st) != 0)
+            if (launch_flash_attn(rt->qkv, B, S, rt->n_head, rt->Dh, scale, rt->att, rt->attn_scratch,
+                                  rt->attn_scratch_n, st) != 0)
                 throw Err("flash attention launch failed");
         });
         if (L.o.wtype != 0) op("Quantize", [&] { launch_quant_act_tiled(rt->att, R, E, rt->aE, qc, st); });
@@ -494,7 +508,7 @@ void destroy_runtime(mgc_runtime* rt) {
     free_weight(rt->proj);
     for (float* p : rt->f32_allocs) cudaFree(p);
     cudaFree(rt->x); cudaFree(rt->t); cudaFree(rt->qkv); cudaFree(rt->att); cudaFree(rt->ff);
-    cudaFree(rt->logits); cudaFree(rt->tokens);
+    cudaFree(rt->logits); cudaFree(rt->tokens); cudaFree(rt->attn_scratch);
     free_actq(rt->aE); free_actq(rt->aF);
     if (rt->h_tokens) cudaFreeHost(rt->h_tokens);
     if (rt->h_logits) cudaFreeHost(rt->h_logits);
@@ -578,6 +592,8 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->tokens = dalloc<int32_t>(R);
         rt->aE = alloc_actq(rt->Mpad, E);
         rt->aF = alloc_actq(rt->Mpad, F);
+        rt->attn_scratch_n = attn_scratch_floats(1, rt->Mpad, rt->n_head);
+        rt->attn_scratch = dalloc<float>(rt->attn_scratch_n);
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
         CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
         CK(cudaDeviceSynchronize());

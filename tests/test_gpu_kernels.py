@@ -113,7 +113,7 @@ def test_layernorm_bit_exact(dev, oracle_mod, rows, D):
     assert np.array_equal(y, oracle_mod.layernorm_affine(x, g, b, 1e-12))
 
 
-@pytest.mark.parametrize("B,S", [(1, 257), (2, 17), (1, 1), (1, 33)])
+@pytest.mark.parametrize("B,S", [(1, 257), (2, 17), (1, 1), (1, 33), (3, 257), (1, 1025), (2, 129)])
 def test_flash_attn(dev, oracle_mod, B, S):
     from edge_maskgit_b200 import runtime as rt
     H, Dh = 16, 48
