@@ -208,12 +208,12 @@ def run_cuda_arm(args) -> None:
         r.forward(tok_host)
     prof = {p.op: p for p in r.profile_report()}
     r.profile_enable(False)
-    launches_per_fwd = sum(p.count for p in prof.values()) // 5
 
     # ---- device-resident timing: CUDA-graph replay, inputs in HBM
     for _ in range(args.warmup):
         r.forward_dev(tok_dev, logits_dev, 1, S)
     r.sync()
+    launches_per_fwd = r.kernel_count()   # kernels in the captured step graph
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()

@@ -46,6 +46,7 @@ _SIGS = {
     "mgc_runtime_sync": (I, [P]),
     "mgc_runtime_stream": (P, [P]),
     "mgc_generate": (I, [P, I, P, P, I, F, P]),
+    "mgc_runtime_kernel_count": (I, [P]),
     "mgc_profile_enable": (I, [P, I]),
     "mgc_profile_reset": (I, [P]),
     "mgc_profile_report": (I, [P, C.c_char_p, C.c_size_t]),

@@ -68,6 +68,7 @@ __global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, int8
 
 void launch_quant_act_plain(const float* x, int M, int K, int8_t* qx, float* dx, int32_t* sumx,
                             cudaStream_t st) {
+    ++g_launch_count;
     const long n = (long)M * (K / 32);
     quant_act_kernel<false><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, M, K, qx, dx, nullptr, sumx, 0);
 }
@@ -346,6 +347,7 @@ static bool launch_rows(int D, const float* x, const float* tok, int vocab, cons
 
 void launch_ln(const float* x, const float* gamma, const float* beta, int rows, int D, float eps,
                float* y, const ActQ* a, bool want_c, cudaStream_t st) {
+    ++g_launch_count;
     if (D <= 2048 && launch_rows<0>(D, x, nullptr, 0, nullptr, nullptr, 1, rows, gamma, beta, eps, y, a, want_c, st))
         return;
     const ActQ aa = a ? *a : ActQ{};
@@ -356,6 +358,7 @@ void launch_ln(const float* x, const float* gamma, const float* beta, int rows, 
 
 void launch_embed(const float* tok, int vocab, const float* pos, int E, const int32_t* tokens, int B,
                   int S, float* y, cudaStream_t st) {
+    ++g_launch_count;
     const int rows = B * S;
     const unsigned blocks = (unsigned)((rows + 7) / 8);
     MGC_NV_SWITCH(E, (embed_ln_kernel<NV><<<blocks, 256, 0, st>>>(tok, vocab, pos, tokens, S, rows, nullptr,
@@ -365,6 +368,7 @@ void launch_embed(const float* tok, int vocab, const float* pos, int E, const in
 void launch_embed_ln(const float* tok, int vocab, const float* pos, int E, const int32_t* tokens, int B,
                      int S, const float* gamma, const float* beta, float eps, float* y, const ActQ* a,
                      bool want_c, cudaStream_t st) {
+    ++g_launch_count;
     if (E <= 2048 && launch_rows<1>(E, nullptr, tok, vocab, pos, tokens, S, B * S, gamma, beta, eps, y, a, want_c, st))
         return;
     const int rows = B * S;
@@ -375,6 +379,7 @@ void launch_embed_ln(const float* tok, int vocab, const float* pos, int E, const
 }
 
 void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st) {
+    ++g_launch_count;
     if (launch_rows<2>(K, x, nullptr, 0, nullptr, nullptr, 1, M, nullptr, nullptr, 0.0f, nullptr, &a, want_c, st))
         return;
     const long n = (long)M * (K / 32);

@@ -323,6 +323,7 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     float* mlpart = scratch ? scratch + (size_t)nsplit * R * H * fa::D : nullptr;
     dim3 grid(qt, H, B * nsplit);
     flash_attn_tc<<<grid, 128, fa::SMEM, st>>>(qkv, S, H, scale, out, nsplit, tiles_per, opart, mlpart);
+    g_launch_count += nsplit > 1 ? 2 : 1;
     if (nsplit > 1) attn_combine<<<(R * H * (fa::D / 4) + 255) / 256, 256, 0, st>>>(opart, mlpart, nsplit, R, H, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }

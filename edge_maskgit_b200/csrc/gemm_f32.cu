@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
 
 void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const float* bias, int act,
                      const float* resid, float* y, cudaStream_t st) {
+    ++g_launch_count;
     dim3 grid((N + GF_BN - 1) / GF_BN, (M + GF_BM - 1) / GF_BM);
     gemm_f32_kernel<<<grid, 256, 0, st>>>(w, x, M, N, K, bias, act, resid, y);
 }

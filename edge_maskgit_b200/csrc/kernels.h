@@ -37,6 +37,11 @@ struct QWeight {
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+// Kernels this library has launched (host-side count, for the runtime's launch report).
+extern int g_launch_count;
+// A bounded busy-wait kernel of ~`cycles` SM clocks (profiling: lets the host run ahead).
+void launch_spin(long long cycles, cudaStream_t st);
+
 // quantizer: x [M][K] f32 -> tiled ActQ (want_c: also write the Q4_K correction term)
 void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st);
 // quantizer with plain outputs (kernel-level C ABI)

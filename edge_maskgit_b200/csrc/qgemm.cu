@@ -363,6 +363,7 @@ int qgemm_prepare() {
 
 template <int BN, int CG, bool Q4K>
 static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
+    ++g_launch_count;
     using C = QGemmCfg<BN, CG, Q4K>;
     dim3 grid((a.N + BN - 1) / BN, (a.M + 127) / 128);
     qgemm_kernel<BN, CG, Q4K><<<grid, C::THREADS, C::SMEM, st>>>(a);

@@ -28,6 +28,13 @@
 
 namespace mgc {
 __device__ int g_dev_error = 0;
+int g_launch_count = 0;
+
+__global__ void spin_kernel(long long cycles) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < cycles) {}
+}
+void launch_spin(long long cycles, cudaStream_t st) { spin_kernel<<<1, 1, 0, st>>>(cycles); }
 }
 
 using namespace mgc;
@@ -376,6 +383,7 @@ struct mgc_runtime {
     std::map<std::tuple<int, int, const void*, const void*>, cudaGraphExec_t> graphs;
     // profiling
     bool prof = false;
+    int last_launches = 0;   // kernels enqueued by the last forward
     std::map<std::string, ProfRow> prof_rows;
 
     float* up_f32(const GgufTensor& t, size_t n) {
@@ -426,17 +434,21 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
         CK(cudaMemcpyAsync(dump + doff, src, sizeof(float) * (size_t)R * w, cudaMemcpyDeviceToDevice, st));
         doff += (size_t)R * w;
     };
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    if (rt->prof) { CK(cudaEventCreate(&e0)); CK(cudaEventCreate(&e1)); }
+    // Profiling: a bounded spin kernel holds the GPU while the host enqueues every op with an
+    // event pair, so the events time GPU execution only (no host launch gaps).
+    struct Ev { const char* name; cudaEvent_t a, b; };
+    std::vector<Ev> evs;
+    if (rt->prof) launch_spin(2000000, st);   // ~1 ms at 2 GHz
     auto op = [&](const char* name, auto&& fn) {
         if (!rt->prof) { fn(); return; }
-        CK(cudaEventRecord(e0, st));
+        Ev e{name, nullptr, nullptr};
+        CK(cudaEventCreate(&e.a)); CK(cudaEventCreate(&e.b));
+        CK(cudaEventRecord(e.a, st));
         fn();
-        CK(cudaEventRecord(e1, st));
-        CK(cudaEventSynchronize(e1));
-        float ms = 0; CK(cudaEventElapsedTime(&ms, e0, e1));
-        ProfRow& r = rt->prof_rows[name]; r.ms += ms; r.n++;
+        CK(cudaEventRecord(e.b, st));
+        evs.push_back(e);
     };
+    const int launches0 = g_launch_count;
     const bool qc = rt->any_q4k;
     const char* mm = rt->wtype == 0 ? "MulMat(f32)" : "MulMat(q)";
     op("GetRows+Norm", [&] { launch_embed_ln(rt->tok, rt->V, rt->pos, E, tokens, B, S, rt->g0, rt->b0, rt->eps,
@@ -467,7 +479,16 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
     op("MulMat(f32)", [&] { launch_gemm_f32(rt->tok, rt->x, R, rt->V, E, rt->obias, 0, nullptr, logits, st); });
     put(logits, rt->V);
     CK(cudaPeekAtLastError());
-    if (e0) { cudaEventDestroy(e0); cudaEventDestroy(e1); }
+    rt->last_launches = g_launch_count - launches0;
+    if (rt->prof) {
+        CK(cudaStreamSynchronize(st));
+        for (Ev& e : evs) {
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, e.a, e.b));
+            ProfRow& r = rt->prof_rows[e.name]; r.ms += ms; r.n++;
+            cudaEventDestroy(e.a); cudaEventDestroy(e.b);
+        }
+    }
 }
 
 // Forward through a cached CUDA graph (captured on the first call for this key).
@@ -726,6 +747,8 @@ int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_
         std::memcpy(tokens_out, result.data(), sizeof(int32_t) * B * S);
     });
 }
+
+int mgc_runtime_kernel_count(const mgc_runtime* rt) { return rt ? rt->last_launches : -1; }
 
 int mgc_profile_enable(mgc_runtime* rt, int on) { if (!rt) return -1; rt->prof = on != 0; return 0; }
 int mgc_profile_reset(mgc_runtime* rt) { if (!rt) return -1; rt->prof_rows.clear(); return 0; }

@@ -201,6 +201,10 @@ class CudaRuntime:
     def profile_reset(self) -> None:
         check(lib.mgc_profile_reset(self._h))
 
+    def kernel_count(self) -> int:
+        """Kernels enqueued by the last forward."""
+        return int(lib.mgc_runtime_kernel_count(self._h))
+
     def profile_report(self) -> list[OpProfile]:
         buf = C.create_string_buffer(1 << 14)
         check(lib.mgc_profile_report(self._h, buf, len(buf)))

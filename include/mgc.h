@@ -135,6 +135,9 @@ void* mgc_runtime_stream(mgc_runtime* rt);
 int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_t* seeds,
                  int steps, float temperature, int32_t* tokens_out);
 
+/* Number of kernels the runtime's last forward enqueued (all are this library's own). */
+int mgc_runtime_kernel_count(const mgc_runtime* rt);
+
 /* Per-op-type profile (OpenCLRuntime::profile_enable/reset/report, mg-opencl.hpp:50-53).
  * When enabled, forwards run eagerly with CUDA events around each kernel. */
 int mgc_profile_enable(mgc_runtime* rt, int on);
