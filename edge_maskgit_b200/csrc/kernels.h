@@ -56,9 +56,17 @@ void launch_embed(const float* tok, int vocab, const float* pos, int E, const in
 void launch_embed_ln(const float* tok, int vocab, const float* pos, int E, const int32_t* tokens,
                      int B, int S, const float* gamma, const float* beta, float eps, float* y,
                      const ActQ* a, bool want_c, cudaStream_t st);
-// int8-dot GEMM on tcgen05: y = act(W . x + bias) + resid
+// Split-K scratch: partial sums (part_floats floats) and per-tile arrival counters
+// (n_counters ints, zero-initialised once; the kernel leaves them at zero again).
+struct SplitK {
+    float* part = nullptr;
+    size_t part_floats = 0;
+    int* counters = nullptr;
+    int n_counters = 0;
+};
+// int8-dot GEMM on tcgen05: y = act(W . x + bias) + resid.  sk == nullptr: no split-K.
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
-                 const float* resid, float* y, cudaStream_t st);
+                 const float* resid, float* y, cudaStream_t st, const SplitK* sk = nullptr);
 // set the kernels' shared-memory limits on the current device (once per device)
 int qgemm_prepare();
 int attn_prepare();

@@ -23,6 +23,9 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
+
+
 
 namespace mgc {
 
@@ -31,6 +34,9 @@ struct QGemmArgs {
     const int8_t* wq; const float* wsa; const float* wsb; int Npad;
     int M, N, K;
     const float* bias; const float* resid; float* y; int act;
+    // split-K: CTA z of gridDim.z handles K chunks [z*cps, (z+1)*cps); partials go to
+    // part [nsplit][M][N], the last CTA of a tile (counters[tile] reaches nsplit) reduces them
+    float* part; int* counters; int nsplit, cps;
 };
 
 // Packed f32x2 arithmetic (sm_100): each lane is an IEEE round-to-nearest op, bit-identical
@@ -65,7 +71,7 @@ __device__ __forceinline__ float act_apply(float v, int a) {
 // tiles, [1280,1792) warp 2 done.
 #ifdef MGC_QGEMM_TRACE
 __device__ __forceinline__ void trace(const QGemmArgs& p, int idx, long long t0) {
-    if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1792) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1856) {
         long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         p.y[(size_t)(idx / 32) * p.N + (idx % 32)] = (float)(t - t0);   // inside this CTA's tile
     }
@@ -80,9 +86,9 @@ struct QGemmCfg {
     // NGRP: TMEM ring of 4-block groups (4 * BN columns each) within 512 columns
     static constexpr int NPW = 4 * CG, CW = BN / CG;
     // TMEM ring of 4-block groups (4 * BN columns each), at most 256 columns so two CTAs
-    // can share an SM; shared-memory ring as deep as ~200 KB allows (stage size grows with BN)
+    // can share an SM
     static constexpr int NGRP = 256 / (4 * BN) >= 2 ? 2 : 1;
-    static constexpr int NST = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;
+    static constexpr int NST = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;   // ~190 KB ring: deeper measured faster
     static constexpr int THREADS = 64 + 32 * NPW;
     static constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = BN * 128, DX_BYTES = 128 * 16,
                               DW_BYTES = 16 * BN;
@@ -116,6 +122,7 @@ qgemm_kernel(const QGemmArgs p) {
     long long t_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
 #endif
     const int nkc = p.K / 128;
+    const int kz = blockIdx.z, kc0 = kz * p.cps, nloc = max(0, min(nkc, kc0 + p.cps) - kc0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NST; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + C::NPW); }
@@ -137,11 +144,11 @@ qgemm_kernel(const QGemmArgs p) {
             const uint32_t tx_bytes = C::TX_BYTES - (128 - rows8) * (128 + 16 + (Q4K ? 16 : 0));
             int last_it[NST];
             for (int s = 0; s < NST; s++) last_it[s] = -1;
-            for (int kc = 0; kc < nkc; kc++) {
-                const int s = kc % NST, it = kc / NST;
+            for (int i = 0; i < nloc; i++) {
+                const int kc = kc0 + i, s = i % NST, it = i / NST;
                 if (!mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1)) break;
                 uint8_t* st = smem + s * C::STAGE;
-                TRACE(kc);
+                TRACE(i);
                 mbar_arrive_expect_tx(&full[s], tx_bytes);
                 bulk_g2s(st, p.aq + ((size_t)kc * p.Mpad + m0) * 128, rows8 * 128, &full[s]);
                 bulk_g2s(st + C::OFF_B, p.wq + ((size_t)kc * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
@@ -168,7 +175,7 @@ qgemm_kernel(const QGemmArgs p) {
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_make(2, 1, Q4K ? 0 : 1, 128, BN);
-            for (int kc = 0; kc < nkc; kc++) {
+            for (int kc = 0; kc < nloc; kc++) {   // local chunk index
                 const int s = kc % NST, it = kc / NST, g = kc % NGRP, ug = kc / NGRP;
                 if (!mbar_wait(&full[s], it & 1, abort_flag, 2)) break;
                 if (!mbar_wait(&tempty[g], (ug & 1) ^ 1, abort_flag, 3)) break;
@@ -197,7 +204,7 @@ qgemm_kernel(const QGemmArgs p) {
         // per batch); BPC batches per 4-block chunk.  (Overlapping batch t+1's loads with batch
         // t's math measured slower: it forces smaller batches, and the waits dominate.)
         constexpr int BPC = 4 / BATCH;
-        const int nbatch = nkc * BPC;
+        const int nbatch = nloc * BPC;   // chunk indices below are local to this K split
         bool ok = true;
         // wait for a chunk's operands + dot tiles, then issue the batch's TMEM loads
         auto issue = [&](uint32_t (&I)[BATCH][CW], int t) {
@@ -296,6 +303,46 @@ qgemm_kernel(const QGemmArgs p) {
 #else
         constexpr bool keep_stamps = false;
 #endif
+        if (p.nsplit > 1) {
+            // split-K: publish this split's partial, then the last CTA of the tile sums all
+            // partials in split order (deterministic) and runs the epilogue below
+            const bool vecp = (p.N % 4) == 0;
+            if (m < p.M && !*abort_flag) {
+                float* dst = p.part + ((size_t)kz * p.M + m) * p.N;
+#pragma unroll
+                for (int c = 0; c < CW; c += 4) {
+                    const int n = n0 + c0 + c;
+                    if (n >= p.N) break;
+                    if (vecp) *reinterpret_cast<float4*>(dst + n) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+                    else for (int i = 0; i < 4 && n + i < p.N; i++) dst[n + i] = acc[c + i];
+                }
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, %0;" ::"r"(C::NPW * 32) : "memory");
+            volatile int* last_flag = (volatile int*)(tmem_slot + 2);
+            int* ctr = p.counters + blockIdx.y * gridDim.x + blockIdx.x;
+            if (threadIdx.x == 64) {
+                const int prev = atomicAdd(ctr, 1);
+                *last_flag = prev == p.nsplit - 1;
+                if (prev == p.nsplit - 1) *ctr = 0;   // every split has arrived: re-arm for the next call
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(C::NPW * 32) : "memory");
+            if (!*last_flag) goto done;
+            __threadfence();
+            if (m < p.M) {
+#pragma unroll
+                for (int c = 0; c < CW; c++) {
+                    const int n = n0 + c0 + c;
+                    if (n >= p.N) break;
+                    float v = 0.0f;
+                    for (int z = 0; z < p.nsplit; z++) {
+                        const float pz = z == kz ? acc[c] : __ldcg(p.part + ((size_t)z * p.M + m) * p.N + n);
+                        v = z == 0 ? pz : __fadd_rn(v, pz);
+                    }
+                    acc[c] = v;
+                }
+            }
+        }
         if (m < p.M && !*abort_flag && !keep_stamps) {
             const int nbase = n0 + c0;
             const bool vec = (p.N % 4) == 0;
@@ -333,6 +380,8 @@ qgemm_kernel(const QGemmArgs p) {
         }
     }
 
+    if (warp >= 2 && lane == 0) TRACE(1792 + warp);
+done:
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -365,7 +414,7 @@ template <int BN, int CG, bool Q4K>
 static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
     ++g_launch_count;
     using C = QGemmCfg<BN, CG, Q4K>;
-    dim3 grid((a.N + BN - 1) / BN, (a.M + 127) / 128);
+    dim3 grid((a.N + BN - 1) / BN, (a.M + 127) / 128, a.nsplit);
     qgemm_kernel<BN, CG, Q4K><<<grid, C::THREADS, C::SMEM, st>>>(a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
@@ -388,11 +437,24 @@ static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
 }
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
-                 const float* resid, float* y, cudaStream_t st) {
+                 const float* resid, float* y, cudaStream_t st, const SplitK* sk) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
-    QGemmArgs p{a.q, a.d, a.c, a.Mpad, w.q, w.sa, w.sb, w.Npad, M, w.N, w.K, bias, resid, y, act};
     int bn, cg;
     pick_cfg(M, w.N, w.K, bn, cg);
+    // Split-K (MGC_QGEMM_SPLITK=<n>) is off by default: on the config-1 shapes it measured
+    // slower than one CTA per tile (ncu: attn_o 11 -> 26 us with 3 splits, ffn_down 22 -> 38 us
+    // with 4), so the library only splits when asked.
+    const int nkc = w.K / 128, tiles = ((w.N + bn - 1) / bn) * ((M + 127) / 128);
+    int nsplit = 1;
+    if (sk && sk->part && sk->counters) {
+        if (const char* e = std::getenv("MGC_QGEMM_SPLITK")) nsplit = std::max(1, std::atoi(e));
+        nsplit = std::min(nsplit, nkc);
+        if ((size_t)nsplit * M * w.N > sk->part_floats || tiles > sk->n_counters) nsplit = 1;
+    }
+    const int cps = (nkc + nsplit - 1) / nsplit;
+    nsplit = (nkc + cps - 1) / cps;   // no empty split
+    QGemmArgs p{a.q, a.d, a.c, a.Mpad, w.q, w.sa, w.sb, w.Npad, M, w.N, w.K, bias, resid, y, act,
+                sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps};
     const bool q4 = w.wtype == 12;
 #define X(BN, CG) \
     if (bn == BN && cg == CG) return q4 ? run_qgemm<BN, CG, true>(p, st) : run_qgemm<BN, CG, false>(p, st);

@@ -204,7 +204,19 @@ ActQ alloc_actq(int Mpad, int K) {
 void free_actq(ActQ& a) { cudaFree(a.q); cudaFree(a.d); cudaFree(a.c); a = ActQ{}; }
 
 // Library scratch used by the standalone mgc_qgemm entry point (grown on demand, per device).
-struct Scratch { ActQ a; int Mpad = 0, K = 0; float* attn = nullptr; size_t attn_n = 0; };
+struct Scratch { ActQ a; int Mpad = 0, K = 0, N = 0; float* attn = nullptr; size_t attn_n = 0; SplitK sk; };
+
+// Split-K scratch for up to 4 splits of an [rows][N] output.
+SplitK alloc_splitk(int Mpad, int N) {
+    SplitK k;
+    k.part_floats = (size_t)4 * Mpad * N;
+    k.part = dalloc<float>(k.part_floats);
+    k.n_counters = ((N + 31) / 32) * (Mpad / 128);
+    k.counters = dalloc<int>(k.n_counters);
+    CK(cudaMemset(k.counters, 0, sizeof(int) * k.n_counters));
+    return k;
+}
+void free_splitk(SplitK& k) { cudaFree(k.part); cudaFree(k.counters); k = SplitK{}; }
 std::map<int, Scratch> g_scratch;
 std::mutex g_scratch_mu;
 
@@ -284,15 +296,18 @@ int mgc_qgemm(const mgc_qweight* wq, const float* x, int M, const float* bias, i
         std::lock_guard<std::mutex> lk(g_scratch_mu);
         Scratch& s = g_scratch[dev];
         const int Mpad = round_up(M, 128);
-        if (s.Mpad < Mpad || s.K < w.K) {
+        if (s.Mpad < Mpad || s.K < w.K || s.N < w.N) {
             CK(cudaStreamSynchronize(st));
             free_actq(s.a);
+            free_splitk(s.sk);
             s.Mpad = std::max(s.Mpad, Mpad);
             s.K = std::max(s.K, w.K);
+            s.N = std::max(s.N, w.N);
             s.a = alloc_actq(s.Mpad, s.K);
+            s.sk = alloc_splitk(s.Mpad, s.N);
         }
         launch_quant_act_tiled(x, M, w.K, s.a, w.wtype == 12, st);
-        if (launch_qgemm(w, s.a, M, bias, act, resid, y, st) != 0)
+        if (launch_qgemm(w, s.a, M, bias, act, resid, y, st, &s.sk) != 0)
             throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
     });
 }
@@ -374,6 +389,7 @@ struct mgc_runtime {
     float *x = nullptr, *t = nullptr, *qkv = nullptr, *att = nullptr, *ff = nullptr, *logits = nullptr;
     int32_t* tokens = nullptr;
     ActQ aE, aF;
+    SplitK sk;                       // split-K partials of the quantized GEMMs
     float* attn_scratch = nullptr;   // key-split partials of the attention
     size_t attn_scratch_n = 0;
     // host staging (pinned)
@@ -417,7 +433,7 @@ QWeight load_linear(const Gguf& g, const std::vector<std::string>& names, int K,
 void linear(mgc_runtime* rt, const QWeight& w, const float* xin, const ActQ& a, int M, const float* bias,
             int act, const float* resid, float* y) {
     if (w.wtype == 0) { launch_gemm_f32(w.f32, xin, M, w.N, w.K, bias, act, resid, y, rt->st); return; }
-    if (launch_qgemm(w, a, M, bias, act, resid, y, rt->st) != 0)
+    if (launch_qgemm(w, a, M, bias, act, resid, y, rt->st, &rt->sk) != 0)
         throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
 }
 
@@ -530,6 +546,7 @@ void destroy_runtime(mgc_runtime* rt) {
     for (float* p : rt->f32_allocs) cudaFree(p);
     cudaFree(rt->x); cudaFree(rt->t); cudaFree(rt->qkv); cudaFree(rt->att); cudaFree(rt->ff);
     cudaFree(rt->logits); cudaFree(rt->tokens); cudaFree(rt->attn_scratch);
+    free_splitk(rt->sk);
     free_actq(rt->aE); free_actq(rt->aF);
     if (rt->h_tokens) cudaFreeHost(rt->h_tokens);
     if (rt->h_logits) cudaFreeHost(rt->h_logits);
@@ -613,6 +630,7 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->tokens = dalloc<int32_t>(R);
         rt->aE = alloc_actq(rt->Mpad, E);
         rt->aF = alloc_actq(rt->Mpad, F);
+        rt->sk = alloc_splitk(rt->Mpad, std::max(3 * E, F));
         rt->attn_scratch_n = attn_scratch_floats(1, rt->Mpad, rt->n_head);
         rt->attn_scratch = dalloc<float>(rt->attn_scratch_n);
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));

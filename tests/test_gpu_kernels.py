@@ -42,11 +42,23 @@ def test_quantize_act_bit_exact(dev, oracle_mod, M, K):
 SHAPES = [(768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 2025)]
 
 
+def close_to_oracle(y, ref):
+    """Split-K sums per-split partials in split order instead of one chain: a few ulp of the
+    output scale."""
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5 * float(np.abs(ref).max()))
+
+
 @pytest.mark.parametrize("wtype", [8, 12])
 @pytest.mark.parametrize("M", [1, 31, 257])
 @pytest.mark.parametrize("K,N", SHAPES)
-def test_qgemm_bit_exact(dev, oracle_mod, wtype, M, K, N):
+@pytest.mark.parametrize("split", ["1", "auto"])
+def test_qgemm_vs_oracle(dev, oracle_mod, monkeypatch, wtype, M, K, N, split):
+    """split "1": one K chain per output, bit-exact; "auto": the library's split-K choice."""
     from edge_maskgit_b200 import runtime as rt
+    if split == "1":
+        monkeypatch.setenv("MGC_QGEMM_SPLITK", "1")
+    else:
+        monkeypatch.delenv("MGC_QGEMM_SPLITK", raising=False)
     rng = np.random.default_rng(0)
     x = rng.standard_normal((M, K), dtype=np.float32)
     w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
@@ -54,12 +66,15 @@ def test_qgemm_bit_exact(dev, oracle_mod, wtype, M, K, N):
     qw = rt.QWeight(wtype, blocks, N, K)
     y = qw.qgemm(_t(x, dev)).cpu().numpy()
     ref = oracle_mod.qgemm(wtype, blocks, x, N)
-    assert np.array_equal(y, ref), f"max diff {np.abs(y - ref).max()}"
+    if split == "1":
+        assert np.array_equal(y, ref), f"max diff {np.abs(y - ref).max()}"
+    else:
+        close_to_oracle(y, ref)
 
 
 @pytest.mark.parametrize("wtype", [8, 12])
 @pytest.mark.parametrize("act", [0, 1])
-def test_qgemm_epilogue(dev, oracle_mod, wtype, act):
+def test_qgemm_epilogue(dev, oracle_mod, monkeypatch, wtype, act):
     from edge_maskgit_b200 import runtime as rt
     rng = np.random.default_rng(5)
     M, K, N = 257, 768, 3072
@@ -69,12 +84,22 @@ def test_qgemm_epilogue(dev, oracle_mod, wtype, act):
     r = rng.standard_normal((M, N), dtype=np.float32)
     blocks = rt.pack_q8_0(w) if wtype == 8 else rt.pack_q4_k(w)
     qw = rt.QWeight(wtype, blocks, N, K)
+    monkeypatch.setenv("MGC_QGEMM_SPLITK", "1")
     y = qw.qgemm(_t(x, dev), bias=_t(b, dev), act=act, resid=_t(r, dev)).cpu().numpy()
     ref = oracle_mod.qgemm(wtype, blocks, x, N, bias=b, act=act, resid=r)
     if act == 0:
         assert np.array_equal(y, ref)
     else:
         np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-6)
+    monkeypatch.delenv("MGC_QGEMM_SPLITK")
+    # split-K with the fused epilogue (768 -> 3072 at M=257 is split by default only for
+    # smaller N; force it)
+    monkeypatch.setenv("MGC_QGEMM_SPLITK", "3")
+    y = qw.qgemm(_t(x, dev), bias=_t(b, dev), act=act, resid=_t(r, dev)).cpu().numpy()
+    close_to_oracle(y, ref)
+    # the arrival counters re-arm: a second split call gives the same result
+    y2 = qw.qgemm(_t(x, dev), bias=_t(b, dev), act=act, resid=_t(r, dev)).cpu().numpy()
+    assert np.array_equal(y, y2)
 
 
 def test_qgemm_large_m(dev, oracle_mod):
