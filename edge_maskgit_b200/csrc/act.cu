@@ -33,8 +33,10 @@ __device__ __forceinline__ void quant_block32(const float* v, int8_t* q, float& 
 
 // thread per (row, 32-block)
 template <bool TILED>
-__global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, int8_t* qx, float* dx,
-                                 float* cx, int32_t* sumx, int Mpad) {
+__global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, ActQ a, int want_c, int8_t* qx,
+                                 float* dx, int32_t* sumx) {
+    griddep_wait();
+    griddep_launch();
     const int nb = K / 32;
     const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (long)M * nb) return;
@@ -51,12 +53,10 @@ __global__ void quant_act_kernel(const float* __restrict__ x, int M, int K, int8
     quant_block32(v, q, d, s);
     if (TILED) {
         const int kc = b >> 2, j = b & 3;
-        int8_t* row = qx + ((size_t)kc * Mpad + m) * 128;
-        const uint32_t c0 = (uint32_t)(2 * j) ^ (uint32_t)(m & 7), c1 = (uint32_t)(2 * j + 1) ^ (uint32_t)(m & 7);
-        *reinterpret_cast<int4*>(row + c0 * 16) = *reinterpret_cast<const int4*>(q);
-        *reinterpret_cast<int4*>(row + c1 * 16) = *reinterpret_cast<const int4*>(q + 16);
-        dx[((size_t)kc * Mpad + m) * 4 + j] = d;
-        if (cx) cx[((size_t)kc * Mpad + m) * 4 + j] = __fmul_rn(d, (float)s);
+        *reinterpret_cast<int4*>(a.q + act_code(a, kc, m, j * 32)) = *reinterpret_cast<const int4*>(q);
+        *reinterpret_cast<int4*>(a.q + act_code(a, kc, m, j * 32 + 16)) = *reinterpret_cast<const int4*>(q + 16);
+        act_dx(a, kc, m)[j] = d;
+        if (want_c) act_cx(a, kc, m)[j] = __fmul_rn(d, (float)s);
     } else {
         int4* dst = reinterpret_cast<int4*>(qx + (size_t)m * K + b * 32);
         dst[0] = *reinterpret_cast<const int4*>(q);
@@ -70,7 +70,7 @@ void launch_quant_act_plain(const float* x, int M, int K, int8_t* qx, float* dx,
                             cudaStream_t st) {
     ++g_launch_count;
     const long n = (long)M * (K / 32);
-    quant_act_kernel<false><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, M, K, qx, dx, nullptr, sumx, 0);
+    launch_k(quant_act_kernel<false>, (unsigned)((n + 255) / 256), 256, 0, st, x, M, K, ActQ{}, 0, qx, dx, sumx);
 }
 
 // ---------------------------------------------------------------- LayerNorm (+ quantizer)
@@ -119,15 +119,15 @@ __device__ __forceinline__ void quant_row_warp(const float (&v)[NV], int m, cons
         const int q = (int)roundf(__fmul_rn(v[b], id));
         const int kc = b >> 2, j = b & 3;
         const uint32_t kb = (uint32_t)(j * 32 + lane);
-        a.q[((size_t)kc * a.Mpad + m) * 128 + sw128_off(m & 7, kb) - (uint32_t)(m & 7) * 128u] = (int8_t)q;
+        a.q[act_code(a, kc, m, kb)] = (int8_t)q;
         int s = q;
         if (want_c) {
 #pragma unroll
             for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
         }
         if (lane == 0) {
-            a.d[((size_t)kc * a.Mpad + m) * 4 + j] = d;
-            if (want_c) a.c[((size_t)kc * a.Mpad + m) * 4 + j] = __fmul_rn(d, (float)s);
+            act_dx(a, kc, m)[j] = d;
+            if (want_c) act_cx(a, kc, m)[j] = __fmul_rn(d, (float)s);
         }
     }
 }
@@ -136,6 +136,8 @@ template <int NV>
 __global__ void ln_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                           const float* __restrict__ beta, int rows, float eps, float* y, ActQ a,
                           int quant, int want_c) {
+    griddep_wait();
+    griddep_launch();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     constexpr int D = NV * 32;
@@ -155,6 +157,8 @@ __global__ void embed_ln_kernel(const float* __restrict__ tok, int vocab, const 
                                 const int32_t* __restrict__ tokens, int S, int rows,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 float eps, float* y, ActQ a, int do_ln, int quant, int want_c) {
+    griddep_wait();
+    griddep_launch();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
     constexpr int D = NV * 32;
@@ -201,15 +205,14 @@ __device__ __forceinline__ void quant_chunks(const float (&v)[NC][8], int m, con
         }
         const int b = 8 * i + (lane >> 2), kc = b >> 2, j = b & 3;
         const uint32_t kb = (uint32_t)(j * 32 + (lane & 3) * 8);
-        int8_t* row = a.q + ((size_t)kc * a.Mpad + m) * 128;
-        *reinterpret_cast<uint2*>(row + ((((kb >> 4) ^ (uint32_t)(m & 7)) << 4) | (kb & 15))) = make_uint2(lo, hi);
+        *reinterpret_cast<uint2*>(a.q + act_code(a, kc, m, kb)) = make_uint2(lo, hi);
         if (want_c) {
             sum += __shfl_xor_sync(0xffffffffu, sum, 1);
             sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         }
         if ((lane & 3) == 0) {
-            a.d[((size_t)kc * a.Mpad + m) * 4 + j] = d;
-            if (want_c) a.c[((size_t)kc * a.Mpad + m) * 4 + j] = __fmul_rn(d, (float)sum);
+            act_dx(a, kc, m)[j] = d;
+            if (want_c) act_cx(a, kc, m)[j] = __fmul_rn(d, (float)sum);
         }
     }
 }
@@ -286,6 +289,8 @@ __global__ void __launch_bounds__(128) rows_kernel(const float* __restrict__ x, 
                                                    const int32_t* __restrict__ tokens, int S, int rows,
                                                    const float* __restrict__ gamma, const float* __restrict__ beta,
                                                    float eps, float* y, ActQ a, int quant, int want_c) {
+    griddep_wait();
+    griddep_launch();
     extern __shared__ float stage[];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = blockIdx.x * 4 + w;
@@ -321,7 +326,7 @@ static bool launch_rows(int D, const float* x, const float* tok, int vocab, cons
     const size_t sm = MODE == 2 ? 0 : (size_t)4 * D * sizeof(float);
 #define MGC_ROWS(NC)                                                                                       \
     case NC:                                                                                               \
-        rows_kernel<NC, MODE><<<blocks, 128, sm, st>>>(x, tok, vocab, pos, tokens, S, rows, gamma, beta, eps, y, \
+        launch_k(rows_kernel<NC, MODE>, blocks, 128, sm, st, x, tok, vocab, pos, tokens, S, rows, gamma, beta, eps, y, \
                                                        aa, a != nullptr, want_c);                          \
         return true;
     switch (D % 256 == 0 ? D / 256 : 0) {
@@ -352,7 +357,7 @@ void launch_ln(const float* x, const float* gamma, const float* beta, int rows, 
         return;
     const ActQ aa = a ? *a : ActQ{};
     const unsigned blocks = (unsigned)((rows + 7) / 8);
-    MGC_NV_SWITCH(D, (ln_kernel<NV><<<blocks, 256, 0, st>>>(x, gamma, beta, rows, eps, y, aa, a != nullptr,
+    MGC_NV_SWITCH(D, (launch_k(ln_kernel<NV>, blocks, 256, 0, st, x, gamma, beta, rows, eps, y, aa, a != nullptr,
                                                             want_c)));
 }
 
@@ -361,7 +366,7 @@ void launch_embed(const float* tok, int vocab, const float* pos, int E, const in
     ++g_launch_count;
     const int rows = B * S;
     const unsigned blocks = (unsigned)((rows + 7) / 8);
-    MGC_NV_SWITCH(E, (embed_ln_kernel<NV><<<blocks, 256, 0, st>>>(tok, vocab, pos, tokens, S, rows, nullptr,
+    MGC_NV_SWITCH(E, (launch_k(embed_ln_kernel<NV>, blocks, 256, 0, st, tok, vocab, pos, tokens, S, rows, nullptr,
                                                                   nullptr, 0.0f, y, ActQ{}, 0, 0, 0)));
 }
 
@@ -374,7 +379,7 @@ void launch_embed_ln(const float* tok, int vocab, const float* pos, int E, const
     const int rows = B * S;
     const ActQ aa = a ? *a : ActQ{};
     const unsigned blocks = (unsigned)((rows + 7) / 8);
-    MGC_NV_SWITCH(E, (embed_ln_kernel<NV><<<blocks, 256, 0, st>>>(tok, vocab, pos, tokens, S, rows, gamma,
+    MGC_NV_SWITCH(E, (launch_k(embed_ln_kernel<NV>, blocks, 256, 0, st, tok, vocab, pos, tokens, S, rows, gamma,
                                                                   beta, eps, y, aa, 1, a != nullptr, want_c)));
 }
 
@@ -383,8 +388,8 @@ void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool wa
     if (launch_rows<2>(K, x, nullptr, 0, nullptr, nullptr, 1, M, nullptr, nullptr, 0.0f, nullptr, &a, want_c, st))
         return;
     const long n = (long)M * (K / 32);
-    quant_act_kernel<true><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, M, K, a.q, a.d,
-                                                                         want_c ? a.c : nullptr, nullptr, a.Mpad);
+    launch_k(quant_act_kernel<true>, (unsigned)((n + 255) / 256), 256, 0, st, x, M, K, a, want_c ? 1 : 0,
+             (int8_t*)nullptr, (float*)nullptr, (int32_t*)nullptr);
 }
 
 }  // namespace mgc

@@ -67,6 +67,8 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
         mbar_fence_init();
     }
     if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
+    griddep_wait();   // qkv comes from the preceding kernel
+    griddep_launch();
 
     // Q tile -> f16, swizzled
     {
@@ -266,6 +268,8 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
 // Merge the key-range partials: m = max m_s, l = sum l_s e^(m_s - m), o = sum o_s e^(m_s - m) / l.
 __global__ void attn_combine(const float* __restrict__ opart, const float* __restrict__ mlpart, int nsplit,
                              int R, int H, float* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;   // (row, head, 4-dim group)
     constexpr int G = fa::D / 4;
     if (i >= R * H * G) return;
@@ -322,9 +326,9 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     float* opart = scratch;
     float* mlpart = scratch ? scratch + (size_t)nsplit * R * H * fa::D : nullptr;
     dim3 grid(qt, H, B * nsplit);
-    flash_attn_tc<<<grid, 128, fa::SMEM, st>>>(qkv, S, H, scale, out, nsplit, tiles_per, opart, mlpart);
+    launch_k(flash_attn_tc, grid, 128, fa::SMEM, st, qkv, S, H, scale, out, nsplit, tiles_per, opart, mlpart);
     g_launch_count += nsplit > 1 ? 2 : 1;
-    if (nsplit > 1) attn_combine<<<(R * H * (fa::D / 4) + 255) / 256, 256, 0, st>>>(opart, mlpart, nsplit, R, H, out);
+    if (nsplit > 1) launch_k(attn_combine, (R * H * (fa::D / 4) + 255) / 256, 256, 0, st, opart, mlpart, nsplit, R, H, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

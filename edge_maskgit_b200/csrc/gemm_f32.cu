@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
                                                        int M, int N, int K, const float* __restrict__ bias,
                                                        int act, const float* __restrict__ resid,
                                                        float* __restrict__ y) {
+    griddep_wait();
+    griddep_launch();
     __shared__ __align__(16) float As[GF_BK][GF_BM + 4];   // x slab, As[k][m]
     __shared__ __align__(16) float Bs[GF_BK][GF_BN + 4];   // w slab, Bs[k][n]
     const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;   // 16 x 16 threads, 4 x 4 each
@@ -89,7 +91,7 @@ void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const 
                      const float* resid, float* y, cudaStream_t st) {
     ++g_launch_count;
     dim3 grid((N + GF_BN - 1) / GF_BN, (M + GF_BM - 1) / GF_BM);
-    gemm_f32_kernel<<<grid, 256, 0, st>>>(w, x, M, N, K, bias, act, resid, y);
+    launch_k(gemm_f32_kernel, grid, 256, 0, st, w, x, M, N, K, bias, act, resid, y);
 }
 
 }  // namespace mgc

@@ -1,41 +1,89 @@
 // kernels.h -- internal launch interface between the runtime and the CUDA kernels.
 //
-// Device layouts (all chosen so every tile a CTA needs is one contiguous, 16-byte aligned
-// run that a single cp.async.bulk can move into shared memory in its MMA layout):
+// Device layouts.  Every operand a qGEMM CTA needs for one 4-block K chunk is one contiguous,
+// 16-byte aligned run that a single cp.async.bulk moves into shared memory already in the
+// tcgen05 128-byte-swizzle layout (three copies per chunk):
 //
-//   ActQ  quantized activation of an [M][K] f32 tensor, rows padded to Mpad (multiple of 128)
-//     q : int8 [K/128][Mpad][128]  -- row r's 128-byte K-chunk, 16-byte groups XOR-swizzled
-//                                     by (r % 8) (the tcgen05 128-byte swizzle)
-//     d : f32  [K/128][Mpad][4]    -- dx of the 4 32-blocks of each chunk
-//     c : f32  [K/128][Mpad][4]    -- dx * sum(qx) per block (only for Q4_K consumers)
+//   ActQ  quantized activation of an [M][K] f32 tensor, rows padded to Mpad (multiple of 128),
+//         as tiles of (128-column K chunk kc, 128-row m-tile mt), tile (kc, mt) at byte
+//         ((kc * Mpad/128) + mt) * kActTile:
+//     [0, 16384)       int8 codes, row r's 128 bytes at r*128 with 16-byte groups XOR-swizzled
+//                      by (r % 8)
+//     [16384, 18432)   dx  f32 [128 rows][4 blocks]
+//     [18432, 20480)   dx * sum(qx) f32 [128][4] (written only for Q4_K consumers)
 //
 //   QWeight  quantized [N][K] weight, rows padded to Npad (multiple of 128)
-//     q  : int8 (Q8_0) or u8 nibble values 0..15 (Q4_K), [K/128][Npad][128], same swizzle
-//     sa : f32 [K/32][Npad]   Q8_0: d (fp16 -> f32);  Q4_K: scl = d * sc_j
-//     sb : f32 [K/32][Npad]   Q4_K only: mnl = dmin * m_j
+//     q : int8 (Q8_0) or u8 nibble values 0..15 (Q4_K), [K/128][Npad][128], same swizzle
+//     s : f32 scale tiles [K/128][Npad/4][T][4 blocks][4 columns], T = 1 for Q8_0 (d) and
+//         2 for Q4_K (scl = d*sc_j, then mnl = dmin*m_j) -- a BN-column tile is BN*4*T floats
 //     f32: for wtype 0 the weight itself, [N][K] row-major
 #pragma once
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 
 namespace mgc {
 
+constexpr int kActTile = 20480;
+
 struct ActQ {
-    int8_t* q = nullptr;
-    float* d = nullptr;
-    float* c = nullptr;
+    int8_t* q = nullptr;   // tiles as above; Mpad * K * 5/4 bytes
     int Mpad = 0;
 };
+
+__host__ __device__ inline size_t act_tile(const ActQ& a, int kc, int m) {
+    return ((size_t)kc * (a.Mpad / 128) + (m >> 7)) * kActTile;
+}
+// byte offset of code k (0..127 within chunk kc) of row m
+__host__ __device__ inline size_t act_code(const ActQ& a, int kc, int m, uint32_t k) {
+    const uint32_t r = m & 127;
+    return act_tile(a, kc, m) + r * 128u + ((((k >> 4) ^ (r & 7u)) << 4) | (k & 15u));
+}
+__host__ __device__ inline float* act_dx(const ActQ& a, int kc, int m) {   // 4 floats (blocks of kc)
+    return reinterpret_cast<float*>(a.q + act_tile(a, kc, m) + 16384 + (m & 127) * 16);
+}
+__host__ __device__ inline float* act_cx(const ActQ& a, int kc, int m) {
+    return reinterpret_cast<float*>(a.q + act_tile(a, kc, m) + 18432 + (m & 127) * 16);
+}
 
 struct QWeight {
     int wtype = 0, N = 0, K = 0, Npad = 0;
     int8_t* q = nullptr;
-    float* sa = nullptr;
-    float* sb = nullptr;
+    float* s = nullptr;
     float* f32 = nullptr;
 };
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Launch with programmatic dependent launch (the kernel overlaps its prologue with the tail of
+// the previous kernel in the stream; every kernel here calls griddep_wait() before reading
+// inputs).  Off unless MGC_PDL=1: on the config-1 step it measured slower (408 vs 428 steps/s),
+// the step being bound by kernel bodies rather than launch gaps.
+inline bool pdl_enabled() {
+    static const bool on = [] { const char* e = std::getenv("MGC_PDL"); return e && e[0] == '1'; }();
+    return on;
+}
+// Every kernel runs with the max-shared carveout so consecutive kernels never reconfigure the
+// SM's L1 / shared-memory split (set once per kernel and device, on its first launch).
+void set_max_shared_carveout(const void* kernel);
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+    set_max_shared_carveout((const void*)kernel);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Kernels this library has launched (host-side count, for the runtime's launch report).
 extern int g_launch_count;

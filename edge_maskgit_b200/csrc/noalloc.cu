@@ -16,14 +16,13 @@
 
 namespace {
 
-// Fixed scratch for the quantized activation: int8 codes [K/128][Mpad][128], then the
-// per-block scales and the Q4_K correction terms, f32 [K/128][Mpad][4] each.
-// MGC_NOALLOC_MAX_ELEMS bounds Mpad*K (Mpad = M rounded up to 128).  Every GPU that loads
-// the library holds these bytes until the process exits.
+// Fixed scratch for the quantized activation, in the tile layout of kernels.h: per 128 x 128
+// tile the int8 codes, then the per-block scales and the Q4_K correction terms (20480 bytes
+// per 16384 codes).  MGC_NOALLOC_MAX_ELEMS bounds Mpad*K (Mpad = M rounded up to 128).
+// Every GPU that loads the library holds these bytes until the process exits.
 constexpr size_t kMaxElems = MGC_NOALLOC_MAX_ELEMS;
-constexpr size_t kQBytes = kMaxElems;                       // int8 codes
-constexpr size_t kSBytes = kMaxElems / 32 * sizeof(float);  // one f32 per 32 codes
-static __device__ __align__(256) unsigned char g_noalloc_scratch[kQBytes + 2 * kSBytes];
+constexpr size_t kScratchBytes = kMaxElems / 16384 * mgc::kActTile;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 void* g_scratch_ptr[kMaxDevices] = {};
@@ -66,12 +65,9 @@ extern "C" int mgc_qgemm_noalloc(const mgc_qweight* wq, const float* x_dev, int 
         }
         base = g_scratch_ptr[dev];
     }
-    unsigned char* b = (unsigned char*)base;
     mgc::ActQ a;
     a.Mpad = Mpad;
-    a.q = (int8_t*)b;
-    a.d = (float*)(b + kQBytes);
-    a.c = (float*)(b + kQBytes + kSBytes);
+    a.q = (int8_t*)base;
     cudaStream_t st = (cudaStream_t)stream;
     mgc::launch_quant_act_tiled(x_dev, M, w.K, a, w.wtype == MGC_Q4_K, st);
     if (cudaPeekAtLastError() != cudaSuccess ||

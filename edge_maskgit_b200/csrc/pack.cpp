@@ -142,38 +142,37 @@ void dequant(int wtype, const uint8_t* w, int64_t N, int64_t K, float* out) {
     }
 }
 
-// GGUF blocks -> device streaming planes (see kernels.h).  Lossless: the int8 / nibble
-// codes are copied and the scales become exact f32 (fp16 -> f32, d*sc and dmin*m are exact
-// products of an 11-bit and a 6-bit significand).
-void repack(int wtype, const uint8_t* w, int N, int K, int Npad, std::vector<int8_t>& q,
-            std::vector<float>& sa, std::vector<float>& sb) {
-    const int nb = K / 32;
+// GGUF blocks -> device streaming layout (see kernels.h).  Lossless: the int8 / nibble codes
+// are copied and the scales become exact f32 (fp16 -> f32; d*sc and dmin*m are exact products
+// of an 11-bit and a 6-bit significand).
+void repack(int wtype, const uint8_t* w, int N, int K, int Npad, std::vector<int8_t>& q, std::vector<float>& sc) {
+    const int nb = K / 32, T = wtype == 12 ? 2 : 1;
     q.assign((size_t)K * Npad, 0);
-    sa.assign((size_t)nb * Npad, 0.0f);
-    sb.assign(wtype == 12 ? (size_t)nb * Npad : 0, 0.0f);
+    sc.assign((size_t)nb * Npad * T, 0.0f);
     for (int n = 0; n < N; ++n)
         for (int b = 0; b < nb; ++b) {
             int8_t codes[32];
+            const int kc = b >> 2, j = b & 3;
+            float* tile = sc.data() + (((size_t)kc * (Npad / 4) + n / 4) * T) * 16;
             if (wtype == 8) {
                 const uint8_t* blk = w + ((size_t)n * nb + b) * 34;
-                sa[(size_t)b * Npad + n] = rdh(blk);
+                tile[j * 4 + (n & 3)] = rdh(blk);
                 std::memcpy(codes, blk + 2, 32);
             } else {
                 const uint8_t* blk = w + ((size_t)n * (K / 256) + b / 8) * 144;
-                const int j = b & 7;
-                int sc, mn;
-                q4k_get_scale_min(blk + 4, j, &sc, &mn);
-                sa[(size_t)b * Npad + n] = rdh(blk) * (float)sc;
-                sb[(size_t)b * Npad + n] = rdh(blk + 2) * (float)mn;
+                const int sub = b & 7;
+                int s6, m6;
+                q4k_get_scale_min(blk + 4, sub, &s6, &m6);
+                tile[j * 4 + (n & 3)] = rdh(blk) * (float)s6;
+                tile[16 + j * 4 + (n & 3)] = rdh(blk + 2) * (float)m6;
                 for (int i = 0; i < 32; ++i) {
-                    const uint8_t byte = blk[16 + (j >> 1) * 32 + i];
-                    codes[i] = (int8_t)((j & 1) ? (byte >> 4) : (byte & 0xF));
+                    const uint8_t byte = blk[16 + (sub >> 1) * 32 + i];
+                    codes[i] = (int8_t)((sub & 1) ? (byte >> 4) : (byte & 0xF));
                 }
             }
-            const int kc = b >> 2, kin = (b & 3) * 32;
             int8_t* row = q.data() + ((size_t)kc * Npad + n) * 128;
             for (int i = 0; i < 32; ++i) {
-                const int k = kin + i;
+                const int k = j * 32 + i;
                 row[((((k >> 4) ^ (n & 7)) << 4) | (k & 15))] = codes[i];
             }
         }

@@ -10,6 +10,5 @@ void q4k_get_scale_min(const uint8_t* s12, int j, int* sc, int* mn);
 void pack_q8_0(const float* w, int64_t N, int64_t K, uint8_t* out);
 void pack_q4_k(const float* w, int64_t N, int64_t K, uint8_t* out);
 void dequant(int wtype, const uint8_t* w, int64_t N, int64_t K, float* out);
-void repack(int wtype, const uint8_t* w, int N, int K, int Npad, std::vector<int8_t>& q,
-            std::vector<float>& sa, std::vector<float>& sb);
+void repack(int wtype, const uint8_t* w, int N, int K, int Npad, std::vector<int8_t>& q, std::vector<float>& sc);
 }  // namespace mgc

@@ -25,13 +25,20 @@
 #include <cstdlib>
 #include <algorithm>
 
+#ifndef MGC_QGEMM_MINB
+#define MGC_QGEMM_MINB 1     // CTAs per SM the register budget is sized for
+#endif
+#ifndef MGC_QGEMM_IREGS
+#define MGC_QGEMM_IREGS 64   // int32 dot values a promotion thread loads per TMEM batch
+#endif
+
 
 
 namespace mgc {
 
 struct QGemmArgs {
-    const int8_t* aq; const float* adx; const float* acx; int Mpad;
-    const int8_t* wq; const float* wsa; const float* wsb; int Npad;
+    const int8_t* aq; int Mpad;      // activation tiles (kernels.h ActQ)
+    const int8_t* wq; const float* ws; int Npad;   // weight codes / scale tiles
     int M, N, K;
     const float* bias; const float* resid; float* y; int act;
     // split-K: CTA z of gridDim.z handles K chunks [z*cps, (z+1)*cps); partials go to
@@ -71,7 +78,7 @@ __device__ __forceinline__ float act_apply(float v, int a) {
 // tiles, [1280,1792) warp 2 done.
 #ifdef MGC_QGEMM_TRACE
 __device__ __forceinline__ void trace(const QGemmArgs& p, int idx, long long t0) {
-    if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1856) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1888) {
         long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         p.y[(size_t)(idx / 32) * p.N + (idx % 32)] = (float)(t - t0);   // inside this CTA's tile
     }
@@ -88,25 +95,27 @@ struct QGemmCfg {
     // TMEM ring of 4-block groups (4 * BN columns each), at most 256 columns so two CTAs
     // can share an SM
     static constexpr int NGRP = 256 / (4 * BN) >= 2 ? 2 : 1;
+#ifdef MGC_NST
+    static constexpr int NST = MGC_NST;
+#else
     static constexpr int NST = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;   // ~190 KB ring: deeper measured faster
+#endif
     static constexpr int THREADS = 64 + 32 * NPW;
-    static constexpr uint32_t A_BYTES = 128 * 128, B_BYTES = BN * 128, DX_BYTES = 128 * 16,
-                              DW_BYTES = 16 * BN;
-    static constexpr uint32_t OFF_B = A_BYTES, OFF_DX = OFF_B + B_BYTES, OFF_DW = OFF_DX + DX_BYTES,
-                              OFF_MN = OFF_DW + DW_BYTES, OFF_CX = OFF_MN + (Q4K ? DW_BYTES : 0),
-                              STAGE_RAW = OFF_CX + (Q4K ? DX_BYTES : 0),
-                              STAGE = (STAGE_RAW + 1023) & ~1023u;
-    static constexpr uint32_t TX_BYTES = A_BYTES + B_BYTES + DX_BYTES + DW_BYTES +
-                                         (Q4K ? DW_BYTES + DX_BYTES : 0);
+    // stage = [activation tile: codes | dx | (dx*sumx)] [weight codes] [scale tile]
+    static constexpr uint32_t T = Q4K ? 2 : 1;
+    static constexpr uint32_t A_BYTES = Q4K ? 20480 : 18432, B_BYTES = BN * 128, S_BYTES = BN * 16 * T;
+    static constexpr uint32_t OFF_DX = 16384, OFF_CX = 18432, OFF_B = A_BYTES, OFF_S = OFF_B + B_BYTES,
+                              STAGE = (OFF_S + S_BYTES + 1023) & ~1023u;
+    static constexpr uint32_t TX_BYTES = A_BYTES + B_BYTES + S_BYTES;
     static constexpr uint32_t SMEM = 1024 + NST * STAGE + 256;
     static constexpr uint32_t TMEM_COLS = 4 * BN * NGRP;
 };
 
 template <int BN, int CG, bool Q4K>
-__global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K>::THREADS, 1)
+__global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K>::THREADS, MGC_QGEMM_MINB)
 qgemm_kernel(const QGemmArgs p) {
     using C = QGemmCfg<BN, CG, Q4K>;
-    constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= 64 ? 1 : 64 / CW > 4 ? 4 : 64 / CW;
+    constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= MGC_QGEMM_IREGS ? 1 : MGC_QGEMM_IREGS / CW > 4 ? 4 : MGC_QGEMM_IREGS / CW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* full = (uint64_t*)(smem + NST * C::STAGE);
@@ -131,6 +140,8 @@ qgemm_kernel(const QGemmArgs p) {
         mbar_fence_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+    griddep_wait();   // activations / residual come from the preceding kernel
+    griddep_launch();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -138,10 +149,6 @@ qgemm_kernel(const QGemmArgs p) {
 
     if (warp == 0) {
         if (lane == 0) {
-            // a partial last m-tile streams only its valid rows (rounded up to the 8-row
-            // swizzle atom); the MMA rows beyond read stale shared memory and are discarded
-            const uint32_t rows8 = (uint32_t)min(128, (p.M - m0 + 7) & ~7);
-            const uint32_t tx_bytes = C::TX_BYTES - (128 - rows8) * (128 + 16 + (Q4K ? 16 : 0));
             int last_it[NST];
             for (int s = 0; s < NST; s++) last_it[s] = -1;
             for (int i = 0; i < nloc; i++) {
@@ -149,21 +156,11 @@ qgemm_kernel(const QGemmArgs p) {
                 if (!mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1)) break;
                 uint8_t* st = smem + s * C::STAGE;
                 TRACE(i);
-                mbar_arrive_expect_tx(&full[s], tx_bytes);
-                bulk_g2s(st, p.aq + ((size_t)kc * p.Mpad + m0) * 128, rows8 * 128, &full[s]);
+                // three copies per chunk: activation tile (+ its scales), weight codes, weight scales
+                mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+                bulk_g2s(st, p.aq + ((size_t)kc * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES, &full[s]);
                 bulk_g2s(st + C::OFF_B, p.wq + ((size_t)kc * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
-                bulk_g2s(st + C::OFF_DX, p.adx + ((size_t)kc * p.Mpad + m0) * 4, rows8 * 16, &full[s]);
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    bulk_g2s(st + C::OFF_DW + j * BN * 4, p.wsa + (size_t)(kc * 4 + j) * p.Npad + n0,
-                             BN * 4, &full[s]);
-                if constexpr (Q4K) {
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        bulk_g2s(st + C::OFF_MN + j * BN * 4, p.wsb + (size_t)(kc * 4 + j) * p.Npad + n0,
-                                 BN * 4, &full[s]);
-                    bulk_g2s(st + C::OFF_CX, p.acx + ((size_t)kc * p.Mpad + m0) * 4, rows8 * 16, &full[s]);
-                }
+                bulk_g2s(st + C::OFF_S, p.ws + ((size_t)kc * (p.Npad / 4) + n0 / 4) * 16 * C::T, C::S_BYTES, &full[s]);
                 last_it[s] = it;
             }
             if (*abort_flag) {   // let copies already in flight land before the CTA exits
@@ -184,10 +181,13 @@ qgemm_kernel(const QGemmArgs p) {
                 const uint32_t a_base = smem_u32(smem + s * C::STAGE), b_base = a_base + C::OFF_B;
                 // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
 #pragma unroll
-                for (int j = 0; j < 4; j++)
+                for (int j = 0; j < 4; j++) {
                     mma_i8(tmem + (g * 4 + j) * BN, sdesc_sw128(a_base + 32 * j), sdesc_sw128(b_base + 32 * j),
                            idesc, 0);
+                    if (kc < 8) TRACE(1808 + kc * 6 + j);
+                }
                 mma_commit(&tfull[g]);   // the chunk's 4 dot tiles are ready
+                if (kc < 8) TRACE(1808 + kc * 6 + 4);
                 mma_commit(&empty[s]);   // its shared-memory operands may be overwritten
                 TRACE(256 + kc);
             }
@@ -257,10 +257,11 @@ qgemm_kernel(const QGemmArgs p) {
                 for (int jj = 0; jj < BATCH; jj++) {   // blocks in ascending order: b = 4 kc + j
                     const int j = jb * BATCH + jj;
                     const uint64_t dx2 = pack2(dxa[j], dxa[j]);
-                    const float* dw = reinterpret_cast<const float*>(st + C::OFF_DW) + j * BN + c0;
+                    // scale tile: [BN/4 column quads][T][4 blocks][4 columns]
+                    const float* sq = reinterpret_cast<const float*>(st + C::OFF_S) + (c0 / 4) * 16 * C::T + j * 4;
 #pragma unroll
                     for (int c = 0; c < CW; c += 4) {
-                        const float4 w4 = *reinterpret_cast<const float4*>(dw + c);
+                        const float4 w4 = *reinterpret_cast<const float4*>(sq + (c / 4) * 16 * C::T);
                         // exact int32 -> f32: bits(v + 0x4B400000) = 1.5*2^23 + v, minus 1.5*2^23
                         const uint64_t f01 = add2(pack2(__uint_as_float(I[jj][c] + 0x4B400000u),
                                                         __uint_as_float(I[jj][c + 1] + 0x4B400000u)), kMagicNeg2);
@@ -271,10 +272,9 @@ qgemm_kernel(const QGemmArgs p) {
                     }
                     if constexpr (Q4K) {
                         const uint64_t cx2 = pack2(cxa[j], cxa[j]);
-                        const float* mn = reinterpret_cast<const float*>(st + C::OFF_MN) + j * BN + c0;
 #pragma unroll
                         for (int c = 0; c < CW; c += 4) {
-                            const float4 n4 = *reinterpret_cast<const float4*>(mn + c);
+                            const float4 n4 = *reinterpret_cast<const float4*>(sq + (c / 4) * 16 * C::T + 16);
                             acc2[c / 2] = fma2(pack2(-n4.x, -n4.y), cx2, acc2[c / 2]);
                             acc2[c / 2 + 1] = fma2(pack2(-n4.z, -n4.w), cx2, acc2[c / 2 + 1]);
                         }
@@ -299,7 +299,7 @@ qgemm_kernel(const QGemmArgs p) {
 #pragma unroll
         for (int c = 0; c < CW / 2; c++) unpack2(acc2[c], acc[2 * c], acc[2 * c + 1]);
 #ifdef MGC_QGEMM_TRACE
-        const bool keep_stamps = blockIdx.x == 0 && blockIdx.y == 0;   // trace build: no stores
+        const bool keep_stamps = true;   // trace build: no output stores
 #else
         constexpr bool keep_stamps = false;
 #endif
@@ -381,6 +381,13 @@ qgemm_kernel(const QGemmArgs p) {
     }
 
     if (warp >= 2 && lane == 0) TRACE(1792 + warp);
+#ifdef MGC_QGEMM_TRACE
+    if (threadIdx.x == 64 && !(blockIdx.x == 0 && blockIdx.y == 0)) {   // per-CTA [start, end] stamps (low 32 bits)
+        long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        p.y[(size_t)m0 * p.N + n0] = __int_as_float((int)(t_start & 0x7fffffff));
+        p.y[(size_t)m0 * p.N + n0 + 1] = __int_as_float((int)(t & 0x7fffffff));
+    }
+#endif
 done:
     tc_fence_before();
     __syncthreads();
@@ -415,7 +422,7 @@ static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
     ++g_launch_count;
     using C = QGemmCfg<BN, CG, Q4K>;
     dim3 grid((a.N + BN - 1) / BN, (a.M + 127) / 128, a.nsplit);
-    qgemm_kernel<BN, CG, Q4K><<<grid, C::THREADS, C::SMEM, st>>>(a);
+    launch_k(qgemm_kernel<BN, CG, Q4K>, grid, C::THREADS, C::SMEM, st, a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -431,7 +438,8 @@ static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
     (void)K;
     // measured (ncu, cold L2) over the config-2 sweep: 32 columns x 2 warp groups wins at
     // M <= ~512, 64 x 2 above
-    bn = M <= 512 ? 32 : 64;
+    const int mt = (M + 127) / 128;
+    bn = (M <= 512 && (long)mt * ((N + 31) / 32) <= 148 * MGC_QGEMM_MINB) ? 32 : 64;
     cg = 2;
     (void)N;
 }
@@ -453,7 +461,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     }
     const int cps = (nkc + nsplit - 1) / nsplit;
     nsplit = (nkc + cps - 1) / cps;   // no empty split
-    QGemmArgs p{a.q, a.d, a.c, a.Mpad, w.q, w.sa, w.sb, w.Npad, M, w.N, w.K, bias, resid, y, act,
+    QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
                 sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps};
     const bool q4 = w.wtype == 12;
 #define X(BN, CG) \

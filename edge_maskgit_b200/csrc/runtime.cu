@@ -15,6 +15,7 @@
 #include <mutex>
 #include <memory>
 #include <random>
+#include <set>
 #include <stdexcept>
 #include <string>
 #include <tuple>
@@ -35,6 +36,16 @@ __global__ void spin_kernel(long long cycles) {
     while (clock64() - t0 < cycles) {}
 }
 void launch_spin(long long cycles, cudaStream_t st) { spin_kernel<<<1, 1, 0, st>>>(cycles); }
+
+void set_max_shared_carveout(const void* kernel) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.insert({kernel, dev}).second)
+        cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+}
 }
 
 using namespace mgc;
@@ -177,31 +188,27 @@ QWeight upload_weight(int wtype, const void* host, int N, int K) {
     if (wtype != 8 && wtype != 12) throw Err("unsupported weight type " + std::to_string(wtype));
     if (K % 128 != 0 || (wtype == 12 && K % 256 != 0)) throw Err("qweight: K must be a multiple of 128 (256 for Q4_K)");
     w.Npad = round_up(N, 128);
-    std::vector<int8_t> q; std::vector<float> sa, sb;
-    repack(wtype, (const uint8_t*)host, N, K, w.Npad, q, sa, sb);
+    std::vector<int8_t> q; std::vector<float> sc;
+    repack(wtype, (const uint8_t*)host, N, K, w.Npad, q, sc);
     w.q = dupload(q.data(), q.size());
-    w.sa = dupload(sa.data(), sa.size());
-    if (wtype == 12) w.sb = dupload(sb.data(), sb.size());
+    w.s = dupload(sc.data(), sc.size());
     return w;
 }
 void free_weight(QWeight& w) {
-    cudaFree(w.q); cudaFree(w.sa); cudaFree(w.sb); cudaFree(w.f32);
+    cudaFree(w.q); cudaFree(w.s); cudaFree(w.f32);
     w = QWeight{};
 }
 
-// Quantized-activation buffers for up to Mpad rows and K columns.
+// Quantized-activation tiles for up to Mpad rows and K columns (kernels.h layout).
 ActQ alloc_actq(int Mpad, int K) {
     ActQ a;
     a.Mpad = Mpad;
-    a.q = dalloc<int8_t>((size_t)K * Mpad);
-    a.d = dalloc<float>((size_t)(K / 32) * Mpad);
-    a.c = dalloc<float>((size_t)(K / 32) * Mpad);
-    CK(cudaMemset(a.q, 0, (size_t)K * Mpad));
-    CK(cudaMemset(a.d, 0, sizeof(float) * (K / 32) * Mpad));
-    CK(cudaMemset(a.c, 0, sizeof(float) * (K / 32) * Mpad));
+    const size_t bytes = (size_t)(K / 128) * (Mpad / 128) * kActTile;
+    a.q = dalloc<int8_t>(bytes);
+    CK(cudaMemset(a.q, 0, bytes));
     return a;
 }
-void free_actq(ActQ& a) { cudaFree(a.q); cudaFree(a.d); cudaFree(a.c); a = ActQ{}; }
+void free_actq(ActQ& a) { cudaFree(a.q); a = ActQ{}; }
 
 // Library scratch used by the standalone mgc_qgemm entry point (grown on demand, per device).
 struct Scratch { ActQ a; int Mpad = 0, K = 0, N = 0; float* attn = nullptr; size_t attn_n = 0; SplitK sk; };
@@ -456,6 +463,12 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
     std::vector<Ev> evs;
     if (rt->prof) launch_spin(2000000, st);   // ~1 ms at 2 GHz
     auto op = [&](const char* name, auto&& fn) {
+#ifdef MGC_DEBUG_SKIP_OPS
+        // diagnostic builds only: MGC_SKIP="MulMat(q),Norm,..." drops op classes (wrong
+        // results) to attribute graph step time
+        if (const char* sk = std::getenv("MGC_SKIP"))
+            if (std::strstr(sk, name)) return;
+#endif
         if (!rt->prof) { fn(); return; }
         Ev e{name, nullptr, nullptr};
         CK(cudaEventCreate(&e.a)); CK(cudaEventCreate(&e.b));
@@ -636,6 +649,11 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
         CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
         CK(cudaDeviceSynchronize());
+        // one eager forward: sets every kernel's attributes outside any later stream capture
+        CK(cudaMemsetAsync(rt->tokens, 0, sizeof(int32_t) * R, rt->st));
+        enqueue_forward(rt.get(), rt->tokens, 1, std::min(max_rows, rt->n_pos), rt->logits, nullptr);
+        CK(cudaStreamSynchronize(rt->st));
+        check_dev_error();
         *out = rt.release();
     });
 }
