@@ -79,7 +79,7 @@ __device__ __forceinline__ float act_apply(float v, int a) {
 #ifdef MGC_QGEMM_TRACE
 __device__ __forceinline__ void trace(const QGemmArgs& p, int idx, long long t0) {
     if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1888) {
-        long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        const long long t = clock64();   // SM cycles since kernel entry
         p.y[(size_t)(idx / 32) * p.N + (idx % 32)] = (float)(t - t0);   // inside this CTA's tile
     }
 }
@@ -94,7 +94,11 @@ struct QGemmCfg {
     static constexpr int NPW = 4 * CG, CW = BN / CG;
     // TMEM ring of 4-block groups (4 * BN columns each), at most 256 columns so two CTAs
     // can share an SM
+#ifdef MGC_NGRP
+    static constexpr int NGRP = MGC_NGRP;
+#else
     static constexpr int NGRP = 256 / (4 * BN) >= 2 ? 2 : 1;
+#endif
 #ifdef MGC_NST
     static constexpr int NST = MGC_NST;
 #else
@@ -108,14 +112,19 @@ struct QGemmCfg {
                               STAGE = (OFF_S + S_BYTES + 1023) & ~1023u;
     static constexpr uint32_t TX_BYTES = A_BYTES + B_BYTES + S_BYTES;
     static constexpr uint32_t SMEM = 1024 + NST * STAGE + 256;
-    static constexpr uint32_t TMEM_COLS = 4 * BN * NGRP;
+    // allocation is a power of two >= 32 columns
+    static constexpr uint32_t TMEM_NEED = 4 * BN * NGRP,
+                              TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                        : TMEM_NEED <= 256 ? 256 : 512;
 };
 
 template <int BN, int CG, bool Q4K>
 __global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K>::THREADS, MGC_QGEMM_MINB)
 qgemm_kernel(const QGemmArgs p) {
     using C = QGemmCfg<BN, CG, Q4K>;
-    constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= MGC_QGEMM_IREGS ? 1 : MGC_QGEMM_IREGS / CW > 4 ? 4 : MGC_QGEMM_IREGS / CW;
+    // int32 dot values per TMEM batch: 64 registers, 32 when the CTA is too wide for that
+    constexpr int IREGS = C::THREADS > 448 ? 32 : MGC_QGEMM_IREGS;
+    constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= IREGS ? 1 : IREGS / CW > 4 ? 4 : IREGS / CW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* full = (uint64_t*)(smem + NST * C::STAGE);
@@ -125,10 +134,14 @@ qgemm_kernel(const QGemmArgs p) {
     uint32_t* tmem_slot = (uint32_t*)(tempty + NGRP);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
+#ifdef MGC_EXP_EMPTY
+    return;
+#endif
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128;
 #ifdef MGC_QGEMM_TRACE
-    long long t_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
+    const long long t_start = clock64();
+    long long g_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g_start));
 #endif
     const int nkc = p.K / 128;
     const int kz = blockIdx.z, kc0 = kz * p.cps, nloc = max(0, min(nkc, kc0 + p.cps) - kc0);
@@ -146,7 +159,9 @@ qgemm_kernel(const QGemmArgs p) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
+#ifdef MGC_EXP_SETUP
+    if (true) {} else
+#endif
     if (warp == 0) {
         if (lane == 0) {
             int last_it[NST];
@@ -157,8 +172,13 @@ qgemm_kernel(const QGemmArgs p) {
                 uint8_t* st = smem + s * C::STAGE;
                 TRACE(i);
                 // three copies per chunk: activation tile (+ its scales), weight codes, weight scales
+#ifdef MGC_EXP_SMALLA
+                mbar_arrive_expect_tx(&full[s], C::TX_BYTES - C::A_BYTES + 1024);
+                bulk_g2s(st, p.aq + ((size_t)kc * (p.Mpad / 128) + blockIdx.y) * kActTile, 1024, &full[s]);
+#else
                 mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
                 bulk_g2s(st, p.aq + ((size_t)kc * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES, &full[s]);
+#endif
                 bulk_g2s(st + C::OFF_B, p.wq + ((size_t)kc * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
                 bulk_g2s(st + C::OFF_S, p.ws + ((size_t)kc * (p.Npad / 4) + n0 / 4) * 16 * C::T, C::S_BYTES, &full[s]);
                 last_it[s] = it;
@@ -182,6 +202,12 @@ qgemm_kernel(const QGemmArgs p) {
                 // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
+#ifdef MGC_EXP_MMA1
+                    if (j > 0) continue;
+#endif
+#ifdef MGC_EXP_MMA0
+                    continue;
+#endif
                     mma_i8(tmem + (g * 4 + j) * BN, sdesc_sw128(a_base + 32 * j), sdesc_sw128(b_base + 32 * j),
                            idesc, 0);
                     if (kc < 8) TRACE(1808 + kc * 6 + j);
@@ -210,6 +236,7 @@ qgemm_kernel(const QGemmArgs p) {
         auto issue = [&](uint32_t (&I)[BATCH][CW], int t) {
             const int kc = t / BPC, jb = t % BPC, g = kc % NGRP;
             if (jb == 0) {
+                if (warp == 2 && lane == 0) TRACE(864 + kc);
                 bool w = mbar_wait(&full[kc % NST], (kc / NST) & 1, abort_flag, 4) &&
                          mbar_wait(&tfull[g], (kc / NGRP) & 1, abort_flag, 5);
                 ok = __all_sync(0xffffffffu, w);
@@ -217,6 +244,9 @@ qgemm_kernel(const QGemmArgs p) {
                 tc_fence_after();
                 if (warp == 2 && lane == 0) TRACE(768 + kc);
             }
+#ifdef MGC_EXP_NOLD
+            return;
+#endif
 #pragma unroll
             for (int jj = 0; jj < BATCH; jj++) {
                 const uint32_t ta = t_lane + (g * 4 + jb * BATCH + jj) * BN;
@@ -232,6 +262,7 @@ qgemm_kernel(const QGemmArgs p) {
         // wait for batch t's loads, pin the registers after the wait, release the TMEM group
         auto landed = [&](uint32_t (&I)[BATCH][CW], int t) {
             tmem_ld_wait();
+            if (warp == 2 && lane == 0 && t % BPC == 0) TRACE(800 + t / BPC);
 #pragma unroll
             for (int jj = 0; jj < BATCH; jj++)
 #pragma unroll
@@ -294,6 +325,7 @@ qgemm_kernel(const QGemmArgs p) {
             landed(I, t);
             promote(I, t);
         }
+        if (lane == 0) TRACE(1800 + warp);
         // epilogue: bias -> act -> residual (mg-opencl.cpp:481-493)
         float acc[CW];
 #pragma unroll
@@ -384,7 +416,7 @@ qgemm_kernel(const QGemmArgs p) {
 #ifdef MGC_QGEMM_TRACE
     if (threadIdx.x == 64 && !(blockIdx.x == 0 && blockIdx.y == 0)) {   // per-CTA [start, end] stamps (low 32 bits)
         long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        p.y[(size_t)m0 * p.N + n0] = __int_as_float((int)(t_start & 0x7fffffff));
+        p.y[(size_t)m0 * p.N + n0] = __int_as_float((int)(g_start & 0x7fffffff));
         p.y[(size_t)m0 * p.N + n0 + 1] = __int_as_float((int)(t & 0x7fffffff));
     }
 #endif
@@ -407,7 +439,7 @@ static int set_smem_attr() {
 // Sets the dynamic shared-memory limit of every instantiation on the current device.  Must
 // run once per device before the first launch (the runtime does it at creation, outside any
 // stream capture).
-#define MGC_QGEMM_CONFIGS(X) X(32, 1) X(32, 2) X(64, 2) X(64, 4) X(128, 4)
+#define MGC_QGEMM_CONFIGS(X) X(16, 1) X(32, 1) X(32, 2) X(48, 3) X(64, 2) X(64, 4)
 
 int qgemm_prepare() {
     int rc = 0;
@@ -436,12 +468,19 @@ static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
     }
     if (fbn) { bn = fbn; cg = fcg; return; }
     (void)K;
-    // measured (ncu, cold L2) over the config-2 sweep: 32 columns x 2 warp groups wins at
-    // M <= ~512, 64 x 2 above
-    const int mt = (M + 127) / 128;
-    bn = (M <= 512 && (long)mt * ((N + 31) / 32) <= 148 * MGC_QGEMM_MINB) ? 32 : 64;
-    cg = 2;
-    (void)N;
+    // 16 columns per promotion warp; pick the width whose tile grid fills the 148 SMs in the
+    // fewest waves, weighing a wave by its per-CTA work (BN) plus a fixed per-chunk cost (~16
+    // columns' worth).  Widths whose last tile would run past the padded weight rows are skipped.
+    const int mt = (M + 127) / 128, npad = round_up(N, 128);
+    const int cand[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
+    long best = -1;
+    for (const auto& c : cand) {
+        const int tiles_n = (N + c[0] - 1) / c[0];
+        if (tiles_n * c[0] > npad) continue;
+        const long waves = ((long)tiles_n * mt + 148 * MGC_QGEMM_MINB - 1) / (148 * MGC_QGEMM_MINB);
+        const long cost = waves * (c[0] + 16);
+        if (best < 0 || cost < best) { best = cost; bn = c[0]; cg = c[1]; }
+    }
 }
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
