@@ -134,9 +134,6 @@ qgemm_kernel(const QGemmArgs p) {
     uint32_t* tmem_slot = (uint32_t*)(tempty + NGRP);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
-#ifdef MGC_EXP_EMPTY
-    return;
-#endif
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128;
 #ifdef MGC_QGEMM_TRACE
@@ -159,9 +156,6 @@ qgemm_kernel(const QGemmArgs p) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-#ifdef MGC_EXP_SETUP
-    if (true) {} else
-#endif
     if (warp == 0) {
         if (lane == 0) {
             int last_it[NST];
@@ -172,13 +166,8 @@ qgemm_kernel(const QGemmArgs p) {
                 uint8_t* st = smem + s * C::STAGE;
                 TRACE(i);
                 // three copies per chunk: activation tile (+ its scales), weight codes, weight scales
-#ifdef MGC_EXP_SMALLA
-                mbar_arrive_expect_tx(&full[s], C::TX_BYTES - C::A_BYTES + 1024);
-                bulk_g2s(st, p.aq + ((size_t)kc * (p.Mpad / 128) + blockIdx.y) * kActTile, 1024, &full[s]);
-#else
                 mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
                 bulk_g2s(st, p.aq + ((size_t)kc * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES, &full[s]);
-#endif
                 bulk_g2s(st + C::OFF_B, p.wq + ((size_t)kc * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
                 bulk_g2s(st + C::OFF_S, p.ws + ((size_t)kc * (p.Npad / 4) + n0 / 4) * 16 * C::T, C::S_BYTES, &full[s]);
                 last_it[s] = it;
@@ -202,18 +191,10 @@ qgemm_kernel(const QGemmArgs p) {
                 // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-#ifdef MGC_EXP_MMA1
-                    if (j > 0) continue;
-#endif
-#ifdef MGC_EXP_MMA0
-                    continue;
-#endif
                     mma_i8(tmem + (g * 4 + j) * BN, sdesc_sw128(a_base + 32 * j), sdesc_sw128(b_base + 32 * j),
                            idesc, 0);
-                    if (kc < 8) TRACE(1808 + kc * 6 + j);
                 }
                 mma_commit(&tfull[g]);   // the chunk's 4 dot tiles are ready
-                if (kc < 8) TRACE(1808 + kc * 6 + 4);
                 mma_commit(&empty[s]);   // its shared-memory operands may be overwritten
                 TRACE(256 + kc);
             }
@@ -244,9 +225,6 @@ qgemm_kernel(const QGemmArgs p) {
                 tc_fence_after();
                 if (warp == 2 && lane == 0) TRACE(768 + kc);
             }
-#ifdef MGC_EXP_NOLD
-            return;
-#endif
 #pragma unroll
             for (int jj = 0; jj < BATCH; jj++) {
                 const uint32_t ta = t_lane + (g * 4 + jb * BATCH + jj) * BN;
