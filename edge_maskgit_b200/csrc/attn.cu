@@ -18,6 +18,7 @@
 //   5. each thread rescales its register accumulator o[48] by alpha and adds O_tile.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "rowquant.cuh"
 #include <cuda_fp16.h>
 
 namespace mgc {
@@ -292,6 +293,48 @@ __global__ void attn_combine(const float* __restrict__ opart, const float* __res
         make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
 }
 
+// Same merge as attn_combine, one warp per row over all heads (row held in chunk layout:
+// lane l owns elements 256 i + 8 l .. +7, which lie in one head since 48 % 8 == 0), followed by
+// the quantizer of the O projection's input.  out may be null (only the quantized row needed).
+template <int NC>
+__global__ void __launch_bounds__(128) attn_combine_rows(const float* __restrict__ opart, const float* __restrict__ mlpart,
+                                                         int nsplit, int R, int H, float* __restrict__ out, ActQ a,
+                                                         int want_c) {
+    griddep_wait();
+    griddep_launch();
+    const int lane = threadIdx.x & 31, r = blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (r >= R) return;
+    constexpr int E = NC * 256;
+    const float2* ml = reinterpret_cast<const float2*>(mlpart);
+    float v[NC][8];
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        const int e0 = 256 * i + 8 * lane, h = e0 / fa::D, rh = r * H + h;
+        float m = -INFINITY;
+        for (int s = 0; s < nsplit; s++) m = fmaxf(m, ml[(size_t)s * R * H + rh].x);
+        float l = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int s = 0; s < nsplit; s++) {
+            const float2 v2 = ml[(size_t)s * R * H + rh];
+            const float wgt = expf(v2.x - m);
+            l = __fmaf_rn(v2.y, wgt, l);
+            const float4* src = reinterpret_cast<const float4*>(opart + ((size_t)s * R + r) * E + e0);
+            const float4 x0 = src[0], x1 = src[1];
+            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[e] = __fmaf_rn(xs[e], wgt, acc[e]);
+        }
+        const float inv = __fdiv_rn(1.0f, l);
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[i][e] = __fmul_rn(acc[e], inv);
+        if (out) {
+            float4* dst = reinterpret_cast<float4*>(out + (size_t)r * E + e0);
+            dst[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+            dst[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+        }
+    }
+    quant_chunks<NC>(v, r, a, want_c != 0, lane);
+}
+
 size_t attn_scratch_floats(int B, int S, int H) {
     return (size_t)kAttnMaxSplit * B * S * H * (fa::D + 2);
 }
@@ -308,7 +351,8 @@ int attn_prepare() {
 }
 
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
-                      size_t scratch_floats, cudaStream_t st) {
+                      size_t scratch_floats, cudaStream_t st, const ActQ* qo, bool qo_c, bool* quantized) {
+    if (quantized) *quantized = false;
     if (Dh != fa::D) return -2;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -328,7 +372,10 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     dim3 grid(qt, H, B * nsplit);
     launch_k(flash_attn_tc, grid, 128, fa::SMEM, st, qkv, S, H, scale, out, nsplit, tiles_per, opart, mlpart);
     g_launch_count += nsplit > 1 ? 2 : 1;
-    if (nsplit > 1) launch_k(attn_combine, (R * H * (fa::D / 4) + 255) / 256, 256, 0, st, opart, mlpart, nsplit, R, H, out);
+    if (nsplit > 1 && qo && H * fa::D == 768) {   // merge + quantize in one pass (warp per row)
+        launch_k(attn_combine_rows<3>, (R + 3) / 4, 128, 0, st, opart, mlpart, nsplit, R, H, out, *qo, qo_c ? 1 : 0);
+        if (quantized) *quantized = true;
+    } else if (nsplit > 1) launch_k(attn_combine, (R * H * (fa::D / 4) + 255) / 256, 256, 0, st, opart, mlpart, nsplit, R, H, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -113,8 +113,11 @@ struct SplitK {
     int n_counters = 0;
 };
 // int8-dot GEMM on tcgen05: y = act(W . x + bias) + resid.  sk == nullptr: no split-K.
+// qo != nullptr: also quantize y into qo (the quantizer of the next linear layer, bit-identical
+// to launch_quant_act_tiled on y; qo_c: write the Q4_K term); y may then be null.
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
-                 const float* resid, float* y, cudaStream_t st, const SplitK* sk = nullptr);
+                 const float* resid, float* y, cudaStream_t st, const SplitK* sk = nullptr,
+                 const ActQ* qo = nullptr, bool qo_c = false);
 // set the kernels' shared-memory limits on the current device (once per device)
 int qgemm_prepare();
 int attn_prepare();
@@ -125,8 +128,11 @@ void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const 
 // scratch (optional) holds the key-split partials: attn_scratch_floats() floats.
 constexpr int kAttnMaxSplit = 4;
 size_t attn_scratch_floats(int B, int S, int H);
+// qo (optional): when the key range is split, the merge pass also quantizes the output rows
+// into qo (*quantized = true); otherwise the caller quantizes.
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
-                      size_t scratch_floats, cudaStream_t st);
+                      size_t scratch_floats, cudaStream_t st, const ActQ* qo = nullptr, bool qo_c = false,
+                      bool* quantized = nullptr);
 
 }  // namespace mgc
 

@@ -44,6 +44,9 @@ struct QGemmArgs {
     // split-K: CTA z of gridDim.z handles K chunks [z*cps, (z+1)*cps); partials go to
     // part [nsplit][M][N], the last CTA of a tile (counters[tile] reaches nsplit) reduces them
     float* part; int* counters; int nsplit, cps;
+    // fused output quantizer (optional): quantize y per 32-block into ActQ tiles qo (the next
+    // layer's activation); y may then be null.  Needs CW == 16 and BN % 32 == 0.
+    int8_t* qo; int qo_Mpad; int qo_c;
 };
 
 // Packed f32x2 arithmetic (sm_100): each lane is an IEEE round-to-nearest op, bit-identical
@@ -111,7 +114,8 @@ struct QGemmCfg {
     static constexpr uint32_t OFF_DX = 16384, OFF_CX = 18432, OFF_B = A_BYTES, OFF_S = OFF_B + B_BYTES,
                               STAGE = (OFF_S + S_BYTES + 1023) & ~1023u;
     static constexpr uint32_t TX_BYTES = A_BYTES + B_BYTES + S_BYTES;
-    static constexpr uint32_t SMEM = 1024 + NST * STAGE + 256;
+    static constexpr uint32_t XCHG = NST * STAGE + 256;   // epilogue exchange: [2][NPW][32] f32
+    static constexpr uint32_t SMEM = 1024 + XCHG + 2 * NPW * 32 * 4;
     // allocation is a power of two >= 32 columns
     static constexpr uint32_t TMEM_NEED = 4 * BN * NGRP,
                               TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
@@ -353,15 +357,16 @@ qgemm_kernel(const QGemmArgs p) {
                 }
             }
         }
-        if (m < p.M && !*abort_flag && !keep_stamps) {
-            const int nbase = n0 + c0;
+        const bool store = m < p.M && !*abort_flag && !keep_stamps;
+        const int nbase = n0 + c0;
+        float vals[CW];
+        if (store) {
             const bool vec = (p.N % 4) == 0;
 #pragma unroll
             for (int c = 0; c < CW; c += 4) {
                 const int n = nbase + c;
-                if (n >= p.N) break;
                 float v[4] = {acc[c], acc[c + 1], acc[c + 2], acc[c + 3]};
-                if (vec) {
+                if (n + 3 < p.N && vec) {
                     if (p.bias) {
                         const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + n));
                         v[0] = __fadd_rn(v[0], b4.x); v[1] = __fadd_rn(v[1], b4.y);
@@ -374,16 +379,62 @@ qgemm_kernel(const QGemmArgs p) {
                         v[0] = __fadd_rn(v[0], r4.x); v[1] = __fadd_rn(v[1], r4.y);
                         v[2] = __fadd_rn(v[2], r4.z); v[3] = __fadd_rn(v[3], r4.w);
                     }
-                    *reinterpret_cast<float4*>(p.y + (size_t)m * p.N + n) = make_float4(v[0], v[1], v[2], v[3]);
+                    if (p.y) *reinterpret_cast<float4*>(p.y + (size_t)m * p.N + n) = make_float4(v[0], v[1], v[2], v[3]);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        if (n + i >= p.N) break;
+                        if (n + i >= p.N) { v[i] = 0.0f; continue; }
                         float x = v[i];
                         if (p.bias) x = __fadd_rn(x, p.bias[n + i]);
                         x = act_apply(x, p.act);
                         if (p.resid) x = __fadd_rn(x, p.resid[(size_t)m * p.N + n + i]);
-                        p.y[(size_t)m * p.N + n + i] = x;
+                        if (p.y) p.y[(size_t)m * p.N + n + i] = x;
+                        v[i] = x;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) vals[c + i] = v[i];
+            }
+        } else {
+#pragma unroll
+            for (int c = 0; c < CW; c++) vals[c] = 0.0f;
+        }
+        if constexpr (CW == 16) {
+            if (p.qo) {
+                // The 32-block of columns [32k, 32k+32) is split between this warp (16 columns) and
+                // the warp of the neighbouring column group (same rows): exchange amax and sum.
+                float* xa = reinterpret_cast<float*>(smem + C::XCHG);
+                int* xs = reinterpret_cast<int*>(xa + C::NPW * 32);
+                float amax = 0.0f;
+#pragma unroll
+                for (int c = 0; c < CW; c++) amax = fmaxf(amax, fabsf(vals[c]));
+                xa[pw * 32 + lane] = amax;
+                asm volatile("bar.sync 1, %0;" ::"r"(C::NPW * 32) : "memory");
+                amax = fmaxf(amax, xa[(pw ^ 4) * 32 + lane]);
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float id = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                alignas(16) int8_t qv[16];
+                int sum = 0;
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    const int qi = (int)roundf(__fmul_rn(vals[c], id));
+                    qv[c] = (int8_t)qi;
+                    sum += qi;
+                }
+                if (p.qo_c) {
+                    xs[pw * 32 + lane] = sum;
+                    asm volatile("bar.sync 1, %0;" ::"r"(C::NPW * 32) : "memory");
+                    sum += xs[(pw ^ 4) * 32 + lane];
+                }
+                if (store) {
+                    ActQ qa;
+                    qa.q = p.qo;
+                    qa.Mpad = p.qo_Mpad;
+                    const int kc = nbase >> 7, j = (nbase >> 5) & 3;
+                    *reinterpret_cast<int4*>(qa.q + act_code(qa, kc, m, nbase & 127)) = *reinterpret_cast<const int4*>(qv);
+                    if (((nbase >> 4) & 1) == 0) {   // the lower half writes the block's scales
+                        act_dx(qa, kc, m)[j] = d;
+                        if (p.qo_c) act_cx(qa, kc, m)[j] = __fmul_rn(d, (float)sum);
                     }
                 }
             }
@@ -438,13 +489,13 @@ static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
 
 // Tile shape (BN columns, CG column groups of promotion warps).  MGC_QGEMM_CFG="BN,CG"
 // overrides the heuristic (used to sweep shapes).
-static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
+static void pick_cfg(int M, int N, int K, bool fused_quant, int& bn, int& cg) {
     static int fbn = -1, fcg = 0;
     if (fbn < 0) {
         fbn = 0;
         if (const char* e = std::getenv("MGC_QGEMM_CFG")) std::sscanf(e, "%d,%d", &fbn, &fcg);
     }
-    if (fbn) { bn = fbn; cg = fcg; return; }
+    if (fbn && (!fused_quant || (fbn % 32 == 0 && fbn / fcg == 16))) { bn = fbn; cg = fcg; return; }
     (void)K;
     // 16 columns per promotion warp; pick the width whose tile grid fills the 148 SMs in the
     // fewest waves, weighing a wave by its per-CTA work (BN) plus a fixed per-chunk cost (~16
@@ -455,6 +506,7 @@ static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
     for (const auto& c : cand) {
         const int tiles_n = (N + c[0] - 1) / c[0];
         if (tiles_n * c[0] > npad) continue;
+        if (fused_quant && c[0] % 32 != 0) continue;   // both halves of a 32-block in one CTA
         const long waves = ((long)tiles_n * mt + 148 * MGC_QGEMM_MINB - 1) / (148 * MGC_QGEMM_MINB);
         const long cost = waves * (c[0] + 16);
         if (best < 0 || cost < best) { best = cost; bn = c[0]; cg = c[1]; }
@@ -462,10 +514,11 @@ static void pick_cfg(int M, int N, int K, int& bn, int& cg) {
 }
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
-                 const float* resid, float* y, cudaStream_t st, const SplitK* sk) {
+                 const float* resid, float* y, cudaStream_t st, const SplitK* sk, const ActQ* qo, bool qo_c) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
+    if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
     int bn, cg;
-    pick_cfg(M, w.N, w.K, bn, cg);
+    pick_cfg(M, w.N, w.K, qo != nullptr, bn, cg);
     // Split-K (MGC_QGEMM_SPLITK=<n>) is off by default: on the config-1 shapes it measured
     // slower than one CTA per tile (ncu: attn_o 11 -> 26 us with 3 splits, ffn_down 22 -> 38 us
     // with 4), so the library only splits when asked.
@@ -479,7 +532,8 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     const int cps = (nkc + nsplit - 1) / nsplit;
     nsplit = (nkc + cps - 1) / cps;   // no empty split
     QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
-                sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps};
+                sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps,
+                qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0};
     const bool q4 = w.wtype == 12;
 #define X(BN, CG) \
     if (bn == BN && cg == CG) return q4 ? run_qgemm<BN, CG, true>(p, st) : run_qgemm<BN, CG, false>(p, st);

@@ -406,6 +406,7 @@ struct mgc_runtime {
     std::map<std::tuple<int, int, const void*, const void*>, cudaGraphExec_t> graphs;
     // profiling
     bool prof = false;
+    bool fuse = true;        // fused epilogue quantizers (MGC_NO_FUSE=1 runs them as separate kernels)
     int last_launches = 0;   // kernels enqueued by the last forward
     std::map<std::string, ProfRow> prof_rows;
 
@@ -487,17 +488,28 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
     for (int l = 0; l < rt->n_layer; l++) {
         const LayerW& L = rt->layers[l];
         op(mm, [&] { linear(rt, L.qkv, rt->x, rt->aE, R, L.bqkv, 0, nullptr, rt->qkv); });
+        bool att_quantized = false;
         op("FlashAttention", [&] {
+            const bool fq = rt->fuse && L.o.wtype != 0;
             if (launch_flash_attn(rt->qkv, B, S, rt->n_head, rt->Dh, scale, rt->att, rt->attn_scratch,
-                                  rt->attn_scratch_n, st) != 0)
+                                  rt->attn_scratch_n, st, fq ? &rt->aE : nullptr, qc, &att_quantized) != 0)
                 throw Err("flash attention launch failed");
         });
-        if (L.o.wtype != 0) op("Quantize", [&] { launch_quant_act_tiled(rt->att, R, E, rt->aE, qc, st); });
+        if (L.o.wtype != 0 && !att_quantized)
+            op("Quantize", [&] { launch_quant_act_tiled(rt->att, R, E, rt->aE, qc, st); });
         op(mm, [&] { linear(rt, L.o, rt->att, rt->aE, R, L.bo, 0, rt->x, rt->t); });
         op("Norm", [&] { launch_ln(rt->t, L.g1, L.b1, R, E, rt->eps, rt->x, &rt->aE, qc, st); });
         put(rt->x, E);
-        op(mm, [&] { linear(rt, L.up, rt->x, rt->aE, R, L.bup, 1, nullptr, rt->ff); });
-        if (L.down.wtype != 0) op("Quantize", [&] { launch_quant_act_tiled(rt->ff, R, F, rt->aF, qc, st); });
+        if (L.up.wtype != 0 && L.down.wtype != 0 && rt->fuse) {
+            // ffn_up's epilogue quantizes GELU(x W_up + b) straight into ffn_down's input tiles
+            op(mm, [&] {
+                if (launch_qgemm(L.up, rt->aE, R, L.bup, 1, nullptr, nullptr, st, &rt->sk, &rt->aF, qc) != 0)
+                    throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+            });
+        } else {
+            op(mm, [&] { linear(rt, L.up, rt->x, rt->aE, R, L.bup, 1, nullptr, rt->ff); });
+            if (L.down.wtype != 0) op("Quantize", [&] { launch_quant_act_tiled(rt->ff, R, F, rt->aF, qc, st); });
+        }
         op(mm, [&] { linear(rt, L.down, rt->ff, rt->aF, R, L.bdown, 0, rt->x, rt->t); });
         op("Norm", [&] { launch_ln(rt->t, L.g2, L.b2, R, E, rt->eps, rt->x, &rt->aE, qc, st); });
         put(rt->x, E);
@@ -576,6 +588,7 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         if (!path || !out || max_rows <= 0) throw Err("mgc_runtime_create: bad arguments");
         std::unique_ptr<mgc_runtime, void (*)(mgc_runtime*)> rt(new mgc_runtime(), destroy_runtime);
         rt->device = device;
+        if (const char* e = std::getenv("MGC_NO_FUSE")) rt->fuse = e[0] != '1';
         CK(cudaSetDevice(device));
         cudaDeviceProp prop;
         CK(cudaGetDeviceProperties(&prop, device));

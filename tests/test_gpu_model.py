@@ -88,3 +88,21 @@ def test_profile_report(small_models):
     assert rows["MulMat(q)"].count == spec.n_layer * 4 + 1
     assert rows["FlashAttention"].count == spec.n_layer
     r.close()
+
+
+def test_fused_quantizers_match_separate_kernels(small_models, monkeypatch):
+    """The quantizers fused into GEMM / attention epilogues give the same logits, bit for bit,
+    as the separate quantizer kernels (same f32 values, same per-block arithmetic)."""
+    from edge_maskgit_b200 import runtime as rt, synth
+    for q in ("gq8", "gq4"):
+        path, spec = small_models[q]
+        tok = synth.config1_tokens(spec)
+        monkeypatch.delenv("MGC_NO_FUSE", raising=False)
+        a = rt.CudaRuntime(path, max_rows=spec.n_tokens + 1)
+        fused = a.forward(tok)
+        a.close()
+        monkeypatch.setenv("MGC_NO_FUSE", "1")
+        b = rt.CudaRuntime(path, max_rows=spec.n_tokens + 1)
+        sep = b.forward(tok)
+        b.close()
+        assert np.array_equal(fused, sep), q
