@@ -281,6 +281,60 @@ def run_cuda_arm(args) -> None:
         dist.destroy_process_group()
 
 
+def run_tp_workload(args) -> None:
+    """Config 5: step-1 forward at M=4097 (64x64 tokens + class), batch 4, Q4_K, column-split
+    over the ranks with NCCL all-gathers.  Total work is fixed, so scaling is strong."""
+    import torch
+    import torch.distributed as dist
+    from edge_maskgit_b200 import synth
+    from edge_maskgit_b200.tp import TPForward
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    MODEL_DIR.mkdir(parents=True, exist_ok=True)
+    path = MODEL_DIR / "c5_gq4_n4096.gguf"
+    spec = synth.ModelSpec(n_tokens=4096, quant="gq4")
+    if rank == 0 and not path.exists():
+        tmp = path.with_suffix(f".tmp{os.getpid()}")
+        synth.make_model(tmp, spec)
+        os.replace(tmp, path)
+    if world > 1:
+        dist.barrier()
+    tp = TPForward(path, rank, world)
+    tokens = np.tile(synth.config1_tokens(spec), (4, 1))
+    tokens[:, 0] = 1024 + np.array([207, 1, 500, 999])
+    for _ in range(args.warmup):
+        tp.forward(tokens)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        logits = tp.forward(tokens)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "transformer steps/s", "value": args.steps / (ms * 1e-3), "unit": "steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
+            "data": "synthetic",
+            "config": {"workload": "config5 step-1 forward, 24 layers, M=4097, batch 4, gq4",
+                       "parallelism": f"column-split tensor parallel x{world}, NCCL all-gather"},
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -289,7 +343,12 @@ def main():
     ap.add_argument("--quant", default="gq8", choices=["gq8", "gq4"])
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c5"],
+                    help="c1: the headline config-1 step (default); c5: M=4097 tensor-parallel step")
     args = ap.parse_args()
+    if args.workload == "c5" and args.impl == "cuda":
+        run_tp_workload(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args)
     else:
