@@ -6,16 +6,20 @@
 // the output accumulator are f32 with the online (flash) rescale per key tile.  Input is the
 // fused QKV projection [B*S][3E] (q | k | v, head h at columns h*Dh); the output is written
 // head-merged [B*S][E], i.e. what the reference's permute+cont (mg-transformer.cpp:84) makes.
+// Exponentials run in the base-2 domain (scores pre-scaled by log2 e) with exp2f.
 //
-// One CTA = 128 query rows of one (image, head), 4 warps, thread = one query row (= one TMEM
-// lane).  Per key tile of 128:
-//   1. all threads stage K (row-major) and V^T as f16 into 128-byte-swizzled shared memory;
-//   2. one thread issues S = Q K^T (M=128, N=128, K=48 as 3 x K16 MMAs) into TMEM;
-//   3. each thread reads its score row from TMEM, updates max / sum, and writes P split as
-//      P_hi = f16(p), P_lo = f16(p - P_hi) to shared memory (so P keeps ~22 bits, like the
-//      reference's f32 P);
-//   4. one thread issues O_tile = P_hi V + P_lo V (M=128, N=48, K=128) into TMEM;
-//   5. each thread rescales its register accumulator o[48] by alpha and adds O_tile.
+// attn_prep converts Q, K, V once to f16 tiles of 128 rows per (image, head), already in the
+// 128-byte-swizzled shared-memory layout the MMAs read (Q and K rows of 64 halves, V
+// transposed as two [48 dims][64 keys] atom blocks), so the attention kernel streams whole
+// tiles with one bulk copy each instead of re-converting every K/V tile in every query-tile CTA.
+//
+// flash_attn_tc: one CTA = 128 query rows of one (image, head, key range); 8 warps, warps w and
+// w+4 share TMEM lanes 32(w%4).. (one query row per lane) and split each tile's 128 scores and
+// the 48 output dims in halves.  Per key tile (K/V double-buffered by bulk copies):
+//   S = Q K^T (3 x K16 MMAs) in TMEM -> row max / exp / sum in registers (halves exchange max
+//   and sum through shared memory) -> P split as P_hi = f16(p), P_lo = f16(p - P_hi) (keeps
+//   ~22 bits, like the reference's f32 P) -> O_tile = P_hi V + P_lo V in TMEM -> o = alpha o +
+//   O_tile in registers.
 #include "kernels.h"
 #include "ptx.cuh"
 #include "rowquant.cuh"
@@ -31,10 +35,13 @@ constexpr uint32_t VT_BLK = D * 128;              // V^T atom block: [48 dims][6
 constexpr uint32_t VT_BYTES = 2 * VT_BLK;         // keys 0..63 | 64..127
 constexpr uint32_t P_BLK = BM * 128;              // P atom block: [128 rows][64 keys]
 constexpr uint32_t P_BYTES = 2 * P_BLK;
-constexpr uint32_t OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_VT = OFF_K + K_BYTES,
-                   OFF_PH = OFF_VT + VT_BYTES, OFF_PL = OFF_PH + P_BYTES, OFF_BAR = OFF_PL + P_BYTES;
-constexpr uint32_t SMEM = 1024 + OFF_BAR + 64;
+constexpr uint32_t PREP_ROW = Q_BYTES / BM + K_BYTES / BC + VT_BYTES / BC;   // 352 bytes per row
+constexpr uint32_t OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_V = OFF_K + 2 * K_BYTES,
+                   OFF_PH = OFF_V + 2 * VT_BYTES, OFF_PL = OFF_PH + P_BYTES, OFF_X = OFF_PL + P_BYTES,
+                   OFF_BAR = OFF_X + 4 * BM * 4;
+constexpr uint32_t SMEM = 1024 + OFF_BAR + 128;
 constexpr uint32_t TMEM_COLS = 256;               // S: cols 0..127, O tile: cols 128..175
+constexpr float LOG2E = 1.4426950408889634f;
 }  // namespace fa
 
 // store 8 halves (16 bytes) as logical chunk `c` of row `r` in a 128B-swizzled block
@@ -45,216 +52,238 @@ __device__ __forceinline__ void st_half(uint8_t* blk, int r, int k, __half v) {
     *reinterpret_cast<__half*>(blk + sw128_off(r, k * 2)) = v;
 }
 
-__global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ qkv, int S, int H, float scale,
+// prep layout per (image b, head h), nt = ceil(S/128) tiles: [nt x Q tile][nt x K tile][nt x V^T tile]
+__device__ __forceinline__ uint8_t* prep_base(uint8_t* prep, int b, int h, int H, int nt) {
+    return prep + ((size_t)b * H + h) * nt * (size_t)(128 * fa::PREP_ROW);
+}
+
+__global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, int S, int H, int nt,
+                                                 uint8_t* __restrict__ prep) {
+    griddep_wait();
+    griddep_launch();
+    using namespace fa;
+    const int t = blockIdx.x % nt, h = (blockIdx.x / nt) % H, b = blockIdx.x / (nt * H);
+    const int r = threadIdx.x, s = t * BM + r, E = H * D, W = 3 * E;
+    uint8_t* base = prep_base(prep, b, h, H, nt);
+    uint8_t* qt = base + (size_t)t * Q_BYTES;
+    uint8_t* kt = base + (size_t)nt * Q_BYTES + (size_t)t * K_BYTES;
+    uint8_t* vt = base + (size_t)nt * (Q_BYTES + K_BYTES) + (size_t)t * VT_BYTES + (r >> 6) * VT_BLK;
+    const float* src = qkv + ((size_t)b * S + s) * W + h * D;
+#pragma unroll
+    for (int c = 0; c < D / 8; c++) {
+        __half2 hq[4], hk[4];
+        float v8[8];
+        if (s < S) {
+            const float4 q0 = *reinterpret_cast<const float4*>(src + 8 * c), q1 = *reinterpret_cast<const float4*>(src + 8 * c + 4);
+            const float4 k0 = *reinterpret_cast<const float4*>(src + E + 8 * c), k1 = *reinterpret_cast<const float4*>(src + E + 8 * c + 4);
+            const float4 a0 = *reinterpret_cast<const float4*>(src + 2 * E + 8 * c), a1 = *reinterpret_cast<const float4*>(src + 2 * E + 8 * c + 4);
+            hq[0] = __floats2half2_rn(q0.x, q0.y); hq[1] = __floats2half2_rn(q0.z, q0.w);
+            hq[2] = __floats2half2_rn(q1.x, q1.y); hq[3] = __floats2half2_rn(q1.z, q1.w);
+            hk[0] = __floats2half2_rn(k0.x, k0.y); hk[1] = __floats2half2_rn(k0.z, k0.w);
+            hk[2] = __floats2half2_rn(k1.x, k1.y); hk[3] = __floats2half2_rn(k1.z, k1.w);
+            v8[0] = a0.x; v8[1] = a0.y; v8[2] = a0.z; v8[3] = a0.w;
+            v8[4] = a1.x; v8[5] = a1.y; v8[6] = a1.z; v8[7] = a1.w;
+        } else {   // padding keys / queries: zeros (masked in the softmax, finite in P.V)
+            hq[0] = hq[1] = hq[2] = hq[3] = __floats2half2_rn(0.f, 0.f);
+            hk[0] = hk[1] = hk[2] = hk[3] = hq[0];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v8[i] = 0.f;
+        }
+        st_chunk(qt, r, c, hq);
+        st_chunk(kt, r, c, hk);
+#pragma unroll
+        for (int i = 0; i < 8; i++) st_half(vt, c * 8 + i, r & 63, __float2half_rn(v8[i]));
+    }
+}
+
+__global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__ prep, int S, int H, float scale,
                                                      float* __restrict__ out, int nsplit, int tiles_per,
                                                      float* __restrict__ opart, float* __restrict__ mlpart) {
     using namespace fa;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bar_s = (uint64_t*)(sm + OFF_BAR);
-    uint64_t* bar_o = bar_s + 1;
-    uint32_t* tmem_slot = (uint32_t*)(bar_s + 2);
+    uint64_t* bar_q = (uint64_t*)(sm + OFF_BAR);
+    uint64_t* bar_kv = bar_q + 1;   // [2]
+    uint64_t* bar_s = bar_q + 3;
+    uint64_t* bar_o = bar_q + 4;
+    uint32_t* tmem_slot = (uint32_t*)(bar_q + 5);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+    float* xmax = reinterpret_cast<float*>(sm + OFF_X);   // [2][128]
+    float* xsum = xmax + 2 * BM;                           // [2][128]
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.y, b = blockIdx.z / nsplit, split = blockIdx.z % nsplit, q0 = blockIdx.x * BM;
-    const int E = H * D, W = 3 * E;
-    const float* base = qkv + (size_t)b * S * W + h * D;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = warp >> 2;
+    const int h = blockIdx.y, b = blockIdx.z / nsplit, split = blockIdx.z % nsplit, qti = blockIdx.x, q0 = qti * BM;
+    const int E = H * D, nt = (S + BC - 1) / BC;
+    const int kt0 = split * tiles_per, kt1 = min(nt, kt0 + tiles_per);
+    const uint8_t* base = prep_base(const_cast<uint8_t*>(prep), b, h, H, nt);
+    const uint8_t* gq = base + (size_t)qti * Q_BYTES;
+    const uint8_t* gk = base + (size_t)nt * Q_BYTES;
+    const uint8_t* gv = base + (size_t)nt * (Q_BYTES + K_BYTES);
 
     if (tid == 0) {
-        mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
+        for (int i = 0; i < 5; i++) mbar_init(bar_q + i, 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
     if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
-    griddep_wait();   // qkv comes from the preceding kernel
+    griddep_wait();   // prep / qkv come from the preceding kernel
     griddep_launch();
-
-    // Q tile -> f16, swizzled
-    {
-        const int r = tid, qr = q0 + r;
-        const float4* src = reinterpret_cast<const float4*>(base + (size_t)qr * W);
-#pragma unroll
-        for (int c = 0; c < D / 8; c++) {
-            __half2 hv[4];
-            if (qr < S) {
-                const float4 a = src[2 * c], bq = src[2 * c + 1];
-                hv[0] = __floats2half2_rn(a.x, a.y); hv[1] = __floats2half2_rn(a.z, a.w);
-                hv[2] = __floats2half2_rn(bq.x, bq.y); hv[3] = __floats2half2_rn(bq.z, bq.w);
-            } else {
-                hv[0] = hv[1] = hv[2] = hv[3] = __floats2half2_rn(0.f, 0.f);
-            }
-            st_chunk(sm + OFF_Q, r, c, hv);
-        }
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_row = tmem + ((uint32_t)(warp * 32) << 16);
-
+    const int row = (warp & 3) * 32 + lane;
+    const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t sQ = smem_u32(sm + OFF_Q), sPh = smem_u32(sm + OFF_PH), sPl = smem_u32(sm + OFF_PL);
     constexpr uint32_t idesc_o = idesc_make(1, 0, 0, BM, D);
-    const uint32_t sQ = smem_u32(sm + OFF_Q), sK = smem_u32(sm + OFF_K), sV = smem_u32(sm + OFF_VT),
-                   sPh = smem_u32(sm + OFF_PH), sPl = smem_u32(sm + OFF_PL);
+    auto load_kv = [&](int kt, int buf) {
+        mbar_arrive_expect_tx(bar_kv + buf, K_BYTES + VT_BYTES);
+        bulk_g2s(sm + OFF_K + buf * K_BYTES, gk + (size_t)kt * K_BYTES, K_BYTES, bar_kv + buf);
+        bulk_g2s(sm + OFF_V + buf * VT_BYTES, gv + (size_t)kt * VT_BYTES, VT_BYTES, bar_kv + buf);
+    };
+    if (tid == 0 && kt0 < kt1) {
+        mbar_arrive_expect_tx(bar_q, Q_BYTES);
+        bulk_g2s(sm + OFF_Q, gq, Q_BYTES, bar_q);
+        load_kv(kt0, 0);
+    }
 
-    float o[D];
+    const bool wact = q0 + (warp & 3) * 32 < S;   // warp-uniform: owns at least one real query row
+    const float c1 = scale * LOG2E;               // scores in the base-2 domain
+    float o[D / 2];
 #pragma unroll
-    for (int d = 0; d < D; d++) o[d] = 0.0f;
+    for (int d = 0; d < D / 2; d++) o[d] = 0.0f;
     float m_i = -INFINITY, l_i = 0.0f;
-    const int ntiles = (S + BC - 1) / BC;
-    const int kt0 = split * tiles_per, kt1 = min(ntiles, kt0 + tiles_per);
-    const bool wact = q0 + warp * 32 < S;   // warp-uniform: this warp owns at least one real query row
     bool ok = true;
 
     for (int kt = kt0; kt < kt1 && ok; kt++) {
-        const int kb = kt * BC, ph = (kt - kt0) & 1;
-        // a short last tile runs the MMAs at N (and K for P.V) = valid keys rounded up to 16
-        const int nvalid = min(BC, S - kb), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
-        // ---- 1. stage K and V^T (f16)
-        {
-            const int t = kb + tid;
-            const float4* ks = reinterpret_cast<const float4*>(base + (size_t)t * W + E);
-            const float4* vs = reinterpret_cast<const float4*>(base + (size_t)t * W + 2 * E);
-            uint8_t* vblk = sm + OFF_VT + (tid >> 6) * VT_BLK;
-            const int kk = tid & 63;
-#pragma unroll
-            for (int c = 0; c < D / 8; c++) {
-                __half2 hk[4];
-                float v8[8];
-                if (t < S) {
-                    const float4 a = ks[2 * c], bb = ks[2 * c + 1];
-                    hk[0] = __floats2half2_rn(a.x, a.y); hk[1] = __floats2half2_rn(a.z, a.w);
-                    hk[2] = __floats2half2_rn(bb.x, bb.y); hk[3] = __floats2half2_rn(bb.z, bb.w);
-                    const float4 va = vs[2 * c], vb = vs[2 * c + 1];
-                    v8[0] = va.x; v8[1] = va.y; v8[2] = va.z; v8[3] = va.w;
-                    v8[4] = vb.x; v8[5] = vb.y; v8[6] = vb.z; v8[7] = vb.w;
-                } else {
-                    hk[0] = hk[1] = hk[2] = hk[3] = __floats2half2_rn(0.f, 0.f);
-#pragma unroll
-                    for (int i = 0; i < 8; i++) v8[i] = 0.f;
-                }
-                st_chunk(sm + OFF_K, tid, c, hk);
-#pragma unroll
-                for (int i = 0; i < 8; i++) st_half(vblk, c * 8 + i, kk, __float2half_rn(v8[i]));
+        const int i = kt - kt0, buf = i & 1, ph = i & 1;
+        const int kb = kt * BC, nvalid = min(BC, S - kb), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
+        if (tid == 0) {
+            if (kt + 1 < kt1) load_kv(kt + 1, buf ^ 1);   // that buffer's last reader (tile i-1) is done
+            bool w = (i > 0 || mbar_wait(bar_q, 0, abort_flag, 23)) && mbar_wait(bar_kv + buf, (i >> 1) & 1, abort_flag, 24);
+            if (w) {
+                tc_fence_after();
+                const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
+                const uint32_t sK = smem_u32(sm + OFF_K + buf * K_BYTES);
+                for (int k = 0; k < D / 16; k++)
+                    mma_f16(tmem, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idesc_s, k > 0);
+                mma_commit(bar_s);
             }
         }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        // ---- 2. S = Q K^T
-        if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
-            for (int k = 0; k < D / 16; k++)
-                mma_f16(tmem, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idesc_s, k > 0);
-            mma_commit(bar_s);
-        }
         ok = mbar_wait(bar_s, ph, abort_flag, 21);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; }
         ok = __syncthreads_and(ok);
         if (!ok) break;
         tc_fence_after();
-        // ---- 3. softmax row update, P = hi + lo
-        float m_new = m_i, alpha = 1.0f;
+        // ---- softmax over this half's 64 columns
+        float alpha = 1.0f;
+        uint32_t r[2][32];
+        float mloc = -INFINITY;
         if (wact) {
 #pragma unroll
-        for (int ch = 0; ch < BC / 32; ch++) {
-            if (ch >= nch) break;
-            uint32_t r[32];
-            tmem_ld32(t_row + ch * 32, r);
+            for (int cc = 0; cc < 2; cc++)
+                if (2 * half + cc < nch) tmem_ld32(t_row + (2 * half + cc) * 32, r[cc]);
             tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; j++)
-                if (ch * 32 + j < nvalid) m_new = fmaxf(m_new, __fmul_rn(__uint_as_float(r[j]), scale));
-        }
-        alpha = expf(m_i - m_new);
-        float l_new = __fmul_rn(alpha, l_i);
-        const int row = warp * 32 + lane;
+            for (int cc = 0; cc < 2; cc++) {
+                const int ch = 2 * half + cc;
+                if (ch >= nch) break;
 #pragma unroll
-        for (int ch = 0; ch < BC / 32; ch++) {
-            if (ch >= nch) break;
-            uint32_t r[32];
-            tmem_ld32(t_row + ch * 32, r);
-            tmem_ld_wait();
-            uint8_t* ph = sm + OFF_PH + (ch >> 1) * P_BLK;
-            uint8_t* pl = sm + OFF_PL + (ch >> 1) * P_BLK;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                __half2 hh[4], hl[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    float p2[2];
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int j = c * 8 + i * 2 + e;
-                        const float s = __fmul_rn(__uint_as_float(r[j]), scale);
-                        p2[e] = (ch * 32 + j < nvalid) ? expf(s - m_new) : 0.0f;
-                        l_new = __fadd_rn(l_new, p2[e]);
-                    }
-                    hh[i] = __floats2half2_rn(p2[0], p2[1]);
-                    const float2 back = __half22float2(hh[i]);
-                    hl[i] = __floats2half2_rn(p2[0] - back.x, p2[1] - back.y);
-                }
-                // chunk index within the 64-key atom row: (ch & 1) * 4 + c
-                st_chunk(ph, row, (ch & 1) * 4 + c, hh);
-                st_chunk(pl, row, (ch & 1) * 4 + c, hl);
+                for (int j = 0; j < 32; j++)
+                    if (ch * 32 + j < nvalid) mloc = fmaxf(mloc, __fmul_rn(__uint_as_float(r[cc][j]), c1));
             }
         }
-        m_i = m_new;
-        l_i = l_new;
+        xmax[half * BM + row] = mloc;
+        __syncthreads();
+        const float m_new = fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row]));
+        float lsum = 0.0f;
+        if (wact) {
+            alpha = exp2f(m_i - m_new);
+            uint8_t* pbh = sm + OFF_PH + half * P_BLK;
+            uint8_t* pbl = sm + OFF_PL + half * P_BLK;
+#pragma unroll
+            for (int cc = 0; cc < 2; cc++) {
+                const int ch = 2 * half + cc;
+                if (ch >= nch) break;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    __half2 hh[4], hl[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        float p2[2];
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const int j = c * 8 + u * 2 + e;
+                            p2[e] = (ch * 32 + j < nvalid) ? exp2f(__fmul_rn(__uint_as_float(r[cc][j]), c1) - m_new) : 0.0f;
+                            lsum = __fadd_rn(lsum, p2[e]);
+                        }
+                        hh[u] = __floats2half2_rn(p2[0], p2[1]);
+                        const float2 back = __half22float2(hh[u]);
+                        hl[u] = __floats2half2_rn(p2[0] - back.x, p2[1] - back.y);
+                    }
+                    st_chunk(pbh, row, cc * 4 + c, hh);
+                    st_chunk(pbl, row, cc * 4 + c, hl);
+                }
+            }
         }
+        xsum[half * BM + row] = lsum;
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        // ---- 4. O_tile = P_hi V + P_lo V
+        if (wact) {
+            l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(xsum[row], xsum[BM + row]));
+            m_i = m_new;
+        }
+        // ---- O_tile = P_hi V + P_lo V
         if (tid == 0) {
             tc_fence_after();
-#pragma unroll
+            const uint32_t sV = smem_u32(sm + OFF_V + buf * VT_BYTES);
             for (int part = 0; part < 2; part++) {
                 const uint32_t sP = part == 0 ? sPh : sPl;
-#pragma unroll
                 for (int j = 0; j < nmma / 16; j++) {
-                    const uint32_t a = sP + (j >> 2) * P_BLK + (j & 3) * 32;
-                    const uint32_t bv = sV + (j >> 2) * VT_BLK + (j & 3) * 32;
-                    mma_f16(tmem + BC, sdesc_sw128(a), sdesc_sw128(bv), idesc_o, (part | j) != 0);
+                    const uint32_t pa = sP + (j >> 2) * P_BLK + (j & 3) * 32;
+                    const uint32_t pv = sV + (j >> 2) * VT_BLK + (j & 3) * 32;
+                    mma_f16(tmem + BC, sdesc_sw128(pa), sdesc_sw128(pv), idesc_o, (part | j) != 0);
                 }
             }
             mma_commit(bar_o);
         }
         ok = mbar_wait(bar_o, ph, abort_flag, 22);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; }
         ok = __syncthreads_and(ok);
         if (!ok) break;
         tc_fence_after();
-        // ---- 5. o = alpha * o + O_tile
-        if (wact) {
-            uint32_t r[32], r2[16];
-            tmem_ld32(t_row + BC, r);
-            tmem_ld16(t_row + BC + 32, r2);
+        if (wact) {   // this half's 24 output dims
+            uint32_t a16[16], a8[8];
+            if (half == 0) { tmem_ld16(t_row + BC, a16); tmem_ld8(t_row + BC + 16, a8); }
+            else { tmem_ld8(t_row + BC + 24, a8); tmem_ld16(t_row + BC + 32, a16); }
             tmem_ld_wait();
+            if (half == 0) {
 #pragma unroll
-            for (int d = 0; d < 32; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(r[d]));
+                for (int d = 0; d < 16; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a16[d]));
 #pragma unroll
-            for (int d = 0; d < 16; d++) o[32 + d] = __fmaf_rn(alpha, o[32 + d], __uint_as_float(r2[d]));
+                for (int d = 0; d < 8; d++) o[16 + d] = __fmaf_rn(alpha, o[16 + d], __uint_as_float(a8[d]));
+            } else {
+#pragma unroll
+                for (int d = 0; d < 8; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a8[d]));
+#pragma unroll
+                for (int d = 0; d < 16; d++) o[8 + d] = __fmaf_rn(alpha, o[8 + d], __uint_as_float(a16[d]));
+            }
         }
         tc_fence_before();
-        __syncthreads();   // K / V / P buffers are rewritten by the next tile
+        __syncthreads();   // P and this K/V buffer are rewritten two tiles on
     }
 
-    const int qr = q0 + warp * 32 + lane;
-    if (ok && qr < S && nsplit > 1) {   // partial result of this key range, merged by attn_combine
-        const size_t R = (size_t)(gridDim.z / nsplit) * S, r = (size_t)split * R + (size_t)b * S + qr;
-        float4* dst = reinterpret_cast<float4*>(opart + r * E + h * D);
+    const int qr = q0 + row, d0 = half * (D / 2);
+    if (ok && qr < S && nsplit > 1) {   // partial result of this key range, merged by the combine pass
+        const size_t R = (size_t)(gridDim.z / nsplit) * S, rr = (size_t)split * R + (size_t)b * S + qr;
+        float4* dst = reinterpret_cast<float4*>(opart + rr * E + h * D + d0);
 #pragma unroll
-        for (int d = 0; d < D; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-        reinterpret_cast<float2*>(mlpart)[r * H + h] = make_float2(m_i, l_i);
+        for (int d = 0; d < D / 2; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        if (half == 0) reinterpret_cast<float2*>(mlpart)[rr * H + h] = make_float2(m_i, l_i);
     } else if (ok && qr < S) {
         const float inv = __fdiv_rn(1.0f, l_i);
-        float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D);
+        float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D + d0);
 #pragma unroll
-        for (int d = 0; d < D; d += 4)
+        for (int d = 0; d < D / 2; d += 4)
             dst[d / 4] = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
                                      __fmul_rn(o[d + 3], inv));
     }
@@ -266,7 +295,8 @@ __global__ void __launch_bounds__(128) flash_attn_tc(const float* __restrict__ q
     }
 }
 
-// Merge the key-range partials: m = max m_s, l = sum l_s e^(m_s - m), o = sum o_s e^(m_s - m) / l.
+// Merge the key-range partials (m in the base-2 domain): m = max m_s, l = sum l_s 2^(m_s - m),
+// o = sum o_s 2^(m_s - m) / l.
 __global__ void attn_combine(const float* __restrict__ opart, const float* __restrict__ mlpart, int nsplit,
                              int R, int H, float* __restrict__ out) {
     griddep_wait();
@@ -282,7 +312,7 @@ __global__ void attn_combine(const float* __restrict__ opart, const float* __res
     float4 acc = make_float4(0, 0, 0, 0);
     for (int s = 0; s < nsplit; s++) {
         const float2 v2 = ml[(size_t)s * R * H + rh];
-        const float wgt = expf(v2.x - m);
+        const float wgt = exp2f(v2.x - m);
         l = __fmaf_rn(v2.y, wgt, l);
         const float4 v = *reinterpret_cast<const float4*>(opart + ((size_t)s * R + r) * E + h * fa::D + d);
         acc.x = __fmaf_rn(v.x, wgt, acc.x); acc.y = __fmaf_rn(v.y, wgt, acc.y);
@@ -315,7 +345,7 @@ __global__ void __launch_bounds__(128) attn_combine_rows(const float* __restrict
         float l = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int s = 0; s < nsplit; s++) {
             const float2 v2 = ml[(size_t)s * R * H + rh];
-            const float wgt = expf(v2.x - m);
+            const float wgt = exp2f(v2.x - m);
             l = __fmaf_rn(v2.y, wgt, l);
             const float4* src = reinterpret_cast<const float4*>(opart + ((size_t)s * R + r) * E + e0);
             const float4 x0 = src[0], x1 = src[1];
@@ -335,8 +365,13 @@ __global__ void __launch_bounds__(128) attn_combine_rows(const float* __restrict
     quant_chunks<NC>(v, r, a, want_c != 0, lane);
 }
 
+size_t attn_prep_floats(int B, int S, int H) {
+    const size_t nt = (size_t)(S + fa::BC - 1) / fa::BC;
+    return (size_t)B * H * nt * 128 * fa::PREP_ROW / 4;
+}
+
 size_t attn_scratch_floats(int B, int S, int H) {
-    return (size_t)kAttnMaxSplit * B * S * H * (fa::D + 2);
+    return attn_prep_floats(B, S, H) + (size_t)kAttnMaxSplit * B * S * H * (fa::D + 2);
 }
 
 static bool g_attn_ready[64] = {};
@@ -358,20 +393,25 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return -1;
     if (!g_attn_ready[dev] && attn_prepare() != 0) return -1;   // runtimes prepare at creation
+    const size_t prep_n = attn_prep_floats(B, S, H);
+    if (!scratch || scratch_floats < prep_n) return -3;
     // Split the key range over CTAs when (query tiles x heads x images) leaves SMs idle.
     const int qt = (S + fa::BM - 1) / fa::BM, ntiles = (S + fa::BC - 1) / fa::BC;
     const long ctas = (long)qt * H * B;
     int nsplit = 1;
-    if (scratch && scratch_floats >= attn_scratch_floats(B, S, H))
+    if (scratch_floats >= attn_scratch_floats(B, S, H))
         while (nsplit < kAttnMaxSplit && nsplit < ntiles && ctas * (nsplit + 1) <= 2 * 148) nsplit++;
     const int tiles_per = (ntiles + nsplit - 1) / nsplit;
     nsplit = (ntiles + tiles_per - 1) / tiles_per;   // no empty split
     const int R = B * S;
-    float* opart = scratch;
-    float* mlpart = scratch ? scratch + (size_t)nsplit * R * H * fa::D : nullptr;
+    uint8_t* prep = reinterpret_cast<uint8_t*>(scratch);
+    float* opart = scratch + prep_n;
+    float* mlpart = opart + (size_t)nsplit * R * H * fa::D;
+    launch_k(attn_prep, B * H * ntiles, 128, 0, st, qkv, S, H, ntiles, prep);
     dim3 grid(qt, H, B * nsplit);
-    launch_k(flash_attn_tc, grid, 128, fa::SMEM, st, qkv, S, H, scale, out, nsplit, tiles_per, opart, mlpart);
-    g_launch_count += nsplit > 1 ? 2 : 1;
+    launch_k(flash_attn_tc, grid, 256, fa::SMEM, st, (const uint8_t*)prep, S, H, scale, out, nsplit, tiles_per, opart,
+             mlpart);
+    g_launch_count += nsplit > 1 ? 3 : 2;
     if (nsplit > 1 && qo && H * fa::D == 768) {   // merge + quantize in one pass (warp per row)
         launch_k(attn_combine_rows<3>, (R + 3) / 4, 128, 0, st, opart, mlpart, nsplit, R, H, out, *qo, qo_c ? 1 : 0);
         if (quantized) *quantized = true;

@@ -125,8 +125,10 @@ int attn_prepare();
 void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const float* bias, int act,
                      const float* resid, float* y, cudaStream_t st);
 // fp16-K/V flash attention, qkv [B*S][3E] -> out [B*S][E]
-// scratch (optional) holds the key-split partials: attn_scratch_floats() floats.
+// scratch holds the f16 tiles of the prep pass (attn_prep_floats(), required) followed by the
+// key-split partials (splitting is used when scratch_floats >= attn_scratch_floats()).
 constexpr int kAttnMaxSplit = 4;
+size_t attn_prep_floats(int B, int S, int H);
 size_t attn_scratch_floats(int B, int S, int H);
 // qo (optional): when the key range is split, the merge pass also quantizes the output rows
 // into qo (*quantized = true); otherwise the caller quantizes.

@@ -532,8 +532,23 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
     }
 }
 
+// Grow the attention scratch (prep tiles + key-split partials) for B images of S tokens; the
+// captured graphs hold the old pointer, so they are dropped.  Never called inside a capture.
+void ensure_attn_scratch(mgc_runtime* rt, int B, int S) {
+    const size_t need = attn_scratch_floats(B, S, rt->n_head);
+    if (rt->attn_scratch_n >= need) return;
+    CK(cudaStreamSynchronize(rt->st));
+    for (auto& kv : rt->graphs) cudaGraphExecDestroy(kv.second);
+    rt->graphs.clear();
+    cudaFree(rt->attn_scratch);
+    rt->attn_scratch = nullptr;
+    rt->attn_scratch = dalloc<float>(need);
+    rt->attn_scratch_n = need;
+}
+
 // Forward through a cached CUDA graph (captured on the first call for this key).
 void run_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits) {
+    ensure_attn_scratch(rt, B, S);
     if (rt->prof) { enqueue_forward(rt, tokens, B, S, logits, nullptr); return; }
     auto key = std::make_tuple(B, S, (const void*)tokens, (const void*)logits);
     auto it = rt->graphs.find(key);
@@ -723,6 +738,7 @@ int mgc_transformer_forward_dump(mgc_runtime* rt, const int32_t* tokens, int B, 
         if ((int)R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
         const size_t ndump = R * ((size_t)rt->E * (2 * rt->n_layer + 2) + rt->V);
         CK(cudaSetDevice(rt->device));
+        ensure_attn_scratch(rt, B, S);
         float* d_dump = dalloc<float>(ndump);
         try {
             CK(cudaMemcpyAsync(rt->tokens, tokens, sizeof(int32_t) * R, cudaMemcpyHostToDevice, rt->st));
