@@ -23,76 +23,37 @@
 #include "kernels.h"
 #include "ptx.cuh"
 #include "rowquant.cuh"
-#include <cuda_fp16.h>
+#include "attnprep.cuh"
 
 namespace mgc {
 
-namespace fa {
-constexpr int D = 48, BM = 128, BC = 128;
-constexpr uint32_t Q_BYTES = BM * 128;            // [128 rows][64 halves], cols 48..63 unused
-constexpr uint32_t K_BYTES = BC * 128;            // [128 keys][64 halves]
-constexpr uint32_t VT_BLK = D * 128;              // V^T atom block: [48 dims][64 keys]
-constexpr uint32_t VT_BYTES = 2 * VT_BLK;         // keys 0..63 | 64..127
-constexpr uint32_t P_BLK = BM * 128;              // P atom block: [128 rows][64 keys]
-constexpr uint32_t P_BYTES = 2 * P_BLK;
-constexpr uint32_t PREP_ROW = Q_BYTES / BM + K_BYTES / BC + VT_BYTES / BC;   // 352 bytes per row
-constexpr uint32_t OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_V = OFF_K + 2 * K_BYTES,
-                   OFF_PH = OFF_V + 2 * VT_BYTES, OFF_PL = OFF_PH + P_BYTES, OFF_X = OFF_PL + P_BYTES,
-                   OFF_BAR = OFF_X + 4 * BM * 4;
-constexpr uint32_t SMEM = 1024 + OFF_BAR + 128;
-constexpr uint32_t TMEM_COLS = 256;               // S: cols 0..127, O tile: cols 128..175
-constexpr float LOG2E = 1.4426950408889634f;
-}  // namespace fa
-
-// store 8 halves (16 bytes) as logical chunk `c` of row `r` in a 128B-swizzled block
-__device__ __forceinline__ void st_chunk(uint8_t* blk, int r, int c, const __half2 (&h)[4]) {
-    *reinterpret_cast<uint4*>(blk + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
-}
-__device__ __forceinline__ void st_half(uint8_t* blk, int r, int k, __half v) {
-    *reinterpret_cast<__half*>(blk + sw128_off(r, k * 2)) = v;
-}
-
-// prep layout per (image b, head h), nt = ceil(S/128) tiles: [nt x Q tile][nt x K tile][nt x V^T tile]
-__device__ __forceinline__ uint8_t* prep_base(uint8_t* prep, int b, int h, int H, int nt) {
-    return prep + ((size_t)b * H + h) * nt * (size_t)(128 * fa::PREP_ROW);
-}
-
+// Standalone prep pass: block = 128 positions of one (image, head, part), thread = one position.
+// Padding positions (s >= S) are written as zeros so padded keys stay finite in P.V.
 __global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, int S, int H, int nt,
                                                  uint8_t* __restrict__ prep) {
     griddep_wait();
     griddep_launch();
     using namespace fa;
-    const int t = blockIdx.x % nt, h = (blockIdx.x / nt) % H, b = blockIdx.x / (nt * H);
-    const int r = threadIdx.x, s = t * BM + r, E = H * D, W = 3 * E;
-    uint8_t* base = prep_base(prep, b, h, H, nt);
-    uint8_t* qt = base + (size_t)t * Q_BYTES;
-    uint8_t* kt = base + (size_t)nt * Q_BYTES + (size_t)t * K_BYTES;
-    uint8_t* vt = base + (size_t)nt * (Q_BYTES + K_BYTES) + (size_t)t * VT_BYTES + (r >> 6) * VT_BLK;
-    const float* src = qkv + ((size_t)b * S + s) * W + h * D;
+    int x = blockIdx.x;
+    const int part = x % 3; x /= 3;
+    const int t = x % nt; x /= nt;
+    const int h = x % H, b = x / H;
+    const int s = t * BM + threadIdx.x, E = H * D;
+    const float* src = qkv + ((size_t)b * S + s) * (3 * E) + part * E + h * D;
 #pragma unroll
-    for (int c = 0; c < D / 8; c++) {
-        __half2 hq[4], hk[4];
-        float v8[8];
+    for (int j = 0; j < D / 16; j++) {
+        float v[16];
         if (s < S) {
-            const float4 q0 = *reinterpret_cast<const float4*>(src + 8 * c), q1 = *reinterpret_cast<const float4*>(src + 8 * c + 4);
-            const float4 k0 = *reinterpret_cast<const float4*>(src + E + 8 * c), k1 = *reinterpret_cast<const float4*>(src + E + 8 * c + 4);
-            const float4 a0 = *reinterpret_cast<const float4*>(src + 2 * E + 8 * c), a1 = *reinterpret_cast<const float4*>(src + 2 * E + 8 * c + 4);
-            hq[0] = __floats2half2_rn(q0.x, q0.y); hq[1] = __floats2half2_rn(q0.z, q0.w);
-            hq[2] = __floats2half2_rn(q1.x, q1.y); hq[3] = __floats2half2_rn(q1.z, q1.w);
-            hk[0] = __floats2half2_rn(k0.x, k0.y); hk[1] = __floats2half2_rn(k0.z, k0.w);
-            hk[2] = __floats2half2_rn(k1.x, k1.y); hk[3] = __floats2half2_rn(k1.z, k1.w);
-            v8[0] = a0.x; v8[1] = a0.y; v8[2] = a0.z; v8[3] = a0.w;
-            v8[4] = a1.x; v8[5] = a1.y; v8[6] = a1.z; v8[7] = a1.w;
-        } else {   // padding keys / queries: zeros (masked in the softmax, finite in P.V)
-            hq[0] = hq[1] = hq[2] = hq[3] = __floats2half2_rn(0.f, 0.f);
-            hk[0] = hk[1] = hk[2] = hk[3] = hq[0];
 #pragma unroll
-            for (int i = 0; i < 8; i++) v8[i] = 0.f;
+            for (int i = 0; i < 4; i++) {
+                const float4 f = __ldg(reinterpret_cast<const float4*>(src + 16 * j + 4 * i));
+                v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = 0.0f;
         }
-        st_chunk(qt, r, c, hq);
-        st_chunk(kt, r, c, hk);
-#pragma unroll
-        for (int i = 0; i < 8; i++) st_half(vt, c * 8 + i, r & 63, __float2half_rn(v8[i]));
+        prep_store16_at(prep, H, nt, b, s, h, part, 16 * j, v);
     }
 }
 
@@ -370,6 +331,11 @@ size_t attn_prep_floats(int B, int S, int H) {
     return (size_t)B * H * nt * 128 * fa::PREP_ROW / 4;
 }
 
+AttnPrepOut attn_prep_out(float* scratch, int B, int S, int H) {
+    (void)B;
+    return AttnPrepOut{reinterpret_cast<uint8_t*>(scratch), S, H, (S + fa::BC - 1) / fa::BC};
+}
+
 size_t attn_scratch_floats(int B, int S, int H) {
     return attn_prep_floats(B, S, H) + (size_t)kAttnMaxSplit * B * S * H * (fa::D + 2);
 }
@@ -386,7 +352,8 @@ int attn_prepare() {
 }
 
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
-                      size_t scratch_floats, cudaStream_t st, const ActQ* qo, bool qo_c, bool* quantized) {
+                      size_t scratch_floats, cudaStream_t st, const ActQ* qo, bool qo_c, bool* quantized,
+                      bool prepped) {
     if (quantized) *quantized = false;
     if (Dh != fa::D) return -2;
     int dev = 0;
@@ -407,11 +374,11 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     uint8_t* prep = reinterpret_cast<uint8_t*>(scratch);
     float* opart = scratch + prep_n;
     float* mlpart = opart + (size_t)nsplit * R * H * fa::D;
-    launch_k(attn_prep, B * H * ntiles, 128, 0, st, qkv, S, H, ntiles, prep);
+    if (!prepped) launch_k(attn_prep, B * H * ntiles * 3, 128, 0, st, qkv, S, H, ntiles, prep);
     dim3 grid(qt, H, B * nsplit);
     launch_k(flash_attn_tc, grid, 256, fa::SMEM, st, (const uint8_t*)prep, S, H, scale, out, nsplit, tiles_per, opart,
              mlpart);
-    g_launch_count += nsplit > 1 ? 3 : 2;
+    g_launch_count += (nsplit > 1 ? 2 : 1) + (prepped ? 0 : 1);
     if (nsplit > 1 && qo && H * fa::D == 768) {   // merge + quantize in one pass (warp per row)
         launch_k(attn_combine_rows<3>, (R + 3) / 4, 128, 0, st, opart, mlpart, nsplit, R, H, out, *qo, qo_c ? 1 : 0);
         if (quantized) *quantized = true;

@@ -115,9 +115,11 @@ struct SplitK {
 // int8-dot GEMM on tcgen05: y = act(W . x + bias) + resid.  sk == nullptr: no split-K.
 // qo != nullptr: also quantize y into qo (the quantizer of the next linear layer, bit-identical
 // to launch_quant_act_tiled on y; qo_c: write the Q4_K term); y may then be null.
+// destination of the attention prep tiles (f16 Q/K/V of B = M/S images, H heads, nt = ceil(S/128))
+struct AttnPrepOut { uint8_t* buf; int S, H, nt; };
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
                  const float* resid, float* y, cudaStream_t st, const SplitK* sk = nullptr,
-                 const ActQ* qo = nullptr, bool qo_c = false);
+                 const ActQ* qo = nullptr, bool qo_c = false, const AttnPrepOut* ap = nullptr);
 // set the kernels' shared-memory limits on the current device (once per device)
 int qgemm_prepare();
 int attn_prepare();
@@ -134,7 +136,10 @@ size_t attn_scratch_floats(int B, int S, int H);
 // into qo (*quantized = true); otherwise the caller quantizes.
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
                       size_t scratch_floats, cudaStream_t st, const ActQ* qo = nullptr, bool qo_c = false,
-                      bool* quantized = nullptr);
+                      bool* quantized = nullptr, bool prepped = false);
+// where launch_flash_attn expects the prep tiles inside `scratch` (fill them with a fused
+// QKV-GEMM epilogue, then launch with prepped = true)
+AttnPrepOut attn_prep_out(float* scratch, int B, int S, int H);
 
 }  // namespace mgc
 

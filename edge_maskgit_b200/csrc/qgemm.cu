@@ -20,6 +20,7 @@
 //                fused bias / activation / residual epilogue.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "attnprep.cuh"
 
 #include <cstdio>
 #include <cstdlib>
@@ -47,6 +48,8 @@ struct QGemmArgs {
     // fused output quantizer (optional): quantize y per 32-block into ActQ tiles qo (the next
     // layer's activation); y may then be null.  Needs CW == 16 and BN % 32 == 0.
     int8_t* qo; int qo_Mpad; int qo_c;
+    // fused attention prep (optional): also store y as the f16 Q/K/V tiles of attnprep.cuh
+    uint8_t* ap; int ap_S, ap_H, ap_nt;
 };
 
 // Packed f32x2 arithmetic (sm_100): each lane is an IEEE round-to-nearest op, bit-identical
@@ -400,6 +403,7 @@ qgemm_kernel(const QGemmArgs p) {
             for (int c = 0; c < CW; c++) vals[c] = 0.0f;
         }
         if constexpr (CW == 16) {
+            if (p.ap && store) prep_store16(p.ap, p.ap_S, p.ap_H, p.ap_nt, m, nbase, vals);
             if (p.qo) {
                 // The 32-block of columns [32k, 32k+32) is split between this warp (16 columns) and
                 // the warp of the neighbouring column group (same rows): exchange amax and sum.
@@ -514,8 +518,10 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, int& bn, int& cg) {
 }
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
-                 const float* resid, float* y, cudaStream_t st, const SplitK* sk, const ActQ* qo, bool qo_c) {
+                 const float* resid, float* y, cudaStream_t st, const SplitK* sk, const ActQ* qo, bool qo_c,
+                 const AttnPrepOut* ap) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
+    if (ap && (w.N != 3 * ap->H * fa::D || M % ap->S != 0)) return -2;
     if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
     int bn, cg;
     pick_cfg(M, w.N, w.K, qo != nullptr, bn, cg);
@@ -533,7 +539,8 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     nsplit = (nkc + cps - 1) / cps;   // no empty split
     QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
                 sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps,
-                qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0};
+                qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
+                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1};
     const bool q4 = w.wtype == 12;
 #define X(BN, CG) \
     if (bn == BN && cg == CG) return q4 ? run_qgemm<BN, CG, true>(p, st) : run_qgemm<BN, CG, false>(p, st);

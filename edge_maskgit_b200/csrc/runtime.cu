@@ -487,12 +487,22 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
     const float scale = 1.0f / std::sqrt((float)rt->Dh);
     for (int l = 0; l < rt->n_layer; l++) {
         const LayerW& L = rt->layers[l];
-        op(mm, [&] { linear(rt, L.qkv, rt->x, rt->aE, R, L.bqkv, 0, nullptr, rt->qkv); });
+        // the QKV epilogue writes the attention's f16 Q/K/V tiles directly (no f32 qkv round trip)
+        const bool fprep = rt->fuse && L.qkv.wtype != 0;
+        if (fprep) {
+            op(mm, [&] {
+                const AttnPrepOut ap = attn_prep_out(rt->attn_scratch, B, S, rt->n_head);
+                if (launch_qgemm(L.qkv, rt->aE, R, L.bqkv, 0, nullptr, nullptr, st, &rt->sk, nullptr, false, &ap) != 0)
+                    throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+            });
+        } else {
+            op(mm, [&] { linear(rt, L.qkv, rt->x, rt->aE, R, L.bqkv, 0, nullptr, rt->qkv); });
+        }
         bool att_quantized = false;
         op("FlashAttention", [&] {
             const bool fq = rt->fuse && L.o.wtype != 0;
             if (launch_flash_attn(rt->qkv, B, S, rt->n_head, rt->Dh, scale, rt->att, rt->attn_scratch,
-                                  rt->attn_scratch_n, st, fq ? &rt->aE : nullptr, qc, &att_quantized) != 0)
+                                  rt->attn_scratch_n, st, fq ? &rt->aE : nullptr, qc, &att_quantized, fprep) != 0)
                 throw Err("flash attention launch failed");
         });
         if (L.o.wtype != 0 && !att_quantized)
@@ -543,6 +553,7 @@ void ensure_attn_scratch(mgc_runtime* rt, int B, int S) {
     cudaFree(rt->attn_scratch);
     rt->attn_scratch = nullptr;
     rt->attn_scratch = dalloc<float>(need);
+    CK(cudaMemset(rt->attn_scratch, 0, need * sizeof(float)));   // padded keys of the prep tiles stay finite
     rt->attn_scratch_n = need;
 }
 
@@ -674,6 +685,7 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->sk = alloc_splitk(rt->Mpad, std::max(3 * E, F));
         rt->attn_scratch_n = attn_scratch_floats(1, rt->Mpad, rt->n_head);
         rt->attn_scratch = dalloc<float>(rt->attn_scratch_n);
+        CK(cudaMemset(rt->attn_scratch, 0, rt->attn_scratch_n * sizeof(float)));
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
         CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
         CK(cudaDeviceSynchronize());
