@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, 
 #pragma unroll
             for (int i = 0; i < 16; i++) v[i] = 0.0f;
         }
-        prep_store16_at(prep, H, nt, b, s, h, part, 16 * j, v);
+        prep_store_at<16>(prep, H, nt, b, s, h, part, 16 * j, v);
     }
 }
 

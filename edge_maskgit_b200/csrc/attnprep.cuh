@@ -36,18 +36,19 @@ __device__ __forceinline__ uint8_t* prep_base(uint8_t* prep, int b, int h, int H
     return prep + ((size_t)b * H + h) * nt * (size_t)(128 * fa::PREP_ROW);
 }
 
-// Store 16 columns [n, n+16) (n % 16 == 0) of QKV row m (= b*S + s) as f16 into the prep tiles.
-// 16 columns never straddle a head (48 = 3 x 16) nor the q | k | v boundary (E = 48 H).
-// (prep_store16_at addresses by image b, position s, head h, part 0/1/2 = q/k/v, dim d0.)
-__device__ __forceinline__ void prep_store16_at(uint8_t* prep, int H, int nt, int b, int s, int h, int part, int d0,
-                                                const float* v) {
+// Store NC (8 or 16) columns [n, n+NC) (n % NC == 0) of QKV row (image b, position s) as f16
+// into the prep tiles: part 0/1/2 = q/k/v, head h, first dim d0.  NC columns never straddle a
+// head (48 = 3 x 16 = 6 x 8) nor the q | k | v boundary (E = 48 H).
+template <int NC>
+__device__ __forceinline__ void prep_store_at(uint8_t* prep, int H, int nt, int b, int s, int h, int part, int d0,
+                                              const float* v) {
     using namespace fa;
     const int t = s >> 7, r = s & 127;
     uint8_t* base = prep_base(prep, b, h, H, nt);
     if (part < 2) {
         uint8_t* blk = base + (part == 0 ? (size_t)t * Q_BYTES : (size_t)nt * Q_BYTES + (size_t)t * K_BYTES);
 #pragma unroll
-        for (int c = 0; c < 2; c++) {
+        for (int c = 0; c < NC / 8; c++) {
             __half2 hh[4];
 #pragma unroll
             for (int u = 0; u < 4; u++) hh[u] = __floats2half2_rn(v[8 * c + 2 * u], v[8 * c + 2 * u + 1]);
@@ -56,13 +57,15 @@ __device__ __forceinline__ void prep_store16_at(uint8_t* prep, int H, int nt, in
     } else {
         uint8_t* blk = base + (size_t)nt * (Q_BYTES + K_BYTES) + (size_t)t * VT_BYTES + (r >> 6) * VT_BLK;
 #pragma unroll
-        for (int i = 0; i < 16; i++) st_half(blk, d0 + i, r & 63, __float2half_rn(v[i]));
+        for (int i = 0; i < NC; i++) st_half(blk, d0 + i, r & 63, __float2half_rn(v[i]));
     }
 }
-__device__ __forceinline__ void prep_store16(uint8_t* prep, int S, int H, int nt, int m, int n, const float* v) {
+// the same for QKV row m = b * S + s and column n
+template <int NC>
+__device__ __forceinline__ void prep_store(uint8_t* prep, int S, int H, int nt, int m, int n, const float* v) {
     const int E = H * fa::D, part = n / E, rem = n - part * E, h = rem / fa::D, d0 = rem - h * fa::D;
     const int b = m / S, s = m - b * S;
-    prep_store16_at(prep, H, nt, b, s, h, part, d0, v);
+    prep_store_at<NC>(prep, H, nt, b, s, h, part, d0, v);
 }
 
 }  // namespace mgc

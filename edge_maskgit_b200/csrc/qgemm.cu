@@ -94,41 +94,45 @@ __device__ __forceinline__ void trace(const QGemmArgs& p, int idx, long long t0)
 #define TRACE(i) ((void)0)
 #endif
 
-template <int BN, int CG, bool Q4K>
+template <int BN, int CG, bool Q4K, int CB>
 struct QGemmCfg {
-    // NGRP: TMEM ring of 4-block groups (4 * BN columns each) within 512 columns
+    // CB: 32-blocks per pipeline chunk (4 or 8); a chunk is SUB = CB/4 activation tiles of 128 K
     static constexpr int NPW = 4 * CG, CW = BN / CG;
-    // TMEM ring of 4-block groups (4 * BN columns each), at most 256 columns so two CTAs
-    // can share an SM
-#ifdef MGC_NGRP
-    static constexpr int NGRP = MGC_NGRP;
+    // NGRP: TMEM ring of chunk groups (CB * BN columns each), at most 256 columns by default
+    static constexpr int SUB = CB / 4;
+#ifdef MGC_NGRP   // upper bound; the ring never exceeds the 512 TMEM columns
+    static constexpr int NGRP = MGC_NGRP * CB * BN <= 512 ? MGC_NGRP : 512 / (CB * BN);
 #else
-    static constexpr int NGRP = 256 / (4 * BN) >= 2 ? 2 : 1;
+    static constexpr int NGRP = (CB == 4 ? 256 : 512) / (CB * BN) >= 2 ? 2 : 1;
 #endif
+    static constexpr int THREADS = 64 + 32 * NPW;
+    // stage = [SUB activation tiles: codes | dx | (dx*sumx)] [SUB weight code tiles] [SUB scale tiles]
+    static constexpr uint32_t T = Q4K ? 2 : 1;
+    static constexpr uint32_t A_BYTES = Q4K ? 20480 : 18432, B_BYTES = BN * 128, S_BYTES = BN * 16 * T;
+    static constexpr uint32_t OFF_DX = 16384, OFF_CX = 18432, OFF_B = SUB * A_BYTES, OFF_S = OFF_B + SUB * B_BYTES,
+                              STAGE = (OFF_S + SUB * S_BYTES + 1023) & ~1023u;
+    static constexpr uint32_t TX_BYTES = SUB * (A_BYTES + B_BYTES + S_BYTES);
 #ifdef MGC_NST
     static constexpr int NST = MGC_NST;
 #else
-    static constexpr int NST = BN <= 32 ? 8 : BN <= 64 ? 6 : 4;   // ~190 KB ring: deeper measured faster
+    // ~190 KB ring for 4-block chunks (deeper measured faster); 8-block chunks fill what fits
+    static constexpr int NST = CB == 4 ? (BN <= 32 ? 8 : BN <= 64 ? 6 : 4)
+                                       : ((225u * 1024u - 2048u) / STAGE > 8 ? 8 : (225u * 1024u - 2048u) / STAGE);
 #endif
-    static constexpr int THREADS = 64 + 32 * NPW;
-    // stage = [activation tile: codes | dx | (dx*sumx)] [weight codes] [scale tile]
-    static constexpr uint32_t T = Q4K ? 2 : 1;
-    static constexpr uint32_t A_BYTES = Q4K ? 20480 : 18432, B_BYTES = BN * 128, S_BYTES = BN * 16 * T;
-    static constexpr uint32_t OFF_DX = 16384, OFF_CX = 18432, OFF_B = A_BYTES, OFF_S = OFF_B + B_BYTES,
-                              STAGE = (OFF_S + S_BYTES + 1023) & ~1023u;
-    static constexpr uint32_t TX_BYTES = A_BYTES + B_BYTES + S_BYTES;
     static constexpr uint32_t XCHG = NST * STAGE + 256;   // epilogue exchange: [2][NPW][32] f32
     static constexpr uint32_t SMEM = 1024 + XCHG + 2 * NPW * 32 * 4;
     // allocation is a power of two >= 32 columns
-    static constexpr uint32_t TMEM_NEED = 4 * BN * NGRP,
+    static constexpr uint32_t TMEM_NEED = CB * BN * NGRP,
                               TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                         : TMEM_NEED <= 256 ? 256 : 512;
+    static_assert(NGRP >= 1 && TMEM_NEED <= 512, "TMEM ring exceeds 512 columns");
 };
 
-template <int BN, int CG, bool Q4K>
-__global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K>::THREADS, MGC_QGEMM_MINB)
+template <int BN, int CG, bool Q4K, int CB>
+__global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K, CB>::THREADS, MGC_QGEMM_MINB)
 qgemm_kernel(const QGemmArgs p) {
-    using C = QGemmCfg<BN, CG, Q4K>;
+    using C = QGemmCfg<BN, CG, Q4K, CB>;
+    constexpr int SUB = C::SUB;
     // int32 dot values per TMEM batch: 64 registers, 32 when the CTA is too wide for that
     constexpr int IREGS = C::THREADS > 448 ? 32 : MGC_QGEMM_IREGS;
     constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= IREGS ? 1 : IREGS / CW > 4 ? 4 : IREGS / CW;
@@ -147,7 +151,7 @@ qgemm_kernel(const QGemmArgs p) {
     const long long t_start = clock64();
     long long g_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g_start));
 #endif
-    const int nkc = p.K / 128;
+    const int nkc = p.K / (32 * CB);
     const int kz = blockIdx.z, kc0 = kz * p.cps, nloc = max(0, min(nkc, kc0 + p.cps) - kc0);
 
     if (threadIdx.x == 0) {
@@ -174,9 +178,15 @@ qgemm_kernel(const QGemmArgs p) {
                 TRACE(i);
                 // three copies per chunk: activation tile (+ its scales), weight codes, weight scales
                 mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
-                bulk_g2s(st, p.aq + ((size_t)kc * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES, &full[s]);
-                bulk_g2s(st + C::OFF_B, p.wq + ((size_t)kc * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
-                bulk_g2s(st + C::OFF_S, p.ws + ((size_t)kc * (p.Npad / 4) + n0 / 4) * 16 * C::T, C::S_BYTES, &full[s]);
+#pragma unroll
+                for (int u = 0; u < SUB; u++) {
+                    const size_t kk = (size_t)kc * SUB + u;   // 128-K activation tile index
+                    bulk_g2s(st + u * C::A_BYTES, p.aq + (kk * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES,
+                             &full[s]);
+                    bulk_g2s(st + C::OFF_B + u * C::B_BYTES, p.wq + (kk * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
+                    bulk_g2s(st + C::OFF_S + u * C::S_BYTES, p.ws + (kk * (p.Npad / 4) + n0 / 4) * 16 * C::T,
+                             C::S_BYTES, &full[s]);
+                }
                 last_it[s] = it;
             }
             if (*abort_flag) {   // let copies already in flight land before the CTA exits
@@ -197,9 +207,10 @@ qgemm_kernel(const QGemmArgs p) {
                 const uint32_t a_base = smem_u32(smem + s * C::STAGE), b_base = a_base + C::OFF_B;
                 // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    mma_i8(tmem + (g * 4 + j) * BN, sdesc_sw128(a_base + 32 * j), sdesc_sw128(b_base + 32 * j),
-                           idesc, 0);
+                for (int j = 0; j < CB; j++) {
+                    const uint32_t u = j / 4, jj = j % 4;
+                    mma_i8(tmem + (g * CB + j) * BN, sdesc_sw128(a_base + u * C::A_BYTES + 32 * jj),
+                           sdesc_sw128(b_base + u * C::B_BYTES + 32 * jj), idesc, 0);
                 }
                 mma_commit(&tfull[g]);   // the chunk's 4 dot tiles are ready
                 mma_commit(&empty[s]);   // its shared-memory operands may be overwritten
@@ -217,7 +228,7 @@ qgemm_kernel(const QGemmArgs p) {
         // Work unit = a batch of BATCH blocks (BATCH*CW int32 per thread, one TMEM-load wait
         // per batch); BPC batches per 4-block chunk.  (Overlapping batch t+1's loads with batch
         // t's math measured slower: it forces smaller batches, and the waits dominate.)
-        constexpr int BPC = 4 / BATCH;
+        constexpr int BPC = CB / BATCH;
         const int nbatch = nloc * BPC;   // chunk indices below are local to this K split
         bool ok = true;
         // wait for a chunk's operands + dot tiles, then issue the batch's TMEM loads
@@ -234,13 +245,16 @@ qgemm_kernel(const QGemmArgs p) {
             }
 #pragma unroll
             for (int jj = 0; jj < BATCH; jj++) {
-                const uint32_t ta = t_lane + (g * 4 + jb * BATCH + jj) * BN;
+                const uint32_t ta = t_lane + (g * CB + jb * BATCH + jj) * BN;
                 if constexpr (CW % 32 == 0) {
 #pragma unroll
                     for (int u = 0; u < CW / 32; u++)
                         tmem_ld32(ta + u * 32, *reinterpret_cast<uint32_t(*)[32]>(&I[jj][u * 32]));
-                } else {
+                } else if constexpr (CW == 16) {
                     tmem_ld16(ta, I[jj]);
+                } else {
+                    static_assert(CW == 8, "promotion warps own 8, 16 or a multiple of 32 columns");
+                    tmem_ld8(ta, I[jj]);
                 }
             }
         };
@@ -260,21 +274,23 @@ qgemm_kernel(const QGemmArgs p) {
         };
         auto promote = [&](const uint32_t (&I)[BATCH][CW], int t) {
             const int kc = t / BPC, jb = t % BPC, s = kc % NST;
+            // this batch's blocks lie in one 128-K tile u of the chunk (BATCH divides 4)
+            const int u = (jb * BATCH) / 4;
             const uint8_t* st = smem + s * C::STAGE;
             if (active) {
-                const float4 dxv = reinterpret_cast<const float4*>(st + C::OFF_DX)[row];
+                const float4 dxv = reinterpret_cast<const float4*>(st + u * C::A_BYTES + C::OFF_DX)[row];
                 const float dxa[4] = {dxv.x, dxv.y, dxv.z, dxv.w};
                 float cxa[4] = {0, 0, 0, 0};
                 if constexpr (Q4K) {
-                    const float4 cxv = reinterpret_cast<const float4*>(st + C::OFF_CX)[row];
+                    const float4 cxv = reinterpret_cast<const float4*>(st + u * C::A_BYTES + C::OFF_CX)[row];
                     cxa[0] = cxv.x; cxa[1] = cxv.y; cxa[2] = cxv.z; cxa[3] = cxv.w;
                 }
 #pragma unroll
                 for (int jj = 0; jj < BATCH; jj++) {   // blocks in ascending order: b = 4 kc + j
-                    const int j = jb * BATCH + jj;
+                    const int j = (jb * BATCH + jj) % 4;
                     const uint64_t dx2 = pack2(dxa[j], dxa[j]);
                     // scale tile: [BN/4 column quads][T][4 blocks][4 columns]
-                    const float* sq = reinterpret_cast<const float*>(st + C::OFF_S) + (c0 / 4) * 16 * C::T + j * 4;
+                    const float* sq = reinterpret_cast<const float*>(st + C::OFF_S + u * C::S_BYTES) + (c0 / 4) * 16 * C::T + j * 4;
 #pragma unroll
                     for (int c = 0; c < CW; c += 4) {
                         const float4 w4 = *reinterpret_cast<const float4*>(sq + (c / 4) * 16 * C::T);
@@ -402,8 +418,10 @@ qgemm_kernel(const QGemmArgs p) {
 #pragma unroll
             for (int c = 0; c < CW; c++) vals[c] = 0.0f;
         }
+        if constexpr (CW == 8 || CW == 16) {
+            if (p.ap && store) prep_store<CW>(p.ap, p.ap_S, p.ap_H, p.ap_nt, m, nbase, vals);
+        }
         if constexpr (CW == 16) {
-            if (p.ap && store) prep_store16(p.ap, p.ap_S, p.ap_H, p.ap_nt, m, nbase, vals);
             if (p.qo) {
                 // The 32-block of columns [32k, 32k+32) is split between this warp (16 columns) and
                 // the warp of the neighbouring column group (same rows): exchange amax and sum.
@@ -462,50 +480,62 @@ done:
     }
 }
 
-template <int BN, int CG, bool Q4K>
+template <int BN, int CG, bool Q4K, int CB>
 static int set_smem_attr() {
-    using C = QGemmCfg<BN, CG, Q4K>;
-    return cudaFuncSetAttribute(qgemm_kernel<BN, CG, Q4K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    using C = QGemmCfg<BN, CG, Q4K, CB>;
+    return cudaFuncSetAttribute(qgemm_kernel<BN, CG, Q4K, CB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 C::SMEM) == cudaSuccess ? 0 : -1;
 }
 
 // Sets the dynamic shared-memory limit of every instantiation on the current device.  Must
 // run once per device before the first launch (the runtime does it at creation, outside any
 // stream capture).
-#define MGC_QGEMM_CONFIGS(X) X(16, 1) X(32, 1) X(32, 2) X(48, 3) X(64, 2) X(64, 4)
+// (BN, CG, CB): tile width, column groups, 32-blocks per pipeline chunk
+#define MGC_QGEMM_CONFIGS(X) X(16, 1, 4) X(16, 1, 8) X(16, 2, 4) X(16, 2, 8) X(32, 1, 4) X(32, 2, 4) X(32, 2, 8) X(32, 4, 4) X(32, 4, 8) X(48, 3, 4) \
+    X(48, 6, 4) \
+    X(64, 2, 4) X(64, 4, 4)
 
 int qgemm_prepare() {
     int rc = 0;
-#define X(BN, CG) rc |= set_smem_attr<BN, CG, false>(); rc |= set_smem_attr<BN, CG, true>();
+#define X(BN, CG, CB) rc |= set_smem_attr<BN, CG, false, CB>(); rc |= set_smem_attr<BN, CG, true, CB>();
     MGC_QGEMM_CONFIGS(X)
 #undef X
     return rc;
 }
 
-template <int BN, int CG, bool Q4K>
+template <int BN, int CG, bool Q4K, int CB>
 static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
     ++g_launch_count;
-    using C = QGemmCfg<BN, CG, Q4K>;
+    using C = QGemmCfg<BN, CG, Q4K, CB>;
     dim3 grid((a.N + BN - 1) / BN, (a.M + 127) / 128, a.nsplit);
-    launch_k(qgemm_kernel<BN, CG, Q4K>, grid, C::THREADS, C::SMEM, st, a);
+    launch_k(qgemm_kernel<BN, CG, Q4K, CB>, grid, C::THREADS, C::SMEM, st, a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
-// Tile shape (BN columns, CG column groups of promotion warps).  MGC_QGEMM_CFG="BN,CG"
-// overrides the heuristic (used to sweep shapes).
-static void pick_cfg(int M, int N, int K, bool fused_quant, int& bn, int& cg) {
-    static int fbn = -1, fcg = 0;
+// Tile shape (BN columns, CG column groups of promotion warps, CB 32-blocks per chunk).
+// MGC_QGEMM_CFG="BN,CG[,CB]" overrides the heuristic (used to sweep shapes); MGC_QGEMM_CB=4
+// keeps 4-block chunks everywhere.
+static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, int& cg, int& cb) {
+    static int fbn = -1, fcg = 0, fcb = 0, cb_max = 8;
     if (fbn < 0) {
         fbn = 0;
-        if (const char* e = std::getenv("MGC_QGEMM_CFG")) std::sscanf(e, "%d,%d", &fbn, &fcg);
+        if (const char* e = std::getenv("MGC_QGEMM_CFG")) std::sscanf(e, "%d,%d,%d", &fbn, &fcg, &fcb);
+        if (const char* e = std::getenv("MGC_QGEMM_CB")) cb_max = std::atoi(e) == 4 ? 4 : 8;
     }
-    if (fbn && (!fused_quant || (fbn % 32 == 0 && fbn / fcg == 16))) { bn = fbn; cg = fcg; return; }
-    (void)K;
-    // 16 columns per promotion warp; pick the width whose tile grid fills the 148 SMs in the
-    // fewest waves, weighing a wave by its per-CTA work (BN) plus a fixed per-chunk cost (~16
-    // columns' worth).  Widths whose last tile would run past the padded weight rows are skipped.
+    // 8-block chunks (half the pipeline hand-offs per block) where instantiated and K allows
+    auto chunk = [&](int b, int g) { return cb_max == 8 && K % 256 == 0 && (b == 16 || (b == 32 && g >= 2)) ? 8 : 4; };
+    if (fbn && (!fused_quant || (fbn % 32 == 0 && fbn / fcg == 16)) && (!prep || fbn / fcg <= 16)) {
+        bn = fbn; cg = fcg; cb = fcb ? fcb : chunk(bn, cg);
+        return;
+    }
+    // Pick the width whose tile grid fills the 148 SMs in the fewest waves, weighing a wave by
+    // its per-CTA work (BN) plus a fixed per-chunk cost (~16 columns' worth).  Promotion warps
+    // own 8 columns (two warps per SM sub-partition hide each other's latency), 16 where the
+    // epilogue quantizes (a 32-block split over two warps).  Widths whose last tile would run
+    // past the padded weight rows are skipped.
     const int mt = (M + 127) / 128, npad = round_up(N, 128);
-    const int cand[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
+    static const int cand8[4][2] = {{16, 2}, {32, 4}, {48, 6}, {64, 4}}, cand16[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
+    const auto& cand = fused_quant ? cand16 : cand8;
     long best = -1;
     for (const auto& c : cand) {
         const int tiles_n = (N + c[0] - 1) / c[0];
@@ -515,20 +545,22 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, int& bn, int& cg) {
         const long cost = waves * (c[0] + 16);
         if (best < 0 || cost < best) { best = cost; bn = c[0]; cg = c[1]; }
     }
+    cb = chunk(bn, cg);
 }
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
                  const float* resid, float* y, cudaStream_t st, const SplitK* sk, const ActQ* qo, bool qo_c,
                  const AttnPrepOut* ap) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
+    int bn, cg, cb;
+    pick_cfg(M, w.N, w.K, qo != nullptr, ap != nullptr, bn, cg, cb);
+    if (w.K % (32 * cb) != 0) return -2;
     if (ap && (w.N != 3 * ap->H * fa::D || M % ap->S != 0)) return -2;
     if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
-    int bn, cg;
-    pick_cfg(M, w.N, w.K, qo != nullptr, bn, cg);
     // Split-K (MGC_QGEMM_SPLITK=<n>) is off by default: on the config-1 shapes it measured
     // slower than one CTA per tile (ncu: attn_o 11 -> 26 us with 3 splits, ffn_down 22 -> 38 us
     // with 4), so the library only splits when asked.
-    const int nkc = w.K / 128, tiles = ((w.N + bn - 1) / bn) * ((M + 127) / 128);
+    const int nkc = w.K / (32 * cb), tiles = ((w.N + bn - 1) / bn) * ((M + 127) / 128);
     int nsplit = 1;
     if (sk && sk->part && sk->counters) {
         if (const char* e = std::getenv("MGC_QGEMM_SPLITK")) nsplit = std::max(1, std::atoi(e));
@@ -542,8 +574,8 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
                 qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
                 ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1};
     const bool q4 = w.wtype == 12;
-#define X(BN, CG) \
-    if (bn == BN && cg == CG) return q4 ? run_qgemm<BN, CG, true>(p, st) : run_qgemm<BN, CG, false>(p, st);
+#define X(BN, CG, CB) \
+    if (bn == BN && cg == CG && cb == CB) return q4 ? run_qgemm<BN, CG, true, CB>(p, st) : run_qgemm<BN, CG, false, CB>(p, st);
     MGC_QGEMM_CONFIGS(X)
 #undef X
     return -2;
