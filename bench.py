@@ -41,29 +41,36 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index, self.rows, self._stop = index, [], threading.Event()
-        self._t = threading.Thread(target=self._run, daemon=True)
+    def __init__(self, index: int, period_ms: int = 50):
+        self.index, self.period_ms, self.rows, self._p = index, period_ms, [], None
+        self._t = threading.Thread(target=self._read, daemon=True)
 
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([c.strip() for c in out.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+    def _read(self):
+        for line in self._p.stdout:
+            cols = [c.strip() for c in line.split(",")]
+            if len(cols) >= 9:
+                self.rows.append(cols)
 
     def __enter__(self):
-        self._t.start()
+        # one nvidia-smi in loop mode for the whole timed region (no per-sample process start)
+        try:
+            self._p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                        "--format=csv,noheader,nounits", f"-lms={self.period_ms}"],
+                                       stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t.start()
+            time.sleep(0.3)   # first sample lands before the timed work starts
+        except OSError:
+            self._p = None
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        self._t.join(timeout=10)
+        if self._p is not None:
+            self._p.terminate()
+            try:
+                self._p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._p.kill()
+            self._t.join(timeout=5)
 
     def summary(self) -> dict:
         if not self.rows:
@@ -338,7 +345,8 @@ def run_tp_workload(args) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 300 for c1, 10 for c5, 20 for the reference arm)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--quant", default="gq8", choices=["gq8", "gq4"])
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
@@ -346,6 +354,8 @@ def main():
     ap.add_argument("--workload", default="c1", choices=["c1", "c5"],
                     help="c1: the headline config-1 step (default); c5: M=4097 tensor-parallel step")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.impl == "reference" else 10 if args.workload == "c5" else 300
     if args.workload == "c5" and args.impl == "cuda":
         run_tp_workload(args)
         return

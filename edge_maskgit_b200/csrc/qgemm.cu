@@ -252,9 +252,11 @@ qgemm_kernel(const QGemmArgs p) {
                         tmem_ld32(ta + u * 32, *reinterpret_cast<uint32_t(*)[32]>(&I[jj][u * 32]));
                 } else if constexpr (CW == 16) {
                     tmem_ld16(ta, I[jj]);
-                } else {
-                    static_assert(CW == 8, "promotion warps own 8, 16 or a multiple of 32 columns");
+                } else if constexpr (CW == 8) {
                     tmem_ld8(ta, I[jj]);
+                } else {
+                    static_assert(CW == 4, "promotion warps own 4, 8, 16 or a multiple of 32 columns");
+                    tmem_ld4(ta, I[jj]);
                 }
             }
         };
@@ -491,7 +493,7 @@ static int set_smem_attr() {
 // run once per device before the first launch (the runtime does it at creation, outside any
 // stream capture).
 // (BN, CG, CB): tile width, column groups, 32-blocks per pipeline chunk
-#define MGC_QGEMM_CONFIGS(X) X(16, 1, 4) X(16, 1, 8) X(16, 2, 4) X(16, 2, 8) X(32, 1, 4) X(32, 2, 4) X(32, 2, 8) X(32, 4, 4) X(32, 4, 8) X(48, 3, 4) \
+#define MGC_QGEMM_CONFIGS(X) X(16, 1, 4) X(16, 1, 8) X(16, 2, 4) X(16, 2, 8) X(16, 4, 4) X(16, 4, 8) X(32, 1, 4) X(32, 2, 4) X(32, 2, 8) X(32, 4, 4) X(32, 4, 8) X(48, 3, 4) \
     X(48, 6, 4) \
     X(64, 2, 4) X(64, 4, 4)
 
@@ -524,7 +526,7 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
     }
     // 8-block chunks (half the pipeline hand-offs per block) where instantiated and K allows
     auto chunk = [&](int b, int g) { return cb_max == 8 && K % 256 == 0 && (b == 16 || (b == 32 && g >= 2)) ? 8 : 4; };
-    if (fbn && (!fused_quant || (fbn % 32 == 0 && fbn / fcg == 16)) && (!prep || fbn / fcg <= 16)) {
+    if (fbn && (!fused_quant || (fbn % 32 == 0 && fbn / fcg == 16)) && (!prep || fbn / fcg == 8 || fbn / fcg == 16)) {
         bn = fbn; cg = fcg; cb = fcb ? fcb : chunk(bn, cg);
         return;
     }
