@@ -200,6 +200,14 @@ template <int NC>
 __device__ __forceinline__ void ln_chunks(float (&v)[NC][8], float* sm, const float* gamma, const float* beta,
                                           float eps, int lane) {
     constexpr int D = NC * 256;
+    // gamma / beta do not depend on the row: their loads overlap the reductions
+    float4 gb[NC][4];
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        const float4* gp = reinterpret_cast<const float4*>(gamma + 256 * i + 8 * lane);
+        const float4* bp = reinterpret_cast<const float4*>(beta + 256 * i + 8 * lane);
+        gb[i][0] = __ldg(gp); gb[i][1] = __ldg(gp + 1); gb[i][2] = __ldg(bp); gb[i][3] = __ldg(bp + 1);
+    }
 #pragma unroll
     for (int i = 0; i < NC; i++) {
         float4* p = reinterpret_cast<float4*>(sm + 256 * i + 8 * lane);
@@ -229,9 +237,7 @@ __device__ __forceinline__ void ln_chunks(float (&v)[NC][8], float* sm, const fl
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(w, (float)D), eps)));
 #pragma unroll
     for (int i = 0; i < NC; i++) {
-        const float4* gp = reinterpret_cast<const float4*>(gamma + 256 * i + 8 * lane);
-        const float4* bp = reinterpret_cast<const float4*>(beta + 256 * i + 8 * lane);
-        const float4 g0 = __ldg(gp), g1 = __ldg(gp + 1), b0 = __ldg(bp), b1 = __ldg(bp + 1);
+        const float4 g0 = gb[i][0], g1 = gb[i][1], b0 = gb[i][2], b1 = gb[i][3];
         const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll

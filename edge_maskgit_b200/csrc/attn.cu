@@ -287,38 +287,51 @@ __global__ void attn_combine(const float* __restrict__ opart, const float* __res
 // Same merge as attn_combine, one warp per row over all heads (row held in chunk layout:
 // lane l owns elements 256 i + 8 l .. +7, which lie in one head since 48 % 8 == 0), followed by
 // the quantizer of the O projection's input.  out may be null (only the quantized row needed).
-template <int NC>
+// NS (the number of key ranges) is a template parameter so every load of a row is issued before
+// the first one is used.
+template <int NC, int NS>
 __global__ void __launch_bounds__(128) attn_combine_rows(const float* __restrict__ opart, const float* __restrict__ mlpart,
-                                                         int nsplit, int R, int H, float* __restrict__ out, ActQ a,
-                                                         int want_c) {
+                                                         int R, int H, float* __restrict__ out, ActQ a, int want_c) {
     griddep_wait();
     griddep_launch();
     const int lane = threadIdx.x & 31, r = blockIdx.x * 4 + (threadIdx.x >> 5);
     if (r >= R) return;
     constexpr int E = NC * 256;
     const float2* ml = reinterpret_cast<const float2*>(mlpart);
+    float2 mls[NC][NS];
+    float4 xs[NC][NS][2];
+#pragma unroll
+    for (int i = 0; i < NC; i++) {
+        const int e0 = 256 * i + 8 * lane, rh = r * H + e0 / fa::D;
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            mls[i][s] = __ldcg(ml + (size_t)s * R * H + rh);
+            const float4* src = reinterpret_cast<const float4*>(opart + ((size_t)s * R + r) * E + e0);
+            xs[i][s][0] = __ldcg(src);
+            xs[i][s][1] = __ldcg(src + 1);
+        }
+    }
     float v[NC][8];
 #pragma unroll
     for (int i = 0; i < NC; i++) {
-        const int e0 = 256 * i + 8 * lane, h = e0 / fa::D, rh = r * H + h;
         float m = -INFINITY;
-        for (int s = 0; s < nsplit; s++) m = fmaxf(m, ml[(size_t)s * R * H + rh].x);
-        float l = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int s = 0; s < nsplit; s++) {
-            const float2 v2 = ml[(size_t)s * R * H + rh];
-            const float wgt = exp2f(v2.x - m);
-            l = __fmaf_rn(v2.y, wgt, l);
-            const float4* src = reinterpret_cast<const float4*>(opart + ((size_t)s * R + r) * E + e0);
-            const float4 x0 = src[0], x1 = src[1];
-            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-            for (int e = 0; e < 8; e++) acc[e] = __fmaf_rn(xs[e], wgt, acc[e]);
+        for (int s = 0; s < NS; s++) m = fmaxf(m, mls[i][s].x);
+        float l = 0.0f, acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            const float wgt = exp2f(mls[i][s].x - m);
+            l = __fmaf_rn(mls[i][s].y, wgt, l);
+            const float x8[8] = {xs[i][s][0].x, xs[i][s][0].y, xs[i][s][0].z, xs[i][s][0].w,
+                                 xs[i][s][1].x, xs[i][s][1].y, xs[i][s][1].z, xs[i][s][1].w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[e] = __fmaf_rn(x8[e], wgt, acc[e]);
         }
         const float inv = __fdiv_rn(1.0f, l);
 #pragma unroll
         for (int e = 0; e < 8; e++) v[i][e] = __fmul_rn(acc[e], inv);
         if (out) {
-            float4* dst = reinterpret_cast<float4*>(out + (size_t)r * E + e0);
+            float4* dst = reinterpret_cast<float4*>(out + (size_t)r * E + 256 * i + 8 * lane);
             dst[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
             dst[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
         }
@@ -380,7 +393,8 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
              mlpart);
     g_launch_count += (nsplit > 1 ? 2 : 1) + (prepped ? 0 : 1);
     if (nsplit > 1 && qo && H * fa::D == 768) {   // merge + quantize in one pass (warp per row)
-        launch_k(attn_combine_rows<3>, (R + 3) / 4, 128, 0, st, opart, mlpart, nsplit, R, H, out, *qo, qo_c ? 1 : 0);
+        auto kern = nsplit == 2 ? attn_combine_rows<3, 2> : nsplit == 3 ? attn_combine_rows<3, 3> : attn_combine_rows<3, 4>;
+        launch_k(kern, (R + 3) / 4, 128, 0, st, opart, mlpart, R, H, out, *qo, qo_c ? 1 : 0);
         if (quantized) *quantized = true;
     } else if (nsplit > 1) launch_k(attn_combine, (R * H * (fa::D / 4) + 255) / 256, 256, 0, st, opart, mlpart, nsplit, R, H, out);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;

@@ -103,7 +103,9 @@ struct QGemmCfg {
 #ifdef MGC_NGRP   // upper bound; the ring never exceeds the 512 TMEM columns
     static constexpr int NGRP = MGC_NGRP * CB * BN <= 512 ? MGC_NGRP : 512 / (CB * BN);
 #else
-    static constexpr int NGRP = (CB == 4 ? 256 : 512) / (CB * BN) >= 2 ? 2 : 1;
+    // (one CTA per SM -- the ring's shared memory allows no more -- so the whole 512 columns
+    // are available; with MGC_QGEMM_MINB=2 each CTA keeps to 256)
+    static constexpr int NGRP = (MGC_QGEMM_MINB == 1 ? 512 : 256) / (CB * BN) >= 2 ? 2 : 1;
 #endif
     static constexpr int THREADS = 64 + 32 * NPW;
     // stage = [SUB activation tiles: codes | dx | (dx*sumx)] [SUB weight code tiles] [SUB scale tiles]
@@ -161,8 +163,9 @@ qgemm_kernel(const QGemmArgs p) {
         mbar_fence_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
-    griddep_wait();   // activations / residual come from the preceding kernel
-    griddep_launch();
+    // With programmatic dependent launch this prologue, and the weight copies of the first
+    // stages (weights do not depend on the preceding kernel), overlap the preceding kernel's
+    // tail: only the activation copies and the epilogue wait for it (griddep_wait below).
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -171,22 +174,45 @@ qgemm_kernel(const QGemmArgs p) {
         if (lane == 0) {
             int last_it[NST];
             for (int s = 0; s < NST; s++) last_it[s] = -1;
-            for (int i = 0; i < nloc; i++) {
-                const int kc = kc0 + i, s = i % NST, it = i / NST;
-                if (!mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1)) break;
+            // three copies per 128-K tile: activation tile (+ its scales), weight codes, weight scales
+            auto copy_w = [&](int i) {
+                const int kc = kc0 + i, s = i % NST;
                 uint8_t* st = smem + s * C::STAGE;
-                TRACE(i);
-                // three copies per chunk: activation tile (+ its scales), weight codes, weight scales
-                mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+#pragma unroll
+                for (int u = 0; u < SUB; u++) {
+                    const size_t kk = (size_t)kc * SUB + u;
+                    bulk_g2s(st + C::OFF_B + u * C::B_BYTES, p.wq + (kk * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
+                    bulk_g2s(st + C::OFF_S + u * C::S_BYTES, p.ws + (kk * (p.Npad / 4) + n0 / 4) * 16 * C::T,
+                             C::S_BYTES, &full[s]);
+                }
+            };
+            auto copy_a = [&](int i) {
+                const int kc = kc0 + i, s = i % NST;
+                uint8_t* st = smem + s * C::STAGE;
 #pragma unroll
                 for (int u = 0; u < SUB; u++) {
                     const size_t kk = (size_t)kc * SUB + u;   // 128-K activation tile index
                     bulk_g2s(st + u * C::A_BYTES, p.aq + (kk * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES,
                              &full[s]);
-                    bulk_g2s(st + C::OFF_B + u * C::B_BYTES, p.wq + (kk * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
-                    bulk_g2s(st + C::OFF_S + u * C::S_BYTES, p.ws + (kk * (p.Npad / 4) + n0 / 4) * 16 * C::T,
-                             C::S_BYTES, &full[s]);
                 }
+            };
+            // the first stages are free: their weights go out before the wait on the preceding kernel
+            const int npre = nloc < NST ? nloc : NST;
+            for (int i = 0; i < npre; i++) {
+                TRACE(i);
+                mbar_arrive_expect_tx(&full[i], C::TX_BYTES);
+                copy_w(i);
+                last_it[i] = 0;
+            }
+            griddep_wait();   // the activation tiles come from the preceding kernel
+            for (int i = 0; i < npre; i++) copy_a(i);
+            for (int i = npre; i < nloc; i++) {
+                const int s = i % NST, it = i / NST;
+                if (!mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1)) break;
+                TRACE(i);
+                mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+                copy_w(i);
+                copy_a(i);
                 last_it[s] = it;
             }
             if (*abort_flag) {   // let copies already in flight land before the CTA exits
@@ -195,6 +221,7 @@ qgemm_kernel(const QGemmArgs p) {
                     if (last_it[s] >= 0) mbar_wait(&full[s], last_it[s] & 1, &never, 11);
             }
         }
+        griddep_launch();   // this CTA's loads are all issued: the next kernel may start its prologue
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_make(2, 1, Q4K ? 0 : 1, 128, BN);
@@ -217,6 +244,7 @@ qgemm_kernel(const QGemmArgs p) {
                 TRACE(256 + kc);
             }
         }
+        griddep_launch();
     } else {
         const int pw = warp - 2, q = warp & 3, cg = pw >> 2;
         const int row = q * 32 + lane, m = m0 + row, c0 = cg * CW;
@@ -329,6 +357,8 @@ qgemm_kernel(const QGemmArgs p) {
             promote(I, t);
         }
         if (lane == 0) TRACE(1800 + warp);
+        griddep_launch();
+        griddep_wait();   // the residual and the output buffers belong to the preceding kernels' chain
         // epilogue: bias -> act -> residual (mg-opencl.cpp:481-493)
         float acc[CW];
 #pragma unroll
