@@ -24,8 +24,9 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
                                                        float* __restrict__ y) {
     griddep_wait();
     griddep_launch();
-    __shared__ __align__(16) float As[GF_BK][GF_BM + 4];   // x slab, As[k][m]
-    __shared__ __align__(16) float Bs[GF_BK][GF_BN + 4];   // w slab, Bs[k][n]
+    // two slab buffers: the next slab's global loads are in flight while this one is consumed
+    __shared__ __align__(16) float As[2][GF_BK][GF_BM + 4];   // x slab, As[k][m]
+    __shared__ __align__(16) float Bs[2][GF_BK][GF_BN + 4];   // w slab, Bs[k][n]
     const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;   // 16 x 16 threads, 4 x 4 each
     const int m0 = blockIdx.y * GF_BM, n0 = blockIdx.x * GF_BN;
     const bool vec = (K % 4) == 0;
@@ -34,16 +35,18 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    for (int k0 = 0; k0 < K; k0 += GF_BK) {
-        // 64 rows x 32 k per operand: 2 float4 per thread, transposed into [k][row]
+    // 64 rows x 32 k per operand: 2 float4 per thread, transposed into [k][row]
+    float4 xa[2], wb[2];
+    auto fetch = [&](int k0) {
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const int l = tid + 256 * h, r = l / 8, kq = (l % 8) * 4, gk = k0 + kq;
-            float4 xa = make_float4(0, 0, 0, 0), wb = make_float4(0, 0, 0, 0);
             const int gm = m0 + r, gn = n0 + r;
+            xa[h] = make_float4(0, 0, 0, 0);
+            wb[h] = make_float4(0, 0, 0, 0);
             if (vec && gk + 3 < K) {
-                if (gm < M) xa = *reinterpret_cast<const float4*>(x + (size_t)gm * K + gk);
-                if (gn < N) wb = *reinterpret_cast<const float4*>(w + (size_t)gn * K + gk);
+                if (gm < M) xa[h] = __ldg(reinterpret_cast<const float4*>(x + (size_t)gm * K + gk));
+                if (gn < N) wb[h] = __ldg(reinterpret_cast<const float4*>(w + (size_t)gn * K + gk));
             } else {
                 float t[4], u[4];
 #pragma unroll
@@ -51,24 +54,34 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
                     t[e] = (gm < M && gk + e < K) ? x[(size_t)gm * K + gk + e] : 0.0f;
                     u[e] = (gn < N && gk + e < K) ? w[(size_t)gn * K + gk + e] : 0.0f;
                 }
-                xa = make_float4(t[0], t[1], t[2], t[3]);
-                wb = make_float4(u[0], u[1], u[2], u[3]);
+                xa[h] = make_float4(t[0], t[1], t[2], t[3]);
+                wb[h] = make_float4(u[0], u[1], u[2], u[3]);
             }
-            As[kq][r] = xa.x; As[kq + 1][r] = xa.y; As[kq + 2][r] = xa.z; As[kq + 3][r] = xa.w;
-            Bs[kq][r] = wb.x; Bs[kq + 1][r] = wb.y; Bs[kq + 2][r] = wb.z; Bs[kq + 3][r] = wb.w;
         }
-        __syncthreads();
+    };
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int l = tid + 256 * h, r = l / 8, kq = (l % 8) * 4;
+            As[buf][kq][r] = xa[h].x; As[buf][kq + 1][r] = xa[h].y; As[buf][kq + 2][r] = xa[h].z; As[buf][kq + 3][r] = xa[h].w;
+            Bs[buf][kq][r] = wb[h].x; Bs[buf][kq + 1][r] = wb[h].y; Bs[buf][kq + 2][r] = wb[h].z; Bs[buf][kq + 3][r] = wb[h].w;
+        }
+    };
+    fetch(0);
+    for (int k0 = 0, buf = 0; k0 < K; k0 += GF_BK, buf ^= 1) {
+        stash(buf);
+        __syncthreads();   // (one barrier per slab: the buffer written next was last read two slabs ago)
+        if (k0 + GF_BK < K) fetch(k0 + GF_BK);
         const int kn = min(GF_BK, K - k0);
         for (int kk = 0; kk < kn; kk++) {   // k ascending: each output is a sequential fma chain
-            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][tm * 4]);
-            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][tn * 4]);
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][kk][tm * 4]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tn * 4]);
             const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(bb[j], a[i], acc[i][j]);
         }
-        __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {
