@@ -116,9 +116,18 @@ __global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__
     float m_i = -INFINITY, l_i = 0.0f;
     bool ok = true;
 
+#ifdef MGC_ATTN_TRACE   // development trace: CTA (0,0,0) records per-tile phase stamps (SM cycles)
+    __shared__ int trc[40 * 8];
+    const long long t_0 = clock64();
+    const bool tr = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && tid == 0;
+#define ATR(k) do { if (tr && i < 40) trc[i * 8 + (k)] = (int)(clock64() - t_0); } while (0)
+#else
+#define ATR(k) ((void)0)
+#endif
     for (int kt = kt0; kt < kt1 && ok; kt++) {
         const int i = kt - kt0, buf = i & 1, ph = i & 1;
         const int kb = kt * BC, nvalid = min(BC, S - kb), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
+        ATR(0);
         if (tid == 0) {
             if (kt + 1 < kt1) load_kv(kt + 1, buf ^ 1);   // that buffer's last reader (tile i-1) is done
             bool w = (i > 0 || mbar_wait(bar_q, 0, abort_flag, 23)) && mbar_wait(bar_kv + buf, (i >> 1) & 1, abort_flag, 24);
@@ -126,14 +135,16 @@ __global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__
                 tc_fence_after();
                 const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
                 const uint32_t sK = smem_u32(sm + OFF_K + buf * K_BYTES);
-                for (int k = 0; k < D / 16; k++)
-                    mma_f16(tmem, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idesc_s, k > 0);
+                const uint64_t dq = sdesc_sw128(sQ), dk = sdesc_sw128(sK);
+#pragma unroll
+                for (int k = 0; k < D / 16; k++) mma_f16(tmem, dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
                 mma_commit(bar_s);
             }
         }
         ok = mbar_wait(bar_s, ph, abort_flag, 21);
         ok = __syncthreads_and(ok);
         if (!ok) break;
+        ATR(1);
         tc_fence_after();
         // ---- softmax over this half's 64 columns
         float alpha = 1.0f;
@@ -144,52 +155,73 @@ __global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__
             for (int cc = 0; cc < 2; cc++)
                 if (2 * half + cc < nch) tmem_ld32(t_row + (2 * half + cc) * 32, r[cc]);
             tmem_ld_wait();
+            ATR(2);
+            // max of the raw scores (4 chains), scaled once: rounding is monotonic, so this is
+            // the max of the scaled scores
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int cc = 0; cc < 2; cc++) {
                 const int ch = 2 * half + cc;
                 if (ch >= nch) break;
 #pragma unroll
                 for (int j = 0; j < 32; j++)
-                    if (ch * 32 + j < nvalid) mloc = fmaxf(mloc, __fmul_rn(__uint_as_float(r[cc][j]), c1));
+                    if (ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
             }
+            mloc = __fmul_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), c1);
         }
         xmax[half * BM + row] = mloc;
         __syncthreads();
+        ATR(3);
         const float m_new = fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row]));
         float lsum = 0.0f;
         if (wact) {
             alpha = exp2f(m_i - m_new);
             uint8_t* pbh = sm + OFF_PH + half * P_BLK;
             uint8_t* pbl = sm + OFF_PL + half * P_BLK;
+            // p = 2^(s*c1 - m) on pairs (one packed FMA, two MUFU ex2), row sum in packed partials,
+            // P_hi = f16(p), P_lo = f16(p - P_hi)
+            const uint64_t c1x2 = pack2(c1, c1), nm2 = pack2(-m_new, -m_new), neg1 = pack2(-1.0f, -1.0f);
+            uint64_t ls2[2] = {0, 0};
 #pragma unroll
             for (int cc = 0; cc < 2; cc++) {
                 const int ch = 2 * half + cc;
                 if (ch >= nch) break;
+                const bool full = ch * 32 + 32 <= nvalid;
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
                     __half2 hh[4], hl[4];
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
-                        float p2[2];
-#pragma unroll
-                        for (int e = 0; e < 2; e++) {
-                            const int j = c * 8 + u * 2 + e;
-                            p2[e] = (ch * 32 + j < nvalid) ? exp2f(__fmul_rn(__uint_as_float(r[cc][j]), c1) - m_new) : 0.0f;
-                            lsum = __fadd_rn(lsum, p2[e]);
+                        const int j = c * 8 + u * 2;
+                        float t0, t1;
+                        unpack2(fma2(pack2(__uint_as_float(r[cc][j]), __uint_as_float(r[cc][j + 1])), c1x2, nm2), t0, t1);
+                        float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+                        if (!full) {
+                            p0 = ch * 32 + j < nvalid ? p0 : 0.0f;
+                            p1 = ch * 32 + j + 1 < nvalid ? p1 : 0.0f;
                         }
-                        hh[u] = __floats2half2_rn(p2[0], p2[1]);
+                        const uint64_t p2 = pack2(p0, p1);
+                        ls2[u & 1] = add2(ls2[u & 1], p2);
+                        hh[u] = __floats2half2_rn(p0, p1);
                         const float2 back = __half22float2(hh[u]);
-                        hl[u] = __floats2half2_rn(p2[0] - back.x, p2[1] - back.y);
+                        float l0, l1;
+                        unpack2(fma2(pack2(back.x, back.y), neg1, p2), l0, l1);
+                        hl[u] = __floats2half2_rn(l0, l1);
                     }
                     st_chunk(pbh, row, cc * 4 + c, hh);
                     st_chunk(pbl, row, cc * 4 + c, hl);
                 }
             }
+            float a0, a1, b0, b1;
+            unpack2(ls2[0], a0, a1);
+            unpack2(ls2[1], b0, b1);
+            lsum = (a0 + b0) + (a1 + b1);
         }
         xsum[half * BM + row] = lsum;
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
+        ATR(4);
         if (wact) {
             l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(xsum[row], xsum[BM + row]));
             m_i = m_new;
@@ -198,19 +230,30 @@ __global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__
         if (tid == 0) {
             tc_fence_after();
             const uint32_t sV = smem_u32(sm + OFF_V + buf * VT_BYTES);
+            // descriptors advance by (byte offset >> 4) in their start-address field (no carry:
+            // shared-memory addresses stay below 2^18)
+            const uint64_t dv = sdesc_sw128(sV);
+#pragma unroll
             for (int part = 0; part < 2; part++) {
-                const uint32_t sP = part == 0 ? sPh : sPl;
-                for (int j = 0; j < nmma / 16; j++) {
-                    const uint32_t pa = sP + (j >> 2) * P_BLK + (j & 3) * 32;
-                    const uint32_t pv = sV + (j >> 2) * VT_BLK + (j & 3) * 32;
-                    mma_f16(tmem + BC, sdesc_sw128(pa), sdesc_sw128(pv), idesc_o, (part | j) != 0);
+                const uint64_t dp = sdesc_sw128(part == 0 ? sPh : sPl);
+                if (nmma == BC) {
+#pragma unroll
+                    for (int j = 0; j < BC / 16; j++)
+                        mma_f16(tmem + BC, dp + (j >> 2) * (P_BLK >> 4) + (j & 3) * 2,
+                                dv + (j >> 2) * (VT_BLK >> 4) + (j & 3) * 2, idesc_o, (part | j) != 0);
+                } else {
+                    for (int j = 0; j < nmma / 16; j++)
+                        mma_f16(tmem + BC, dp + (j >> 2) * (P_BLK >> 4) + (j & 3) * 2,
+                                dv + (j >> 2) * (VT_BLK >> 4) + (j & 3) * 2, idesc_o, (part | j) != 0);
                 }
             }
             mma_commit(bar_o);
+            ATR(5);
         }
         ok = mbar_wait(bar_o, ph, abort_flag, 22);
         ok = __syncthreads_and(ok);
         if (!ok) break;
+        ATR(6);
         tc_fence_after();
         if (wact) {   // this half's 24 output dims
             uint32_t a16[16], a8[8];
@@ -231,6 +274,7 @@ __global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__
         }
         tc_fence_before();
         __syncthreads();   // P and this K/V buffer are rewritten two tiles on
+        ATR(7);
     }
 
     const int qr = q0 + row, d0 = half * (D / 2);
@@ -250,6 +294,10 @@ __global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__
     }
     tc_fence_before();
     __syncthreads();
+#ifdef MGC_ATTN_TRACE
+    if (tr)
+        for (int j = 0; j < 40 * 8; j++) out[(size_t)(j / D) * E + j % D] = (float)trc[j];
+#endif
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, fa::TMEM_COLS);

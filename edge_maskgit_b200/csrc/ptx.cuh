@@ -190,6 +190,29 @@ __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- packed f32x2 arithmetic
+// Packed f32x2 arithmetic (sm_100): each lane is an IEEE round-to-nearest op, bit-identical
+// to the scalar fma / mul / add.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r; asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b)); return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d; asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c)); return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d; asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b)); return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b)); return d;
+}
+// 2^x, MUFU approximation (flush-to-zero; relative error a few ulp)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y; asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x)); return y;
+}
+
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 B, 8-row
 // swizzle atoms of 1024 B (stride byte offset), version 1 (sm_100), layout type 2.
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {

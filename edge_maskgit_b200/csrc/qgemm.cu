@@ -52,23 +52,6 @@ struct QGemmArgs {
     uint8_t* ap; int ap_S, ap_H, ap_nt;
 };
 
-// Packed f32x2 arithmetic (sm_100): each lane is an IEEE round-to-nearest op, bit-identical
-// to the scalar fma / mul / add.
-__device__ __forceinline__ uint64_t pack2(float a, float b) {
-    uint64_t r; asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b)); return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t v, float& a, float& b) {
-    asm("mov.b64 {%0,%1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d; asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c)); return d;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t d; asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b)); return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b)); return d;
-}
 // (-1.5 * 2^23, -1.5 * 2^23): |v| < 2^22 always holds (32 * 127 * 128 < 2^22)
 constexpr uint64_t kMagicNeg2 = 0xCB400000CB400000ull;
 
