@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
         __syncthreads();   // (one barrier per slab: the buffer written next was last read two slabs ago)
         if (k0 + GF_BK < K) fetch(k0 + GF_BK);
         const int kn = min(GF_BK, K - k0);
-        for (int kk = 0; kk < kn; kk++) {   // k ascending: each output is a sequential fma chain
+        auto step = [&](int kk) {   // k ascending: each output is a sequential fma chain
             const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][kk][tm * 4]);
             const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tn * 4]);
             const float a[4] = {a4.x, a4.y, a4.z, a4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
@@ -81,6 +81,12 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
             for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(bb[j], a[i], acc[i][j]);
+        };
+        if (kn == GF_BK) {   // full slab: unrolled so the shared-memory loads run ahead of the FMAs
+#pragma unroll
+            for (int kk = 0; kk < GF_BK; kk++) step(kk);
+        } else {
+            for (int kk = 0; kk < kn; kk++) step(kk);
         }
     }
 #pragma unroll

@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <condition_variable>
 #include <map>
 #include <mutex>
 #include <memory>
@@ -18,6 +19,7 @@
 #include <set>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <unordered_map>
 #include <vector>
@@ -376,6 +378,64 @@ struct LayerW {
 
 struct ProfRow { double ms = 0; int n = 0; };
 
+// Host side of the logits read-back: chunk c of the pinned staging buffer is copied to the
+// caller's buffer by thread c (the calling thread takes chunk 0) as soon as its device-to-host
+// copy has landed, so the host copy is split four ways and overlaps the remaining DMA.
+struct ReadPool {
+    static constexpr int kChunks = 4;
+    std::vector<std::thread> th;
+    std::mutex mu;
+    std::condition_variable cv, done_cv;
+    unsigned gen = 0;
+    int pending = 0;
+    bool stop = false;
+    float* dst = nullptr;
+    const float* src = nullptr;
+    size_t off[kChunks + 1] = {};
+    cudaEvent_t ev[kChunks] = {};
+
+    void chunk(int c) {
+        if (off[c + 1] == off[c]) return;
+        cudaEventSynchronize(ev[c]);
+        std::memcpy(dst + off[c], src + off[c], sizeof(float) * (off[c + 1] - off[c]));
+    }
+    void start(int device) {
+        for (int c = 1; c < kChunks; c++)
+            th.emplace_back([this, c, device] {
+                cudaSetDevice(device);
+                unsigned seen = 0;
+                for (;;) {
+                    {
+                        std::unique_lock<std::mutex> lk(mu);
+                        cv.wait(lk, [&] { return stop || gen != seen; });
+                        if (stop) return;
+                        seen = gen;
+                    }
+                    chunk(c);
+                    std::lock_guard<std::mutex> lk(mu);
+                    if (--pending == 0) done_cv.notify_one();
+                }
+            });
+    }
+    // copy [0, total) floats once the events have fired; off[] must be set by the caller
+    void run(float* d, const float* s) {
+        cudaEventSynchronize(ev[0]);   // the forward is done: wake the helpers only now
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            dst = d; src = s; pending = kChunks - 1; ++gen;
+        }
+        cv.notify_all();
+        chunk(0);
+        std::unique_lock<std::mutex> lk(mu);
+        done_cv.wait(lk, [&] { return pending == 0; });
+    }
+    ~ReadPool() {
+        { std::lock_guard<std::mutex> lk(mu); stop = true; }
+        cv.notify_all();
+        for (auto& t : th) t.join();
+    }
+};
+
 struct mgc_runtime {
     int device = 0;
     std::string dev_name;
@@ -401,7 +461,10 @@ struct mgc_runtime {
     size_t attn_scratch_n = 0;
     // host staging (pinned)
     int32_t* h_tokens = nullptr;
+    int* h_err = nullptr;   // pinned copy of the device error word, read back after each forward
     float* h_logits = nullptr;
+    // logits read-back in row chunks (ReadPool)
+    ReadPool rd;
     // CUDA graphs keyed by (B, S, tokens ptr, logits ptr)
     std::map<std::tuple<int, int, const void*, const void*>, cudaGraphExec_t> graphs;
     // profiling
@@ -577,9 +640,9 @@ void run_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* lo
     CK(cudaGraphLaunch(it->second, rt->st));
 }
 
-void check_dev_error() {
-    int v = 0;
-    CK(cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)));
+// v >= 0: a value of the device error word already read back (asynchronously, in stream order)
+void check_dev_error(int v = -1) {
+    if (v < 0) CK(cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)));
     if (v != 0) {
         const int zero = 0;
         cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int));
@@ -600,7 +663,10 @@ void destroy_runtime(mgc_runtime* rt) {
     free_splitk(rt->sk);
     free_actq(rt->aE); free_actq(rt->aF);
     if (rt->h_tokens) cudaFreeHost(rt->h_tokens);
+    if (rt->h_err) cudaFreeHost(rt->h_err);
     if (rt->h_logits) cudaFreeHost(rt->h_logits);
+    for (cudaEvent_t& e : rt->rd.ev)
+        if (e) cudaEventDestroy(e);
     if (rt->st) cudaStreamDestroy(rt->st);
     delete rt;
 }
@@ -621,6 +687,8 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->dev_name = prop.name;
         if (prop.major != 10) throw Err(std::string("libmgcuda needs an sm_100 GPU, found ") + prop.name);
         CK(cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking));
+        for (cudaEvent_t& e : rt->rd.ev) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        rt->rd.start(device);
         if (qgemm_prepare() != 0 || attn_prepare() != 0) throw Err("cannot set kernel shared-memory limits");
         Gguf g;
         g.open(path);
@@ -687,6 +755,7 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->attn_scratch = dalloc<float>(rt->attn_scratch_n);
         CK(cudaMemset(rt->attn_scratch, 0, rt->attn_scratch_n * sizeof(float)));
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
+        CK(cudaMallocHost(&rt->h_err, sizeof(int)));
         CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
         CK(cudaDeviceSynchronize());
         // one eager forward: sets every kernel's attributes outside any later stream capture
@@ -732,13 +801,38 @@ int mgc_transformer_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S
         const size_t R = (size_t)B * S, nl = R * rt->V;
         if ((int)R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
         CK(cudaSetDevice(rt->device));
+#ifdef MGC_E2E_TRACE
+        static double acc[6] = {}; static int ncall = 0;
+        auto now = [] { return std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now().time_since_epoch()).count(); };
+        const double t0 = now();
+#endif
         std::memcpy(rt->h_tokens, tokens, sizeof(int32_t) * R);
         CK(cudaMemcpyAsync(rt->tokens, rt->h_tokens, sizeof(int32_t) * R, cudaMemcpyHostToDevice, rt->st));
         run_forward(rt, rt->tokens, B, S, rt->logits);
-        CK(cudaMemcpyAsync(rt->h_logits, rt->logits, sizeof(float) * nl, cudaMemcpyDeviceToHost, rt->st));
-        CK(cudaStreamSynchronize(rt->st));
-        check_dev_error();
-        std::memcpy(logits, rt->h_logits, sizeof(float) * nl);
+#ifdef MGC_E2E_TRACE
+        const double t1 = now();
+#endif
+        constexpr int NCH = ReadPool::kChunks;
+        size_t* off = rt->rd.off;
+        for (int c = 0; c <= NCH; c++) off[c] = (R * c / NCH) * rt->V;   // whole rows per chunk
+        CK(cudaMemcpyFromSymbolAsync(rt->h_err, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, rt->st));
+        for (int c = 0; c < NCH; c++) {
+            if (off[c + 1] == off[c]) continue;
+            CK(cudaMemcpyAsync(rt->h_logits + off[c], rt->logits + off[c], sizeof(float) * (off[c + 1] - off[c]),
+                               cudaMemcpyDeviceToHost, rt->st));
+            CK(cudaEventRecord(rt->rd.ev[c], rt->st));
+        }
+        rt->rd.run(logits, rt->h_logits);
+#ifdef MGC_E2E_TRACE
+        acc[1] += now() - t1;
+#endif
+        check_dev_error(*rt->h_err);
+#ifdef MGC_E2E_TRACE
+        acc[0] += t1 - t0; acc[4] += now() - t0; ncall++;
+        if (ncall % 100 == 0)
+            std::fprintf(stderr, "e2e trace (us/call): enqueue %.1f  wait-first-chunk %.1f  memcpy-rest %.1f  memcpy-first %.1f  total %.1f\n",
+                         acc[0] / ncall, acc[1] / ncall, acc[2] / ncall, acc[3] / ncall, acc[4] / ncall);
+#endif
     });
 }
 

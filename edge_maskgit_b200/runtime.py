@@ -215,13 +215,19 @@ class CudaRuntime:
         return rows
 
     # --- TransformerFwd
-    def forward(self, tokens: np.ndarray, B: int | None = None) -> np.ndarray:
-        """tokens [B][S] int32 (host) -> logits [B*S][vocab] f32 (host)."""
+    def forward(self, tokens: np.ndarray, B: int | None = None, out: np.ndarray | None = None) -> np.ndarray:
+        """tokens [B][S] int32 (host) -> logits [B*S][vocab] f32 (host).  `out` (optional) is a
+        caller-owned C-contiguous float32 [B*S][vocab] buffer reused across calls, as the
+        reference decode loop reuses its logits vector (mg-generate.cpp:55)."""
         tokens = np.ascontiguousarray(tokens, dtype=np.int32)
         if tokens.ndim == 1:
             tokens = tokens[None]
         B, S = tokens.shape
-        out = np.empty((B * S, self.hparams.vocab_size), np.float32)
+        shape = (B * S, self.hparams.vocab_size)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
         check(lib.mgc_transformer_forward(self._h, _ptr(tokens), B, S, _ptr(out)), "forward")
         return out
 
