@@ -57,250 +57,463 @@ __global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, 
     }
 }
 
-__global__ void __launch_bounds__(256) flash_attn_tc(const uint8_t* __restrict__ prep, int S, int H, float scale,
-                                                     float* __restrict__ out, int nsplit, int tiles_per,
+// Softmax pieces shared by both attention kernels.  A thread holds its query row's scores for
+// this warp half's 64 keys (r[cc][j] = key 64 half + 32 cc + j, as f32 bits).
+// Row max of the raw scores (4 chains), scaled once: rounding is monotonic, so this equals the
+// max of the scaled scores.
+__device__ __forceinline__ float tile_row_max(const uint32_t (&r)[2][32], int half, int nch, int nvalid, float c1) {
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int cc = 0; cc < 2; cc++) {
+        const int ch = 2 * half + cc;
+        if (ch >= nch) break;
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+            if (ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
+    }
+    return __fmul_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), c1);
+}
+// p = 2^(s*c1 - m) on pairs (one packed FMA, two MUFU ex2), P_hi = f16(p), P_lo = f16(p - P_hi)
+// into the two swizzled P blocks; returns this half's row sum (packed partials).
+__device__ __forceinline__ float tile_probs(const uint32_t (&r)[2][32], int half, int nch, int nvalid, float c1,
+                                            float m_new, int row, uint8_t* pbh, uint8_t* pbl) {
+    const uint64_t c1x2 = pack2(c1, c1), nm2 = pack2(-m_new, -m_new), neg1 = pack2(-1.0f, -1.0f);
+    uint64_t ls2[2] = {0, 0};
+#pragma unroll
+    for (int cc = 0; cc < 2; cc++) {
+        const int ch = 2 * half + cc;
+        if (ch >= nch) break;
+        const bool full = ch * 32 + 32 <= nvalid;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            __half2 hh[4], hl[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int j = c * 8 + u * 2;
+                float t0, t1;
+                unpack2(fma2(pack2(__uint_as_float(r[cc][j]), __uint_as_float(r[cc][j + 1])), c1x2, nm2), t0, t1);
+                float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+                if (!full) {
+                    p0 = ch * 32 + j < nvalid ? p0 : 0.0f;
+                    p1 = ch * 32 + j + 1 < nvalid ? p1 : 0.0f;
+                }
+                const uint64_t p2 = pack2(p0, p1);
+                ls2[u & 1] = add2(ls2[u & 1], p2);
+                hh[u] = __floats2half2_rn(p0, p1);
+                const float2 back = __half22float2(hh[u]);
+                float l0, l1;
+                unpack2(fma2(pack2(back.x, back.y), neg1, p2), l0, l1);
+                hl[u] = __floats2half2_rn(l0, l1);
+            }
+            st_chunk(pbh, row, cc * 4 + c, hh);
+            st_chunk(pbl, row, cc * 4 + c, hl);
+        }
+    }
+    float a0, a1, b0, b1;
+    unpack2(ls2[0], a0, a1);
+    unpack2(ls2[1], b0, b1);
+    return (a0 + b0) + (a1 + b1);
+}
+
+// Single-key-tile variant (each CTA's key range is one 128-key tile, as for 257 tokens split
+// over three CTAs): no pipeline to overlap, so all 8 warps run the one chain
+// S -> softmax -> P V, with thread 0 issuing the MMAs; 128-column TMEM, one P buffer.
+namespace fa1 {   // shared-memory layout: Q | K | V^T | (P_hi, P_lo) | row max / sum exchange | barriers
+constexpr uint32_t OQ = 0, OK = fa::Q_BYTES, OV = OK + fa::K_BYTES, OP = OV + fa::VT_BYTES, OX = OP + fa::P_SET,
+                   OBAR = OX + fa::X_SET;
+constexpr uint32_t SMEM = 1024 + OBAR + 128, TMEM_COLS = 256;
+}  // namespace fa1
+
+__global__ void __launch_bounds__(256) flash_attn_1t(const uint8_t* __restrict__ prep, int S, int H, float scale,
+                                                     float* __restrict__ out, int nsplit,
                                                      float* __restrict__ opart, float* __restrict__ mlpart) {
     using namespace fa;
+    using fa1::OQ; using fa1::OK; using fa1::OV; using fa1::OP; using fa1::OX; using fa1::OBAR;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bar_q = (uint64_t*)(sm + OFF_BAR);
-    uint64_t* bar_kv = bar_q + 1;   // [2]
-    uint64_t* bar_s = bar_q + 3;
-    uint64_t* bar_o = bar_q + 4;
-    uint32_t* tmem_slot = (uint32_t*)(bar_q + 5);
+    uint64_t* bar_in = (uint64_t*)(sm + OBAR);   // Q, K, V landed (tx)
+    uint64_t* bar_s = bar_in + 1;
+    uint64_t* bar_o = bar_in + 2;
+    uint32_t* tmem_slot = (uint32_t*)(bar_in + 3);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-    float* xmax = reinterpret_cast<float*>(sm + OFF_X);   // [2][128]
+    float* xmax = reinterpret_cast<float*>(sm + OX);   // [2][128]
     float* xsum = xmax + 2 * BM;                           // [2][128]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = warp >> 2;
     const int h = blockIdx.y, b = blockIdx.z / nsplit, split = blockIdx.z % nsplit, qti = blockIdx.x, q0 = qti * BM;
-    const int E = H * D, nt = (S + BC - 1) / BC;
-    const int kt0 = split * tiles_per, kt1 = min(nt, kt0 + tiles_per);
+    const int E = H * D, nt = (S + BC - 1) / BC, kt = split;   // one key tile per split
     const uint8_t* base = prep_base(const_cast<uint8_t*>(prep), b, h, H, nt);
-    const uint8_t* gq = base + (size_t)qti * Q_BYTES;
-    const uint8_t* gk = base + (size_t)nt * Q_BYTES;
-    const uint8_t* gv = base + (size_t)nt * (Q_BYTES + K_BYTES);
-
     if (tid == 0) {
-        for (int i = 0; i < 5; i++) mbar_init(bar_q + i, 1);
+        for (int i = 0; i < 3; i++) mbar_init(bar_in + i, 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
-    griddep_wait();   // prep / qkv come from the preceding kernel
+    if (warp == 0) tmem_alloc(tmem_slot, fa1::TMEM_COLS);
+    griddep_wait();
     griddep_launch();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int nvalid = min(BC, S - kt * BC), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
+    bool ok = true;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar_in, Q_BYTES + K_BYTES + VT_BYTES);
+        bulk_g2s(sm + OQ, base + (size_t)qti * Q_BYTES, Q_BYTES, bar_in);
+        bulk_g2s(sm + OK, base + (size_t)nt * Q_BYTES + (size_t)kt * K_BYTES, K_BYTES, bar_in);
+        bulk_g2s(sm + OV, base + (size_t)nt * (Q_BYTES + K_BYTES) + (size_t)kt * VT_BYTES, VT_BYTES, bar_in);
+        if (mbar_wait(bar_in, 0, abort_flag, 23)) {
+            tc_fence_after();
+            const uint64_t dq = sdesc_sw128(smem_u32(sm + OQ)), dk = sdesc_sw128(smem_u32(sm + OK));
+            const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
+#pragma unroll
+            for (int k = 0; k < D / 16; k++) mma_f16(tmem, dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
+            mma_commit(bar_s);
+        } else {   // let the copies land before the CTA can exit
+            volatile int never = 0;
+            mbar_wait(bar_in, 0, &never, 12);
+        }
+    }
+    ok = mbar_wait(bar_s, 0, abort_flag, 21);
+    ok = __syncthreads_and(ok);
     const int row = (warp & 3) * 32 + lane;
     const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const uint32_t sQ = smem_u32(sm + OFF_Q), sPh = smem_u32(sm + OFF_PH), sPl = smem_u32(sm + OFF_PL);
-    constexpr uint32_t idesc_o = idesc_make(1, 0, 0, BM, D);
-    auto load_kv = [&](int kt, int buf) {
-        mbar_arrive_expect_tx(bar_kv + buf, K_BYTES + VT_BYTES);
-        bulk_g2s(sm + OFF_K + buf * K_BYTES, gk + (size_t)kt * K_BYTES, K_BYTES, bar_kv + buf);
-        bulk_g2s(sm + OFF_V + buf * VT_BYTES, gv + (size_t)kt * VT_BYTES, VT_BYTES, bar_kv + buf);
-    };
-    if (tid == 0 && kt0 < kt1) {
-        mbar_arrive_expect_tx(bar_q, Q_BYTES);
-        bulk_g2s(sm + OFF_Q, gq, Q_BYTES, bar_q);
-        load_kv(kt0, 0);
-    }
-
-    const bool wact = q0 + (warp & 3) * 32 < S;   // warp-uniform: owns at least one real query row
-    const float c1 = scale * LOG2E;               // scores in the base-2 domain
-    float o[D / 2];
-#pragma unroll
-    for (int d = 0; d < D / 2; d++) o[d] = 0.0f;
+    const bool wact = q0 + (warp & 3) * 32 < S;
+    const float c1 = scale * LOG2E;
     float m_i = -INFINITY, l_i = 0.0f;
-    bool ok = true;
-
-#ifdef MGC_ATTN_TRACE   // development trace: CTA (0,0,0) records per-tile phase stamps (SM cycles)
-    __shared__ int trc[40 * 8];
-    const long long t_0 = clock64();
-    const bool tr = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && tid == 0;
-#define ATR(k) do { if (tr && i < 40) trc[i * 8 + (k)] = (int)(clock64() - t_0); } while (0)
-#else
-#define ATR(k) ((void)0)
-#endif
-    for (int kt = kt0; kt < kt1 && ok; kt++) {
-        const int i = kt - kt0, buf = i & 1, ph = i & 1;
-        const int kb = kt * BC, nvalid = min(BC, S - kb), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
-        ATR(0);
-        if (tid == 0) {
-            if (kt + 1 < kt1) load_kv(kt + 1, buf ^ 1);   // that buffer's last reader (tile i-1) is done
-            bool w = (i > 0 || mbar_wait(bar_q, 0, abort_flag, 23)) && mbar_wait(bar_kv + buf, (i >> 1) & 1, abort_flag, 24);
-            if (w) {
-                tc_fence_after();
-                const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
-                const uint32_t sK = smem_u32(sm + OFF_K + buf * K_BYTES);
-                const uint64_t dq = sdesc_sw128(sQ), dk = sdesc_sw128(sK);
-#pragma unroll
-                for (int k = 0; k < D / 16; k++) mma_f16(tmem, dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
-                mma_commit(bar_s);
-            }
-        }
-        ok = mbar_wait(bar_s, ph, abort_flag, 21);
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        ATR(1);
+    uint32_t r[2][32];
+    if (ok) {
         tc_fence_after();
-        // ---- softmax over this half's 64 columns
-        float alpha = 1.0f;
-        uint32_t r[2][32];
         float mloc = -INFINITY;
         if (wact) {
 #pragma unroll
             for (int cc = 0; cc < 2; cc++)
                 if (2 * half + cc < nch) tmem_ld32(t_row + (2 * half + cc) * 32, r[cc]);
             tmem_ld_wait();
-            ATR(2);
-            // max of the raw scores (4 chains), scaled once: rounding is monotonic, so this is
-            // the max of the scaled scores
-            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int cc = 0; cc < 2; cc++) {
-                const int ch = 2 * half + cc;
-                if (ch >= nch) break;
-#pragma unroll
-                for (int j = 0; j < 32; j++)
-                    if (ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
-            }
-            mloc = __fmul_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), c1);
+            mloc = tile_row_max(r, half, nch, nvalid, c1);
         }
         xmax[half * BM + row] = mloc;
         __syncthreads();
-        ATR(3);
-        const float m_new = fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row]));
+        m_i = fmaxf(xmax[row], xmax[BM + row]);
         float lsum = 0.0f;
         if (wact) {
-            alpha = exp2f(m_i - m_new);
-            uint8_t* pbh = sm + OFF_PH + half * P_BLK;
-            uint8_t* pbl = sm + OFF_PL + half * P_BLK;
-            // p = 2^(s*c1 - m) on pairs (one packed FMA, two MUFU ex2), row sum in packed partials,
-            // P_hi = f16(p), P_lo = f16(p - P_hi)
-            const uint64_t c1x2 = pack2(c1, c1), nm2 = pack2(-m_new, -m_new), neg1 = pack2(-1.0f, -1.0f);
-            uint64_t ls2[2] = {0, 0};
-#pragma unroll
-            for (int cc = 0; cc < 2; cc++) {
-                const int ch = 2 * half + cc;
-                if (ch >= nch) break;
-                const bool full = ch * 32 + 32 <= nvalid;
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    __half2 hh[4], hl[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int j = c * 8 + u * 2;
-                        float t0, t1;
-                        unpack2(fma2(pack2(__uint_as_float(r[cc][j]), __uint_as_float(r[cc][j + 1])), c1x2, nm2), t0, t1);
-                        float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
-                        if (!full) {
-                            p0 = ch * 32 + j < nvalid ? p0 : 0.0f;
-                            p1 = ch * 32 + j + 1 < nvalid ? p1 : 0.0f;
-                        }
-                        const uint64_t p2 = pack2(p0, p1);
-                        ls2[u & 1] = add2(ls2[u & 1], p2);
-                        hh[u] = __floats2half2_rn(p0, p1);
-                        const float2 back = __half22float2(hh[u]);
-                        float l0, l1;
-                        unpack2(fma2(pack2(back.x, back.y), neg1, p2), l0, l1);
-                        hl[u] = __floats2half2_rn(l0, l1);
-                    }
-                    st_chunk(pbh, row, cc * 4 + c, hh);
-                    st_chunk(pbl, row, cc * 4 + c, hl);
-                }
-            }
-            float a0, a1, b0, b1;
-            unpack2(ls2[0], a0, a1);
-            unpack2(ls2[1], b0, b1);
-            lsum = (a0 + b0) + (a1 + b1);
+            uint8_t* pbh = sm + OP + half * P_BLK;
+            lsum = tile_probs(r, half, nch, nvalid, c1, m_i, row, pbh, pbh + P_BYTES);
         }
         xsum[half * BM + row] = lsum;
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        ATR(4);
-        if (wact) {
-            l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(xsum[row], xsum[BM + row]));
-            m_i = m_new;
-        }
-        // ---- O_tile = P_hi V + P_lo V
-        if (tid == 0) {
+        l_i = __fadd_rn(xsum[row], xsum[BM + row]);
+        if (tid == 0) {   // O = P_hi V + P_lo V
             tc_fence_after();
-            const uint32_t sV = smem_u32(sm + OFF_V + buf * VT_BYTES);
-            // descriptors advance by (byte offset >> 4) in their start-address field (no carry:
-            // shared-memory addresses stay below 2^18)
-            const uint64_t dv = sdesc_sw128(sV);
+            constexpr uint32_t idesc_o = idesc_make(1, 0, 0, BM, D);
+            const uint64_t dv = sdesc_sw128(smem_u32(sm + OV));
 #pragma unroll
             for (int part = 0; part < 2; part++) {
-                const uint64_t dp = sdesc_sw128(part == 0 ? sPh : sPl);
+                const uint64_t dp = sdesc_sw128(smem_u32(sm + OP + part * P_BYTES));
                 if (nmma == BC) {
 #pragma unroll
-                    for (int j = 0; j < BC / 16; j++)
-                        mma_f16(tmem + BC, dp + (j >> 2) * (P_BLK >> 4) + (j & 3) * 2,
-                                dv + (j >> 2) * (VT_BLK >> 4) + (j & 3) * 2, idesc_o, (part | j) != 0);
+                    for (int t = 0; t < BC / 16; t++)
+                        mma_f16(tmem + BC, dp + (t >> 2) * (P_BLK >> 4) + (t & 3) * 2,
+                                dv + (t >> 2) * (VT_BLK >> 4) + (t & 3) * 2, idesc_o, (part | t) != 0);
                 } else {
-                    for (int j = 0; j < nmma / 16; j++)
-                        mma_f16(tmem + BC, dp + (j >> 2) * (P_BLK >> 4) + (j & 3) * 2,
-                                dv + (j >> 2) * (VT_BLK >> 4) + (j & 3) * 2, idesc_o, (part | j) != 0);
+                    for (int t = 0; t < nmma / 16; t++)
+                        mma_f16(tmem + BC, dp + (t >> 2) * (P_BLK >> 4) + (t & 3) * 2,
+                                dv + (t >> 2) * (VT_BLK >> 4) + (t & 3) * 2, idesc_o, (part | t) != 0);
                 }
             }
             mma_commit(bar_o);
-            ATR(5);
         }
-        ok = mbar_wait(bar_o, ph, abort_flag, 22);
+        ok = mbar_wait(bar_o, 0, abort_flag, 22);
         ok = __syncthreads_and(ok);
-        if (!ok) break;
-        ATR(6);
-        tc_fence_after();
-        if (wact) {   // this half's 24 output dims
-            uint32_t a16[16], a8[8];
-            if (half == 0) { tmem_ld16(t_row + BC, a16); tmem_ld8(t_row + BC + 16, a8); }
-            else { tmem_ld8(t_row + BC + 24, a8); tmem_ld16(t_row + BC + 32, a16); }
-            tmem_ld_wait();
-            if (half == 0) {
-#pragma unroll
-                for (int d = 0; d < 16; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a16[d]));
-#pragma unroll
-                for (int d = 0; d < 8; d++) o[16 + d] = __fmaf_rn(alpha, o[16 + d], __uint_as_float(a8[d]));
-            } else {
-#pragma unroll
-                for (int d = 0; d < 8; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a8[d]));
-#pragma unroll
-                for (int d = 0; d < 16; d++) o[8 + d] = __fmaf_rn(alpha, o[8 + d], __uint_as_float(a16[d]));
-            }
-        }
-        tc_fence_before();
-        __syncthreads();   // P and this K/V buffer are rewritten two tiles on
-        ATR(7);
     }
+    float o[D / 2];
+    if (ok && wact) {
+        tc_fence_after();
+        uint32_t a16[16], a8[8];
+        if (half == 0) { tmem_ld16(t_row + BC, a16); tmem_ld8(t_row + BC + 16, a8); }
+        else { tmem_ld8(t_row + BC + 24, a8); tmem_ld16(t_row + BC + 32, a16); }
+        tmem_ld_wait();
+        if (half == 0) {
+#pragma unroll
+            for (int d = 0; d < 16; d++) o[d] = __uint_as_float(a16[d]);
+#pragma unroll
+            for (int d = 0; d < 8; d++) o[16 + d] = __uint_as_float(a8[d]);
+        } else {
+#pragma unroll
+            for (int d = 0; d < 8; d++) o[d] = __uint_as_float(a8[d]);
+#pragma unroll
+            for (int d = 0; d < 16; d++) o[8 + d] = __uint_as_float(a16[d]);
+        }
+        const int qr = q0 + row, d0 = half * (D / 2);
+        if (qr < S && nsplit > 1) {
+            const size_t R = (size_t)(gridDim.z / nsplit) * S, rr = (size_t)split * R + (size_t)b * S + qr;
+            float4* dst = reinterpret_cast<float4*>(opart + rr * E + h * D + d0);
+#pragma unroll
+            for (int d = 0; d < D / 2; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+            if (half == 0) reinterpret_cast<float2*>(mlpart)[rr * H + h] = make_float2(m_i, l_i);
+        } else if (qr < S) {
+            const float inv = __fdiv_rn(1.0f, l_i);
+            float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D + d0);
+#pragma unroll
+            for (int d = 0; d < D / 2; d += 4)
+                dst[d / 4] = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
+                                         __fmul_rn(o[d + 3], inv));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, fa1::TMEM_COLS);
+    }
+}
 
-    const int qr = q0 + row, d0 = half * (D / 2);
-    if (ok && qr < S && nsplit > 1) {   // partial result of this key range, merged by the combine pass
-        const size_t R = (size_t)(gridDim.z / nsplit) * S, rr = (size_t)split * R + (size_t)b * S + qr;
-        float4* dst = reinterpret_cast<float4*>(opart + rr * E + h * D + d0);
+__global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* __restrict__ prep, int S, int H,
+                                                               float scale, float* __restrict__ out, int nsplit,
+                                                               int tiles_per, float* __restrict__ opart,
+                                                               float* __restrict__ mlpart) {
+    using namespace fa;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(sm + OFF_BAR);
+    uint64_t* bar_q = bars;            // Q landed (tx)
+    uint64_t* k_full = bars + 1;       // [2] K tile landed (tx)
+    uint64_t* v_full = bars + 3;       // [2] V^T tile landed (tx)
+    uint64_t* s_full = bars + 5;       // [2] S = Q K^T in TMEM (MMA commit)
+    uint64_t* p_full = bars + 7;       // [2] P written to shared memory (8 softmax warps)
+    uint64_t* o_full = bars + 9;       // [2] O tile = P V in TMEM (MMA commit)
+    uint64_t* o_free = bars + 11;      // [2] O tile read back (8 softmax warps)
+    uint64_t* v_free = bars + 13;      // [2] V^T buffer no longer read (MMA commit)
+    uint32_t* tmem_slot = (uint32_t*)(bars + 15);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = (warp >> 2) & 1;
+    const int h = blockIdx.y, b = blockIdx.z / nsplit, split = blockIdx.z % nsplit, qti = blockIdx.x, q0 = qti * BM;
+    const int E = H * D, nt = (S + BC - 1) / BC;
+    const int kt0 = split * tiles_per, kt1 = min(nt, kt0 + tiles_per), n = max(0, kt1 - kt0);
+    const uint8_t* base = prep_base(const_cast<uint8_t*>(prep), b, h, H, nt);
+    const uint8_t* gq = base + (size_t)qti * Q_BYTES;
+    const uint8_t* gk = base + (size_t)nt * Q_BYTES;
+    const uint8_t* gv = base + (size_t)nt * (Q_BYTES + K_BYTES);
+    auto nvalid_of = [&](int i) { return min(BC, S - (kt0 + i) * BC); };
+
+    if (tid == 0) {
+        mbar_init(bar_q, 1);
+        for (int j = 0; j < 2; j++) {
+            mbar_init(k_full + j, 1); mbar_init(v_full + j, 1); mbar_init(s_full + j, 1);
+            mbar_init(p_full + j, 8); mbar_init(o_full + j, 1); mbar_init(o_free + j, 8); mbar_init(v_free + j, 1);
+        }
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 8) tmem_alloc(tmem_slot, TMEM_COLS);
+    griddep_wait();   // prep / qkv come from the preceding kernel
+    griddep_launch();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const float c1 = scale * LOG2E;   // scores in the base-2 domain
+#ifdef MGC_ATTN_TRACE   // development trace: CTA (0,0,0) records per-tile phase stamps (SM cycles)
+    __shared__ int trc[40 * 10];
+    const long long t_0 = clock64();
+    const bool trb = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+#define ATR(i, k) do { if (trb && lane == 0 && (i) < 40) trc[(i) * 10 + (k)] = (int)(clock64() - t_0); } while (0)
+#else
+#define ATR(i, k) ((void)0)
+#endif
+
+    if (warp == 8) {
+        // ------------------------------------------------------------------ MMA + copy warp
+        // per step i: S(i) = Q K(i)^T; then, once softmax(i-1) has written P(i-1),
+        // O(i-1) = P_hi V + P_lo V.  K(i+1) reuses the buffer S(i-1) read; V(i+1) the one PV(i-1) read.
+        if (lane == 0 && n > 0) {
+            auto load_k = [&](int i) {
+                mbar_arrive_expect_tx(k_full + (i & 1), K_BYTES);
+                bulk_g2s(sm + OFF_K + (i & 1) * K_BYTES, gk + (size_t)(kt0 + i) * K_BYTES, K_BYTES, k_full + (i & 1));
+            };
+            auto load_v = [&](int i) {
+                mbar_arrive_expect_tx(v_full + (i & 1), VT_BYTES);
+                bulk_g2s(sm + OFF_V + (i & 1) * VT_BYTES, gv + (size_t)(kt0 + i) * VT_BYTES, VT_BYTES, v_full + (i & 1));
+            };
+            mbar_arrive_expect_tx(bar_q, Q_BYTES);
+            bulk_g2s(sm + OFF_Q, gq, Q_BYTES, bar_q);
+            int nk = 0, nv = 0;   // tiles whose K / V copies were issued
+            load_k(nk++);         // S(0) needs Q and K(0); V(0) follows at once (a one-tile CTA
+            load_v(nv++);         // needs it right after its softmax), the second tile after S(0)
+            auto more_loads = [&] {
+                for (; nv < 2 && nv < n; nv++) load_v(nv);
+                for (; nk < 2 && nk < n; nk++) load_k(nk);
+            };
+            const uint64_t dq = sdesc_sw128(smem_u32(sm + OFF_Q));
+            constexpr uint32_t idesc_o = idesc_make(1, 0, 0, BM, D);
+            bool ok = mbar_wait(bar_q, 0, abort_flag, 23);
+            for (int i = 0; ok && i <= n; i++) {
+                if (i < n) {
+                    const int nmma = (nvalid_of(i) + 15) & ~15;
+                    if (!(ok = mbar_wait(k_full + (i & 1), (i >> 1) & 1, abort_flag, 24))) break;
+                    tc_fence_after();
+                    const uint64_t dk = sdesc_sw128(smem_u32(sm + OFF_K + (i & 1) * K_BYTES));
+                    const uint32_t idesc_s = idesc_make(1, 0, 0, BM, nmma);
 #pragma unroll
-        for (int d = 0; d < D / 2; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-        if (half == 0) reinterpret_cast<float2*>(mlpart)[rr * H + h] = make_float2(m_i, l_i);
-    } else if (ok && qr < S) {
-        const float inv = __fdiv_rn(1.0f, l_i);
-        float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D + d0);
+                    for (int k = 0; k < D / 16; k++) mma_f16(tmem + (i & 1) * BC, dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
+                    mma_commit(s_full + (i & 1));
+                    if (i == 0) more_loads();
+                    ATR(i, 0);
+                }
+                if (i >= 1) {
+                    const int j = i - 1, nmma = (nvalid_of(j) + 15) & ~15;
+                    if (!(ok = mbar_wait(p_full + (j & 1), (j >> 1) & 1, abort_flag, 25))) break;
+                    ATR(j, 1);
+                    if (nk < n) load_k(nk++);   // S(j) has completed: its K buffer is free
+                    if (!(ok = mbar_wait(v_full + (j & 1), (j >> 1) & 1, abort_flag, 26))) break;
+                    if (j >= 2 && !(ok = mbar_wait(o_free + (j & 1), ((j - 2) >> 1) & 1, abort_flag, 27))) break;
+                    tc_fence_after();
+                    const uint64_t dv = sdesc_sw128(smem_u32(sm + OFF_V + (j & 1) * VT_BYTES));
+                    const uint32_t tO = tmem + TM_O + (j & 1) * D;
 #pragma unroll
-        for (int d = 0; d < D / 2; d += 4)
-            dst[d / 4] = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
-                                     __fmul_rn(o[d + 3], inv));
+                    for (int part = 0; part < 2; part++) {
+                        const uint64_t dp = sdesc_sw128(smem_u32(sm + OFF_P + (j & 1) * P_SET + part * P_BYTES));
+                        if (nmma == BC) {
+#pragma unroll
+                            for (int t = 0; t < BC / 16; t++)
+                                mma_f16(tO, dp + (t >> 2) * (P_BLK >> 4) + (t & 3) * 2,
+                                        dv + (t >> 2) * (VT_BLK >> 4) + (t & 3) * 2, idesc_o, (part | t) != 0);
+                        } else {
+                            for (int t = 0; t < nmma / 16; t++)
+                                mma_f16(tO, dp + (t >> 2) * (P_BLK >> 4) + (t & 3) * 2,
+                                        dv + (t >> 2) * (VT_BLK >> 4) + (t & 3) * 2, idesc_o, (part | t) != 0);
+                        }
+                    }
+                    mma_commit(o_full + (j & 1));
+                    mma_commit(v_free + (j & 1));
+                    ATR(j, 2);
+                    if (nv < n) {   // V(j+2) into the buffer PV(j) read
+                        if (!(ok = mbar_wait(v_free + (j & 1), (j >> 1) & 1, abort_flag, 28))) break;
+                        load_v(nv++);
+                    }
+                }
+            }
+            // let every issued copy land before the CTA can exit
+            volatile int never = 0;
+            mbar_wait(bar_q, 0, &never, 12);
+            for (int t = (nk > 2 ? nk - 2 : 0); t < nk; t++) mbar_wait(k_full + (t & 1), (t >> 1) & 1, &never, 13);
+            for (int t = (nv > 2 ? nv - 2 : 0); t < nv; t++) mbar_wait(v_full + (t & 1), (t >> 1) & 1, &never, 14);
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax warps
+        // warps w and w+4 share TMEM lanes 32(w%4).. (query row per lane) and split each tile's
+        // 128 scores and the 48 output dims in halves
+        const int row = (warp & 3) * 32 + lane;
+        const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const bool wact = q0 + (warp & 3) * 32 < S;   // warp-uniform: owns at least one real query row
+        float o[D / 2];
+#pragma unroll
+        for (int d = 0; d < D / 2; d++) o[d] = 0.0f;
+        float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f;
+        bool ok = true;
+        // O(j) accumulation: o = alpha_j o + O(j)
+        auto accumulate = [&](int j, float alpha) {
+            ok = ok && mbar_wait(o_full + (j & 1), (j >> 1) & 1, abort_flag, 22);
+            ok = __all_sync(0xffffffffu, ok);
+            if (warp == 0) ATR(j, 8);
+            if (ok && wact) {
+                tc_fence_after();
+                const uint32_t tO = t_row + TM_O + (j & 1) * D;
+                uint32_t a16[16], a8[8];
+                if (half == 0) { tmem_ld16(tO, a16); tmem_ld8(tO + 16, a8); }
+                else { tmem_ld8(tO + 24, a8); tmem_ld16(tO + 32, a16); }
+                tmem_ld_wait();
+                if (half == 0) {
+#pragma unroll
+                    for (int d = 0; d < 16; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a16[d]));
+#pragma unroll
+                    for (int d = 0; d < 8; d++) o[16 + d] = __fmaf_rn(alpha, o[16 + d], __uint_as_float(a8[d]));
+                } else {
+#pragma unroll
+                    for (int d = 0; d < 8; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a8[d]));
+#pragma unroll
+                    for (int d = 0; d < 16; d++) o[8 + d] = __fmaf_rn(alpha, o[8 + d], __uint_as_float(a16[d]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_free + (j & 1));
+            if (warp == 0) ATR(j, 9);
+        };
+        for (int i = 0; i < n; i++) {
+            const int nvalid = nvalid_of(i), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
+            float* xmax = reinterpret_cast<float*>(sm + OFF_X + (i & 1) * X_SET);   // [2][128]
+            float* xsum = xmax + 2 * BM;                                             // [2][128]
+            ok = ok && mbar_wait(s_full + (i & 1), (i >> 1) & 1, abort_flag, 21);
+            ok = __all_sync(0xffffffffu, ok);
+            if (warp == 0) ATR(i, 3);
+            tc_fence_after();
+            float alpha = 1.0f, mloc = -INFINITY;
+            uint32_t r[2][32];
+            if (ok && wact) {
+                const uint32_t tS = t_row + (i & 1) * BC;
+#pragma unroll
+                for (int cc = 0; cc < 2; cc++)
+                    if (2 * half + cc < nch) tmem_ld32(tS + (2 * half + cc) * 32, r[cc]);
+                tmem_ld_wait();
+                mloc = tile_row_max(r, half, nch, nvalid, c1);
+            }
+            if (warp == 0) ATR(i, 4);
+            xmax[half * BM + row] = mloc;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            if (warp == 0) ATR(i, 5);
+            const float m_new = fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row]));
+            float lsum = 0.0f;
+            if (ok && wact) {
+                alpha = exp2f(m_i - m_new);
+                uint8_t* pbh = sm + OFF_P + (i & 1) * P_SET + half * P_BLK;
+                lsum = tile_probs(r, half, nch, nvalid, c1, m_new, row, pbh, pbh + P_BYTES);
+            }
+            fence_async_smem();   // P is read by the tensor core
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full + (i & 1));
+            if (warp == 0) ATR(i, 6);
+            xsum[half * BM + row] = lsum;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            if (warp == 0) ATR(i, 7);
+            if (ok && wact) {
+                l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(xsum[row], xsum[BM + row]));
+                m_i = m_new;
+            }
+            if (i >= 1) accumulate(i - 1, alpha_prev);
+            alpha_prev = alpha;
+        }
+        if (n >= 1) accumulate(n - 1, alpha_prev);
+
+        const int qr = q0 + row, d0 = half * (D / 2);
+        if (ok && qr < S && nsplit > 1) {   // partial result of this key range, merged by the combine pass
+            const size_t R = (size_t)(gridDim.z / nsplit) * S, rr = (size_t)split * R + (size_t)b * S + qr;
+            float4* dst = reinterpret_cast<float4*>(opart + rr * E + h * D + d0);
+#pragma unroll
+            for (int d = 0; d < D / 2; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+            if (half == 0) reinterpret_cast<float2*>(mlpart)[rr * H + h] = make_float2(m_i, l_i);
+        } else if (ok && qr < S) {
+            const float inv = __fdiv_rn(1.0f, l_i);
+            float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D + d0);
+#pragma unroll
+            for (int d = 0; d < D / 2; d += 4)
+                dst[d / 4] = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
+                                         __fmul_rn(o[d + 3], inv));
+        }
     }
     tc_fence_before();
     __syncthreads();
 #ifdef MGC_ATTN_TRACE
-    if (tr)
-        for (int j = 0; j < 40 * 8; j++) out[(size_t)(j / D) * E + j % D] = (float)trc[j];
+    if (trb && tid == 0)
+        for (int j = 0; j < 40 * 10; j++) out[(size_t)(j / D) * E + j % D] = (float)trc[j];
 #endif
-    if (warp == 0) {
+    if (warp == 8) {
         tc_fence_after();
-        tmem_dealloc(tmem, fa::TMEM_COLS);
+        tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
@@ -406,7 +619,8 @@ static bool g_attn_ready[64] = {};
 int attn_prepare() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
-    if (cudaFuncSetAttribute(flash_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(flash_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(flash_attn_1t, cudaFuncAttributeMaxDynamicSharedMemorySize, fa1::SMEM) != cudaSuccess)
         return -1;
     g_attn_ready[dev] = true;
     return 0;
@@ -437,8 +651,11 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     float* mlpart = opart + (size_t)nsplit * R * H * fa::D;
     if (!prepped) launch_k(attn_prep, B * H * ntiles * 3, 128, 0, st, qkv, S, H, ntiles, prep);
     dim3 grid(qt, H, B * nsplit);
-    launch_k(flash_attn_tc, grid, 256, fa::SMEM, st, (const uint8_t*)prep, S, H, scale, out, nsplit, tiles_per, opart,
-             mlpart);
+    if (tiles_per == 1)   // one key tile per CTA: nothing to pipeline
+        launch_k(flash_attn_1t, grid, 256, fa1::SMEM, st, (const uint8_t*)prep, S, H, scale, out, nsplit, opart, mlpart);
+    else
+        launch_k(flash_attn_tc, grid, fa::THREADS, fa::SMEM, st, (const uint8_t*)prep, S, H, scale, out, nsplit,
+                 tiles_per, opart, mlpart);
     g_launch_count += (nsplit > 1 ? 2 : 1) + (prepped ? 0 : 1);
     if (nsplit > 1 && qo && H * fa::D == 768) {   // merge + quantize in one pass (warp per row)
         auto kern = nsplit == 2 ? attn_combine_rows<3, 2> : nsplit == 3 ? attn_combine_rows<3, 3> : attn_combine_rows<3, 4>;
