@@ -50,6 +50,9 @@ struct QGemmArgs {
     int8_t* qo; int qo_Mpad; int qo_c;
     // fused attention prep (optional): also store y as the f16 Q/K/V tiles of attnprep.cuh
     uint8_t* ap; int ap_S, ap_H, ap_nt;
+    // persistent mode (tiles_n > 0): a 1-D grid of CTAs walks the tiles t = blockIdx.x, +gridDim.x,
+    // ... (tile t = n-tile t % tiles_n of m-tile t / tiles_n); the pipeline runs on across tiles
+    int tiles_n, tiles_m;
 };
 
 // (-1.5 * 2^23, -1.5 * 2^23): |v| < 2^22 always holds (32 * 127 * 128 < 2^22)
@@ -113,7 +116,7 @@ struct QGemmCfg {
     static_assert(NGRP >= 1 && TMEM_NEED <= 512, "TMEM ring exceeds 512 columns");
 };
 
-template <int BN, int CG, bool Q4K, int CB>
+template <int BN, int CG, bool Q4K, int CB, bool PERSIST>
 __global__ void __launch_bounds__(QGemmCfg<BN, CG, Q4K, CB>::THREADS, MGC_QGEMM_MINB)
 qgemm_kernel(const QGemmArgs p) {
     using C = QGemmCfg<BN, CG, Q4K, CB>;
@@ -131,7 +134,18 @@ qgemm_kernel(const QGemmArgs p) {
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128;
+    constexpr bool persist = PERSIST;   // (p.tiles_n > 0)
+    const int my_tiles = persist ? (p.tiles_n * p.tiles_m - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 1;
+    auto tile_of = [&](int ti, int& n0_, int& mt_) {   // ti-th tile of this CTA: n offset, m-tile index
+        if (persist) {
+            const int t = blockIdx.x + ti * gridDim.x;
+            n0_ = (t % p.tiles_n) * BN;
+            mt_ = t / p.tiles_n;
+        } else {
+            n0_ = blockIdx.x * BN;
+            mt_ = blockIdx.y;
+        }
+    };
 #ifdef MGC_QGEMM_TRACE
     const long long t_start = clock64();
     long long g_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g_start));
@@ -158,8 +172,10 @@ qgemm_kernel(const QGemmArgs p) {
             int last_it[NST];
             for (int s = 0; s < NST; s++) last_it[s] = -1;
             // three copies per 128-K tile: activation tile (+ its scales), weight codes, weight scales
-            auto copy_w = [&](int i) {
-                const int kc = kc0 + i, s = i % NST;
+            // (i: chunk within the tile; gc: running chunk index of this CTA, which picks the stage)
+            int n0, mt;
+            auto copy_w = [&](int i, int gc) {
+                const int kc = kc0 + i, s = gc % NST;
                 uint8_t* st = smem + s * C::STAGE;
 #pragma unroll
                 for (int u = 0; u < SUB; u++) {
@@ -169,34 +185,39 @@ qgemm_kernel(const QGemmArgs p) {
                              C::S_BYTES, &full[s]);
                 }
             };
-            auto copy_a = [&](int i) {
-                const int kc = kc0 + i, s = i % NST;
+            auto copy_a = [&](int i, int gc) {
+                const int kc = kc0 + i, s = gc % NST;
                 uint8_t* st = smem + s * C::STAGE;
 #pragma unroll
                 for (int u = 0; u < SUB; u++) {
                     const size_t kk = (size_t)kc * SUB + u;   // 128-K activation tile index
-                    bulk_g2s(st + u * C::A_BYTES, p.aq + (kk * (p.Mpad / 128) + blockIdx.y) * kActTile, C::A_BYTES,
+                    bulk_g2s(st + u * C::A_BYTES, p.aq + (kk * (p.Mpad / 128) + mt) * kActTile, C::A_BYTES,
                              &full[s]);
                 }
             };
             // the first stages are free: their weights go out before the wait on the preceding kernel
             const int npre = nloc < NST ? nloc : NST;
+            tile_of(0, n0, mt);
             for (int i = 0; i < npre; i++) {
                 TRACE(i);
                 mbar_arrive_expect_tx(&full[i], C::TX_BYTES);
-                copy_w(i);
+                copy_w(i, i);
                 last_it[i] = 0;
             }
             griddep_wait();   // the activation tiles come from the preceding kernel
-            for (int i = 0; i < npre; i++) copy_a(i);
-            for (int i = npre; i < nloc; i++) {
-                const int s = i % NST, it = i / NST;
-                if (!mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1)) break;
-                TRACE(i);
-                mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
-                copy_w(i);
-                copy_a(i);
-                last_it[s] = it;
+            for (int i = 0; i < npre; i++) copy_a(i, i);
+            bool go = true;
+            for (int ti = 0; go && ti < my_tiles; ti++) {
+                tile_of(ti, n0, mt);
+                for (int i = ti == 0 ? npre : 0; i < nloc; i++) {
+                    const int gc = ti * nloc + i, s = gc % NST, it = gc / NST;
+                    if (!(go = mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1))) break;
+                    TRACE(i);
+                    mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+                    copy_w(i, gc);
+                    copy_a(i, gc);
+                    last_it[s] = it;
+                }
             }
             if (*abort_flag) {   // let copies already in flight land before the CTA exits
                 volatile int never = 0;
@@ -208,7 +229,7 @@ qgemm_kernel(const QGemmArgs p) {
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_make(2, 1, Q4K ? 0 : 1, 128, BN);
-            for (int kc = 0; kc < nloc; kc++) {   // local chunk index
+            for (int kc = 0; kc < my_tiles * nloc; kc++) {   // running chunk index over this CTA's tiles
                 const int s = kc % NST, it = kc / NST, g = kc % NGRP, ug = kc / NGRP;
                 if (!mbar_wait(&full[s], it & 1, abort_flag, 2)) break;
                 if (!mbar_wait(&tempty[g], (ug & 1) ^ 1, abort_flag, 3)) break;
@@ -230,11 +251,12 @@ qgemm_kernel(const QGemmArgs p) {
         griddep_launch();
     } else {
         const int pw = warp - 2, q = warp & 3, cg = pw >> 2;
-        const int row = q * 32 + lane, m = m0 + row, c0 = cg * CW;
-        const bool active = (m0 + q * 32) < p.M;   // warp-uniform
+        const int row = q * 32 + lane, c0 = cg * CW;
+        int n0, mt;
+        tile_of(0, n0, mt);
+        int m0 = mt * 128, m = m0 + row;
+        bool active = (m0 + q * 32) < p.M;   // warp-uniform
         uint64_t acc2[CW / 2];   // column pairs (2c, 2c+1), packed for f32x2 math
-#pragma unroll
-        for (int c = 0; c < CW / 2; c++) acc2[c] = 0;
         const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16) + c0;
         // Work unit = a batch of BATCH blocks (BATCH*CW int32 per thread, one TMEM-load wait
         // per batch); BPC batches per 4-block chunk.  (Overlapping batch t+1's loads with batch
@@ -332,7 +354,16 @@ qgemm_kernel(const QGemmArgs p) {
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
         };
-        for (int t = 0; ok && t < nbatch; t++) {
+        for (int ti = 0; ok && ti < my_tiles; ti++) {
+        if (ti > 0) {
+            tile_of(ti, n0, mt);
+            m0 = mt * 128;
+            m = m0 + row;
+            active = (m0 + q * 32) < p.M;
+        }
+#pragma unroll
+        for (int c = 0; c < CW / 2; c++) acc2[c] = 0;
+        for (int t = ti * nbatch; ok && t < (ti + 1) * nbatch; t++) {   // running batch index
             uint32_t I[BATCH][CW];
             issue(I, t);
             if (!ok) break;
@@ -368,7 +399,7 @@ qgemm_kernel(const QGemmArgs p) {
             __threadfence();
             asm volatile("bar.sync 1, %0;" ::"r"(C::NPW * 32) : "memory");
             volatile int* last_flag = (volatile int*)(tmem_slot + 2);
-            int* ctr = p.counters + blockIdx.y * gridDim.x + blockIdx.x;
+            int* ctr = p.counters + blockIdx.y * gridDim.x + blockIdx.x;   // (split-K is never persistent)
             if (threadIdx.x == 64) {
                 const int prev = atomicAdd(ctr, 1);
                 *last_flag = prev == p.nsplit - 1;
@@ -476,14 +507,17 @@ qgemm_kernel(const QGemmArgs p) {
                 }
             }
         }
+        }   // tiles
     }
 
     if (warp >= 2 && lane == 0) TRACE(1792 + warp);
 #ifdef MGC_QGEMM_TRACE
     if (threadIdx.x == 64 && !(blockIdx.x == 0 && blockIdx.y == 0)) {   // per-CTA [start, end] stamps (low 32 bits)
         long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        p.y[(size_t)m0 * p.N + n0] = __int_as_float((int)(g_start & 0x7fffffff));
-        p.y[(size_t)m0 * p.N + n0 + 1] = __int_as_float((int)(t & 0x7fffffff));
+        int n0, mt;
+        tile_of(0, n0, mt);
+        p.y[(size_t)mt * 128 * p.N + n0] = __int_as_float((int)(g_start & 0x7fffffff));
+        p.y[(size_t)mt * 128 * p.N + n0 + 1] = __int_as_float((int)(t & 0x7fffffff));
     }
 #endif
 done:
@@ -498,8 +532,11 @@ done:
 template <int BN, int CG, bool Q4K, int CB>
 static int set_smem_attr() {
     using C = QGemmCfg<BN, CG, Q4K, CB>;
-    return cudaFuncSetAttribute(qgemm_kernel<BN, CG, Q4K, CB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                C::SMEM) == cudaSuccess ? 0 : -1;
+    const bool a = cudaFuncSetAttribute(qgemm_kernel<BN, CG, Q4K, CB, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) == cudaSuccess;
+    const bool b = cudaFuncSetAttribute(qgemm_kernel<BN, CG, Q4K, CB, true>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) == cudaSuccess;
+    return a && b ? 0 : -1;
 }
 
 // Sets the dynamic shared-memory limit of every instantiation on the current device.  Must
@@ -518,12 +555,28 @@ int qgemm_prepare() {
     return rc;
 }
 
+static int sm_count() {
+    static int n[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (n[dev] == 0 && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
+    return n[dev];
+}
+
 template <int BN, int CG, bool Q4K, int CB>
-static int run_qgemm(const QGemmArgs& a, cudaStream_t st) {
+static int run_qgemm(QGemmArgs a, cudaStream_t st) {
     ++g_launch_count;
     using C = QGemmCfg<BN, CG, Q4K, CB>;
-    dim3 grid((a.N + BN - 1) / BN, (a.M + 127) / 128, a.nsplit);
-    launch_k(qgemm_kernel<BN, CG, Q4K, CB>, grid, C::THREADS, C::SMEM, st, a);
+    const int tiles_n = (a.N + BN - 1) / BN, tiles_m = (a.M + 127) / 128, ctas = sm_count() * MGC_QGEMM_MINB;
+    if (a.nsplit == 1 && tiles_n * tiles_m > ctas) {   // more tiles than one wave: persistent CTAs
+        a.tiles_n = tiles_n;
+        a.tiles_m = tiles_m;
+        launch_k(qgemm_kernel<BN, CG, Q4K, CB, true>, dim3(ctas, 1, 1), C::THREADS, C::SMEM, st, a);
+        return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+    }
+    dim3 grid(tiles_n, tiles_m, a.nsplit);
+    launch_k(qgemm_kernel<BN, CG, Q4K, CB, false>, grid, C::THREADS, C::SMEM, st, a);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -587,7 +640,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
                 sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps,
                 qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
-                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1};
+                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0};
     const bool q4 = w.wtype == 12;
 #define X(BN, CG, CB) \
     if (bn == BN && cg == CG && cb == CB) return q4 ? run_qgemm<BN, CG, true, CB>(p, st) : run_qgemm<BN, CG, false, CB>(p, st);

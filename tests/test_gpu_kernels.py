@@ -102,17 +102,19 @@ def test_qgemm_epilogue(dev, oracle_mod, monkeypatch, wtype, act):
     assert np.array_equal(y, y2)
 
 
-def test_qgemm_large_m(dev, oracle_mod):
-    """M=4097 (config 5 row count): compare a row sample against the oracle."""
+@pytest.mark.parametrize("wtype,K,N", [(8, 3072, 768), (12, 768, 3072), (12, 768, 2304)])
+def test_qgemm_large_m(dev, oracle_mod, wtype, K, N):
+    """M=4097 (config 5 row count; more tiles than SMs, so the CTAs walk several tiles each):
+    a row sample, first / middle / last m-tiles, bit-exact against the oracle."""
     from edge_maskgit_b200 import runtime as rt
     rng = np.random.default_rng(9)
-    M, K, N = 4097, 3072, 768
+    M = 4097
     x = rng.standard_normal((M, K), dtype=np.float32)
     w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
-    blocks = rt.pack_q8_0(w)
-    y = rt.QWeight(8, blocks, N, K).qgemm(_t(x, dev)).cpu().numpy()
+    blocks = rt.pack_q8_0(w) if wtype == 8 else rt.pack_q4_k(w)
+    y = rt.QWeight(wtype, blocks, N, K).qgemm(_t(x, dev)).cpu().numpy()
     rows = np.r_[0:3, 127:130, 2048:2050, 4094:4097]
-    ref = oracle_mod.qgemm(8, blocks, x[rows], N)
+    ref = oracle_mod.qgemm(wtype, blocks, x[rows], N)
     assert np.array_equal(y[rows], ref)
 
 
