@@ -104,7 +104,8 @@ int mgc_embed(const float* tok_embd_dev, int vocab, const float* pos_embd_dev, i
  * the MaskGIT transformer graph of src/mg-transformer.cpp:32-111. */
 typedef struct mgc_runtime mgc_runtime;
 /* Load a GGUF (mg-model.cpp:139-201 format), upload and repack every weight.
- * max_rows = largest B*S a forward will see. device = CUDA ordinal. */
+ * max_rows = largest B*S a forward will see. device = CUDA ordinal.  The runtime owns one
+ * CUDA stream and three host threads that copy logits out during mgc_transformer_forward. */
 int mgc_runtime_create(const char* gguf_path, int max_rows, int device, mgc_runtime** out);
 void mgc_runtime_destroy(mgc_runtime* rt);
 /* n_layer n_head n_embd n_ffn head_dim vocab n_tokens mask_id codebook wtype */
@@ -112,7 +113,8 @@ int mgc_runtime_hparams(const mgc_runtime* rt, int32_t out[10]);
 const char* mgc_runtime_device_name(const mgc_runtime* rt);
 
 /* The TransformerFwd callback (include/mg-generate.hpp:15): tokens host [B*S] int32 ->
- * logits host [B*S*vocab] f32, row-major s-outer / v-inner; synchronous. */
+ * logits host [B*S*vocab] f32, row-major s-outer / v-inner; synchronous.  The logits come back
+ * in four row chunks, each copied to `logits` by its own host thread as its DMA lands. */
 int mgc_transformer_forward(mgc_runtime* rt, const int32_t* tokens_host, int B, int S,
                             float* logits_host);
 /* Same forward with device buffers, enqueued on the runtime's stream (replayed from a
