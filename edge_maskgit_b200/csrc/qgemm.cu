@@ -598,12 +598,15 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
     }
     // Pick the width whose tile grid fills the 148 SMs in the fewest waves, weighing a wave by
     // its per-CTA work (BN) plus a fixed per-chunk cost (~16 columns' worth).  Promotion warps
-    // own 8 columns (two warps per SM sub-partition hide each other's latency), 16 where the
-    // epilogue quantizes (a 32-block split over two warps).  Widths whose last tile would run
-    // past the padded weight rows are skipped.
+    // own 4-8 columns (several warps per SM sub-partition hide each other's latency), 16 where
+    // the epilogue quantizes (a 32-block split over two warps).  Widths whose last tile would
+    // run past the padded weight rows are skipped.
     const int mt = (M + 127) / 128, npad = round_up(N, 128);
-    static const int cand8[4][2] = {{16, 2}, {32, 4}, {48, 6}, {64, 4}}, cand16[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
-    const auto& cand = fused_quant ? cand16 : cand8;
+    // (16-wide tiles run four 4-column warps, except when the epilogue stores attention tiles,
+    // which take 8 or 16 columns per warp)
+    static const int cand8[4][2] = {{16, 4}, {32, 4}, {48, 6}, {64, 4}}, cand8p[4][2] = {{16, 2}, {32, 4}, {48, 6}, {64, 4}},
+                     cand16[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
+    const auto& cand = fused_quant ? cand16 : prep ? cand8p : cand8;
     long best = -1;
     for (const auto& c : cand) {
         const int tiles_n = (N + c[0] - 1) / c[0];
