@@ -7,7 +7,6 @@
 #include "ptx.cuh"
 
 #include <algorithm>
-#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -801,17 +800,9 @@ int mgc_transformer_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S
         const size_t R = (size_t)B * S, nl = R * rt->V;
         if ((int)R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
         CK(cudaSetDevice(rt->device));
-#ifdef MGC_E2E_TRACE
-        static double acc[6] = {}; static int ncall = 0;
-        auto now = [] { return std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now().time_since_epoch()).count(); };
-        const double t0 = now();
-#endif
         std::memcpy(rt->h_tokens, tokens, sizeof(int32_t) * R);
         CK(cudaMemcpyAsync(rt->tokens, rt->h_tokens, sizeof(int32_t) * R, cudaMemcpyHostToDevice, rt->st));
         run_forward(rt, rt->tokens, B, S, rt->logits);
-#ifdef MGC_E2E_TRACE
-        const double t1 = now();
-#endif
         constexpr int NCH = ReadPool::kChunks;
         size_t* off = rt->rd.off;
         for (int c = 0; c <= NCH; c++) off[c] = (R * c / NCH) * rt->V;   // whole rows per chunk
@@ -823,16 +814,7 @@ int mgc_transformer_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S
             CK(cudaEventRecord(rt->rd.ev[c], rt->st));
         }
         rt->rd.run(logits, rt->h_logits);
-#ifdef MGC_E2E_TRACE
-        acc[1] += now() - t1;
-#endif
         check_dev_error(*rt->h_err);
-#ifdef MGC_E2E_TRACE
-        acc[0] += t1 - t0; acc[4] += now() - t0; ncall++;
-        if (ncall % 100 == 0)
-            std::fprintf(stderr, "e2e trace (us/call): enqueue %.1f  wait-first-chunk %.1f  memcpy-rest %.1f  memcpy-first %.1f  total %.1f\n",
-                         acc[0] / ncall, acc[1] / ncall, acc[2] / ncall, acc[3] / ncall, acc[4] / ncall);
-#endif
     });
 }
 
