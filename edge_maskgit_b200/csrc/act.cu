@@ -365,4 +365,50 @@ void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool wa
              (int8_t*)nullptr, (float*)nullptr, (int32_t*)nullptr);
 }
 
+// ---------------------------------------------------------------- decode-loop sampling
+// Per logits row (one warp per row): softmax over the first CB logits and a categorical draw
+// with the caller's uniform r, in the arithmetic of generate() (src/mg-generate.cpp:87-100,
+// sample_categorical :30-35): mx = max row[v]; e_v = exp(row[v] - mx) (the f32 exponential,
+// correctly rounded here by evaluating it in f64); sum = e_0 + e_1 + ... in order (f32);
+// p_v = e_v * (1 / sum); the first v with r <= p_0 + ... + p_v (accumulated in f64), else
+// CB - 1.  Lanes compute the exponentials, lane 0 runs the two ordered sums.
+__global__ void __launch_bounds__(128) sample_codes_kernel(const float* __restrict__ logits, int rows, int vocab,
+                                                           int CB, const double* __restrict__ r,
+                                                           int32_t* __restrict__ sid, float* __restrict__ psid) {
+    griddep_wait();
+    griddep_launch();
+    extern __shared__ float e_sm[];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, row = blockIdx.x * 4 + w;
+    if (row >= rows) return;
+    const float* L = logits + (size_t)row * vocab;
+    float* e = e_sm + (size_t)w * CB;
+    float mx = -INFINITY;
+    for (int v = lane; v < CB; v += 32) mx = fmaxf(mx, L[v]);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, k));
+    for (int v = lane; v < CB; v += 32) e[v] = (float)exp((double)__fsub_rn(L[v], mx));
+    __syncwarp();
+    if (lane == 0) {
+        float sum = 0.0f;
+        for (int v = 0; v < CB; v++) sum = __fadd_rn(sum, e[v]);
+        const float inv = __fdiv_rn(1.0f, sum);
+        const double rr = r[row];
+        double acc = 0.0;
+        int pick = CB - 1;
+        for (int v = 0; v < CB; v++) {
+            acc = __dadd_rn(acc, (double)__fmul_rn(e[v], inv));
+            if (rr <= acc) { pick = v; break; }
+        }
+        sid[row] = pick;
+        psid[row] = __fmul_rn(e[pick], inv);
+    }
+}
+
+void launch_sample_codes(const float* logits, int rows, int vocab, int CB, const double* r, int32_t* sid, float* psid,
+                         cudaStream_t st) {
+    ++g_launch_count;
+    launch_k(sample_codes_kernel, (unsigned)((rows + 3) / 4), 128, (size_t)4 * CB * sizeof(float), st, logits, rows,
+             vocab, CB, r, sid, psid);
+}
+
 }  // namespace mgc

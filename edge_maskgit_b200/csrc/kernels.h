@@ -90,6 +90,10 @@ extern int g_launch_count;
 // A bounded busy-wait kernel of ~`cycles` SM clocks (profiling: lets the host run ahead).
 void launch_spin(long long cycles, cudaStream_t st);
 
+// decode-loop sampling: per logits row, softmax over the first CB logits and a categorical draw
+// with uniform r[row] (generate(), mg-generate.cpp:87-100) -> sid[row], its probability psid[row]
+void launch_sample_codes(const float* logits, int rows, int vocab, int CB, const double* r, int32_t* sid, float* psid,
+                         cudaStream_t st);
 // quantizer: x [M][K] f32 -> tiled ActQ (want_c: also write the Q4_K correction term)
 void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st);
 // quantizer with plain outputs (kernel-level C ABI)

@@ -461,6 +461,9 @@ struct mgc_runtime {
     // host staging (pinned)
     int32_t* h_tokens = nullptr;
     int* h_err = nullptr;   // pinned copy of the device error word, read back after each forward
+    // decode-loop sampling on the device (mgc_generate): uniforms in, sampled code + probability out
+    double* d_r = nullptr; int32_t* d_sid = nullptr; float* d_psid = nullptr;
+    double* h_r = nullptr; int32_t* h_sid = nullptr; float* h_psid = nullptr;
     float* h_logits = nullptr;
     // logits read-back in row chunks (ReadPool)
     ReadPool rd;
@@ -663,6 +666,10 @@ void destroy_runtime(mgc_runtime* rt) {
     free_actq(rt->aE); free_actq(rt->aF);
     if (rt->h_tokens) cudaFreeHost(rt->h_tokens);
     if (rt->h_err) cudaFreeHost(rt->h_err);
+    cudaFree(rt->d_r); cudaFree(rt->d_sid); cudaFree(rt->d_psid);
+    if (rt->h_r) cudaFreeHost(rt->h_r);
+    if (rt->h_sid) cudaFreeHost(rt->h_sid);
+    if (rt->h_psid) cudaFreeHost(rt->h_psid);
     if (rt->h_logits) cudaFreeHost(rt->h_logits);
     for (cudaEvent_t& e : rt->rd.ev)
         if (e) cudaEventDestroy(e);
@@ -755,6 +762,10 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         CK(cudaMemset(rt->attn_scratch, 0, rt->attn_scratch_n * sizeof(float)));
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
         CK(cudaMallocHost(&rt->h_err, sizeof(int)));
+        rt->d_r = dalloc<double>(R); rt->d_sid = dalloc<int32_t>(R); rt->d_psid = dalloc<float>(R);
+        CK(cudaMallocHost(&rt->h_r, sizeof(double) * R));
+        CK(cudaMallocHost(&rt->h_sid, sizeof(int32_t) * R));
+        CK(cudaMallocHost(&rt->h_psid, sizeof(float) * R));
         CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
         CK(cudaDeviceSynchronize());
         // one eager forward: sets every kernel's attributes outside any later stream capture
@@ -855,28 +866,35 @@ int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_
         for (int i = 0; i < B; i++) rng.emplace_back(seeds[i]);
         std::vector<int32_t> tokens((size_t)B * S, MASK), sampled(S), result((size_t)B * S);
         for (int i = 0; i < B; i++) tokens[(size_t)i * S] = class_ids[i] + CB;
-        std::vector<float> L((size_t)B * S * vocab), selp(S), conf(S), probs(CB);
+        std::vector<float> selp(S), conf(S);
+        const size_t R = (size_t)B * S;
+        CK(cudaSetDevice(rt->device));
+        ensure_attn_scratch(rt, B, S);
         for (int step = 0; step < steps; step++) {
-            if (mgc_transformer_forward(rt, tokens.data(), B, S, L.data()) != 0) throw Err(g_err);
+            // forward on the device; the logits stay there (no read-back)
+            std::memcpy(rt->h_tokens, tokens.data(), sizeof(int32_t) * R);
+            CK(cudaMemcpyAsync(rt->tokens, rt->h_tokens, sizeof(int32_t) * R, cudaMemcpyHostToDevice, rt->st));
+            run_forward(rt, rt->tokens, B, S, rt->logits);
+            // the categorical uniforms of every position, in generate()'s draw order (one per
+            // position, before the step's gumbel draws), drawn while the forward runs
+            for (int i = 0; i < B; i++) {
+                std::uniform_real_distribution<double> u(0.0, 1.0);
+                for (int s = 0; s < S; s++) rt->h_r[(size_t)i * S + s] = u(rng[i]);
+            }
+            CK(cudaMemcpyAsync(rt->d_r, rt->h_r, sizeof(double) * R, cudaMemcpyHostToDevice, rt->st));
+            launch_sample_codes(rt->logits, (int)R, (int)vocab, CB, rt->d_r, rt->d_sid, rt->d_psid, rt->st);
+            CK(cudaMemcpyAsync(rt->h_sid, rt->d_sid, sizeof(int32_t) * R, cudaMemcpyDeviceToHost, rt->st));
+            CK(cudaMemcpyAsync(rt->h_psid, rt->d_psid, sizeof(float) * R, cudaMemcpyDeviceToHost, rt->st));
+            CK(cudaMemcpyFromSymbolAsync(rt->h_err, g_dev_error, sizeof(int), 0, cudaMemcpyDeviceToHost, rt->st));
+            CK(cudaStreamSynchronize(rt->st));
+            check_dev_error(*rt->h_err);
             for (int i = 0; i < B; i++) {
                 std::mt19937_64& r = rng[i];
                 int32_t* tk = tokens.data() + (size_t)i * S;
                 for (int s = 0; s < S; s++) {
-                    const float* row = L.data() + ((size_t)i * S + s) * vocab;
-                    float mx = -INFINITY;
-                    for (int v = 0; v < CB; v++) mx = std::fmax(mx, row[v]);
-                    float sum = 0.f;
-                    for (int v = 0; v < CB; v++) { const float e = std::exp(row[v] - mx); probs[v] = e; sum += e; }
-                    const float inv = 1.f / sum;
-                    for (int v = 0; v < CB; v++) probs[v] *= inv;
-                    std::uniform_real_distribution<double> u(0.0, 1.0);
-                    const double rr = u(r);
-                    double acc = 0.0;
-                    int sid = CB - 1;
-                    for (int v = 0; v < CB; v++) { acc += probs[v]; if (rr <= acc) { sid = v; break; } }
                     const bool unknown = tk[s] == MASK;
-                    sampled[s] = unknown ? sid : tk[s];
-                    selp[s] = unknown ? probs[sid] : INFINITY;
+                    sampled[s] = unknown ? rt->h_sid[(size_t)i * S + s] : tk[s];
+                    selp[s] = unknown ? rt->h_psid[(size_t)i * S + s] : INFINITY;   // known tokens: max confidence
                 }
                 std::copy(sampled.begin(), sampled.end(), result.begin() + (size_t)i * S);
                 const float ratio = (float)(step + 1) / steps;

@@ -133,6 +133,9 @@ void* mgc_runtime_stream(mgc_runtime* rt);
 
 /* Decode loop (generate(), src/mg-generate.cpp:53-123, without the VQGAN): B independent
  * images, image i with class_ids[i] and std::mt19937_64(seeds[i]); forwards are batched.
+ * The per-position softmax and categorical draw run on the device (the host draws the
+ * uniforms in the reference's order; only the sampled codes and their probabilities come
+ * back), the confidence / re-mask step on the host.
  * tokens_out host [B][S] = the final sampled sequence (class token first). */
 int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_t* seeds,
                  int steps, float temperature, int32_t* tokens_out);
