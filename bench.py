@@ -344,6 +344,65 @@ def run_tp_workload(args) -> None:
         dist.destroy_process_group()
 
 
+def run_decode_workload(args) -> None:
+    """Config 4: batched decode of 64 images (classes from default_rng(7), seed 7+i), Q8_0, 8 steps,
+    sharded by image over the ranks (each rank batches its images into one forward per step);
+    one all-gather of the token grids at the end.  Total work is fixed: strong scaling.  Each
+    timed step is one full 8-step decode of the 64 images; timing is CUDA events on the runtime's
+    stream (the loop is host-driven, so host gaps count), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from edge_maskgit_b200 import runtime as rt, shard
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if rank == 0:
+        path, _ = ensure_model("gq8")
+    if world > 1:
+        dist.barrier()
+    path, _ = ensure_model("gq8")
+    n_img, S = 64, 257
+    classes, seeds = shard.batch_classes(n_img), shard.batch_seeds(n_img)
+    lo, hi = shard.shard_range(n_img, rank, world)
+    r = rt.CudaRuntime(path, max_rows=S * max(1, hi - lo), device=local)
+    stream = torch.cuda.ExternalStream(r.stream_handle, device=torch.device("cuda", local))
+    gen = lambda c, sd, steps, t: r.generate(c, sd, steps, t)
+    for _ in range(args.warmup):
+        shard.decode_shard(gen, classes, seeds, rank, world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        local_tok = shard.decode_shard(gen, classes, seeds, rank, world)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        grids = shard.gather_tokens(local_tok, n_img, S)
+    else:
+        grids = local_tok
+    ms = float(ms.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "images/s", "value": n_img * args.steps / (ms * 1e-3), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
+            "data": "synthetic",
+            "config": {"workload": "config4 batched decode, 64 images x 8 steps, gq8, seq 257",
+                       "parallelism": f"images sharded over {world} rank(s), one all-gather of the token grids",
+                       "tokens_checksum": int(np.asarray(grids, dtype=np.int64).sum())},
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,13 +412,17 @@ def main():
     ap.add_argument("--quant", default="gq8", choices=["gq8", "gq4"])
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c5"],
-                    help="c1: the headline config-1 step (default); c5: M=4097 tensor-parallel step")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "c5"],
+                    help="c1: the headline config-1 step (default); c4: 64-image batched decode; "
+                         "c5: M=4097 tensor-parallel step")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 20 if args.impl == "reference" else 10 if args.workload == "c5" else 300
+        args.steps = 20 if args.impl == "reference" else 10 if args.workload == "c5" else 3 if args.workload == "c4" else 300
     if args.workload == "c5" and args.impl == "cuda":
         run_tp_workload(args)
+        return
+    if args.workload == "c4" and args.impl == "cuda":
+        run_decode_workload(args)
         return
     if args.impl == "reference":
         run_reference_arm(args)
