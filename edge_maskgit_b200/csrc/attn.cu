@@ -58,14 +58,15 @@ __global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, 
 }
 
 // Softmax pieces shared by both attention kernels.  A thread holds its query row's scores for
-// this warp half's 64 keys (r[cc][j] = key 64 half + 32 cc + j, as f32 bits).
+// NCH 32-key chunks, chunk index ch = NCH * part + cc (r[cc][j] = key 32 ch + j, as f32 bits).
 // Row max of the raw scores (4 chains), scaled once: rounding is monotonic, so this equals the
 // max of the scaled scores.
-__device__ __forceinline__ float tile_row_max(const uint32_t (&r)[2][32], int half, int nch, int nvalid, float c1) {
+template <int NCH>
+__device__ __forceinline__ float tile_row_max(const uint32_t (&r)[NCH][32], int part, int nch, int nvalid, float c1) {
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int cc = 0; cc < 2; cc++) {
-        const int ch = 2 * half + cc;
+    for (int cc = 0; cc < NCH; cc++) {
+        const int ch = NCH * part + cc;
         if (ch >= nch) break;
 #pragma unroll
         for (int j = 0; j < 32; j++)
@@ -74,16 +75,20 @@ __device__ __forceinline__ float tile_row_max(const uint32_t (&r)[2][32], int ha
     return __fmul_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), c1);
 }
 // p = 2^(s*c1 - m) on pairs (one packed FMA, two MUFU ex2), P_hi = f16(p), P_lo = f16(p - P_hi)
-// into the two swizzled P blocks; returns this half's row sum (packed partials).
-__device__ __forceinline__ float tile_probs(const uint32_t (&r)[2][32], int half, int nch, int nvalid, float c1,
-                                            float m_new, int row, uint8_t* pbh, uint8_t* pbl) {
+// into the swizzled P blocks of the sets ph / pl (64 keys per block); returns the partial row
+// sum of these chunks (packed partials).
+template <int NCH>
+__device__ __forceinline__ float tile_probs(const uint32_t (&r)[NCH][32], int part, int nch, int nvalid, float c1,
+                                            float m_new, int row, uint8_t* ph, uint8_t* pl) {
     const uint64_t c1x2 = pack2(c1, c1), nm2 = pack2(-m_new, -m_new), neg1 = pack2(-1.0f, -1.0f);
     uint64_t ls2[2] = {0, 0};
 #pragma unroll
-    for (int cc = 0; cc < 2; cc++) {
-        const int ch = 2 * half + cc;
+    for (int cc = 0; cc < NCH; cc++) {
+        const int ch = NCH * part + cc;
         if (ch >= nch) break;
         const bool full = ch * 32 + 32 <= nvalid;
+        uint8_t* bh = ph + (ch >> 1) * fa::P_BLK;
+        uint8_t* bl = pl + (ch >> 1) * fa::P_BLK;
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             __half2 hh[4], hl[4];
@@ -105,8 +110,8 @@ __device__ __forceinline__ float tile_probs(const uint32_t (&r)[2][32], int half
                 unpack2(fma2(pack2(back.x, back.y), neg1, p2), l0, l1);
                 hl[u] = __floats2half2_rn(l0, l1);
             }
-            st_chunk(pbh, row, cc * 4 + c, hh);
-            st_chunk(pbl, row, cc * 4 + c, hl);
+            st_chunk(bh, row, (ch & 1) * 4 + c, hh);
+            st_chunk(bl, row, (ch & 1) * 4 + c, hl);
         }
     }
     float a0, a1, b0, b1;
@@ -190,15 +195,14 @@ __global__ void __launch_bounds__(256) flash_attn_1t(const uint8_t* __restrict__
             for (int cc = 0; cc < 2; cc++)
                 if (2 * half + cc < nch) tmem_ld32(t_row + (2 * half + cc) * 32, r[cc]);
             tmem_ld_wait();
-            mloc = tile_row_max(r, half, nch, nvalid, c1);
+            mloc = tile_row_max<2>(r, half, nch, nvalid, c1);
         }
         xmax[half * BM + row] = mloc;
         __syncthreads();
         m_i = fmaxf(xmax[row], xmax[BM + row]);
         float lsum = 0.0f;
         if (wact) {
-            uint8_t* pbh = sm + OP + half * P_BLK;
-            lsum = tile_probs(r, half, nch, nvalid, c1, m_i, row, pbh, pbh + P_BYTES);
+            lsum = tile_probs<2>(r, half, nch, nvalid, c1, m_i, row, sm + OP, sm + OP + P_BYTES);
         }
         xsum[half * BM + row] = lsum;
         fence_async_smem();
@@ -282,14 +286,15 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
     uint64_t* k_full = bars + 1;       // [2] K tile landed (tx)
     uint64_t* v_full = bars + 3;       // [2] V^T tile landed (tx)
     uint64_t* s_full = bars + 5;       // [2] S = Q K^T in TMEM (MMA commit)
-    uint64_t* p_full = bars + 7;       // [2] P written to shared memory (8 softmax warps)
+    uint64_t* p_full = bars + 7;       // [2] P written to shared memory (16 softmax warps)
     uint64_t* o_full = bars + 9;       // [2] O tile = P V in TMEM (MMA commit)
-    uint64_t* o_free = bars + 11;      // [2] O tile read back (8 softmax warps)
+    uint64_t* o_free = bars + 11;      // [2] O tile read back (16 softmax warps)
     uint64_t* v_free = bars + 13;      // [2] V^T buffer no longer read (MMA commit)
     uint32_t* tmem_slot = (uint32_t*)(bars + 15);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = (warp >> 2) & 1;
+    constexpr int MMA_WARP = 16;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, part = (warp >> 2) & 3;
     const int h = blockIdx.y, b = blockIdx.z / nsplit, split = blockIdx.z % nsplit, qti = blockIdx.x, q0 = qti * BM;
     const int E = H * D, nt = (S + BC - 1) / BC;
     const int kt0 = split * tiles_per, kt1 = min(nt, kt0 + tiles_per), n = max(0, kt1 - kt0);
@@ -303,12 +308,12 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
         mbar_init(bar_q, 1);
         for (int j = 0; j < 2; j++) {
             mbar_init(k_full + j, 1); mbar_init(v_full + j, 1); mbar_init(s_full + j, 1);
-            mbar_init(p_full + j, 8); mbar_init(o_full + j, 1); mbar_init(o_free + j, 8); mbar_init(v_free + j, 1);
+            mbar_init(p_full + j, 16); mbar_init(o_full + j, 1); mbar_init(o_free + j, 16); mbar_init(v_free + j, 1);
         }
         *abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 8) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == MMA_WARP) tmem_alloc(tmem_slot, TMEM_COLS);
     griddep_wait();   // prep / qkv come from the preceding kernel
     griddep_launch();
     tc_fence_before();
@@ -325,7 +330,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
 #define ATR(i, k) ((void)0)
 #endif
 
-    if (warp == 8) {
+    if (warp == MMA_WARP) {
         // ------------------------------------------------------------------ MMA + copy warp
         // per step i: S(i) = Q K(i)^T; then, once softmax(i-1) has written P(i-1),
         // O(i-1) = P_hi V + P_lo V.  K(i+1) reuses the buffer S(i-1) read; V(i+1) the one PV(i-1) read.
@@ -404,14 +409,15 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
         }
     } else {
         // ------------------------------------------------------------------ softmax warps
-        // warps w and w+4 share TMEM lanes 32(w%4).. (query row per lane) and split each tile's
-        // 128 scores and the 48 output dims in halves
+        // warps w, w+4, w+8, w+12 share TMEM lanes 32(w%4).. (query row per lane); warp part p
+        // = w / 4 owns keys [32p, 32p+32) of each tile and output dims [12p, 12p+12)
         const int row = (warp & 3) * 32 + lane;
         const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const bool wact = q0 + (warp & 3) * 32 < S;   // warp-uniform: owns at least one real query row
-        float o[D / 2];
+        constexpr int DP = D / 4;
+        float o[DP];
 #pragma unroll
-        for (int d = 0; d < D / 2; d++) o[d] = 0.0f;
+        for (int d = 0; d < DP; d++) o[d] = 0.0f;
         float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f;
         bool ok = true;
         // O(j) accumulation: o = alpha_j o + O(j)
@@ -421,21 +427,24 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
             if (warp == 0) ATR(j, 8);
             if (ok && wact) {
                 tc_fence_after();
-                const uint32_t tO = t_row + TM_O + (j & 1) * D;
-                uint32_t a16[16], a8[8];
-                if (half == 0) { tmem_ld16(tO, a16); tmem_ld8(tO + 16, a8); }
-                else { tmem_ld8(tO + 24, a8); tmem_ld16(tO + 32, a16); }
+                const uint32_t tO = t_row + TM_O + (j & 1) * D + part * DP;
+                // each load starts at a multiple of its own width: 8 + 4 columns for even parts,
+                // 4 + 8 for odd ones
+                uint32_t a8[8], a4[4];
+                const bool even = (part & 1) == 0;
+                tmem_ld8(tO + (even ? 0 : 4), a8);
+                tmem_ld4(tO + (even ? 8 : 0), a4);
                 tmem_ld_wait();
-                if (half == 0) {
-#pragma unroll
-                    for (int d = 0; d < 16; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a16[d]));
-#pragma unroll
-                    for (int d = 0; d < 8; d++) o[16 + d] = __fmaf_rn(alpha, o[16 + d], __uint_as_float(a8[d]));
-                } else {
+                if (even) {
 #pragma unroll
                     for (int d = 0; d < 8; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a8[d]));
 #pragma unroll
-                    for (int d = 0; d < 16; d++) o[8 + d] = __fmaf_rn(alpha, o[8 + d], __uint_as_float(a16[d]));
+                    for (int d = 0; d < 4; d++) o[8 + d] = __fmaf_rn(alpha, o[8 + d], __uint_as_float(a4[d]));
+                } else {
+#pragma unroll
+                    for (int d = 0; d < 4; d++) o[d] = __fmaf_rn(alpha, o[d], __uint_as_float(a4[d]));
+#pragma unroll
+                    for (int d = 0; d < 8; d++) o[4 + d] = __fmaf_rn(alpha, o[4 + d], __uint_as_float(a8[d]));
                 }
             }
             tc_fence_before();
@@ -445,43 +454,42 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
         };
         for (int i = 0; i < n; i++) {
             const int nvalid = nvalid_of(i), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
-            float* xmax = reinterpret_cast<float*>(sm + OFF_X + (i & 1) * X_SET);   // [2][128]
-            float* xsum = xmax + 2 * BM;                                             // [2][128]
+            float* xmax = reinterpret_cast<float*>(sm + OFF_X + (i & 1) * X_SET);   // [4][128]
+            float* xsum = xmax + 4 * BM;                                             // [4][128]
             ok = ok && mbar_wait(s_full + (i & 1), (i >> 1) & 1, abort_flag, 21);
             ok = __all_sync(0xffffffffu, ok);
             if (warp == 0) ATR(i, 3);
             tc_fence_after();
             float alpha = 1.0f, mloc = -INFINITY;
-            uint32_t r[2][32];
+            uint32_t r[1][32];
             if (ok && wact) {
-                const uint32_t tS = t_row + (i & 1) * BC;
-#pragma unroll
-                for (int cc = 0; cc < 2; cc++)
-                    if (2 * half + cc < nch) tmem_ld32(tS + (2 * half + cc) * 32, r[cc]);
+                if (part < nch) tmem_ld32(t_row + (i & 1) * BC + part * 32, r[0]);
                 tmem_ld_wait();
-                mloc = tile_row_max(r, half, nch, nvalid, c1);
+                mloc = tile_row_max<1>(r, part, nch, nvalid, c1);
             }
             if (warp == 0) ATR(i, 4);
-            xmax[half * BM + row] = mloc;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            xmax[part * BM + row] = mloc;
+            asm volatile("bar.sync 1, 512;" ::: "memory");
             if (warp == 0) ATR(i, 5);
-            const float m_new = fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row]));
+            const float m_new = fmaxf(fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row])),
+                                      fmaxf(xmax[2 * BM + row], xmax[3 * BM + row]));
             float lsum = 0.0f;
             if (ok && wact) {
                 alpha = exp2f(m_i - m_new);
-                uint8_t* pbh = sm + OFF_P + (i & 1) * P_SET + half * P_BLK;
-                lsum = tile_probs(r, half, nch, nvalid, c1, m_new, row, pbh, pbh + P_BYTES);
+                uint8_t* ps = sm + OFF_P + (i & 1) * P_SET;
+                lsum = tile_probs<1>(r, part, nch, nvalid, c1, m_new, row, ps, ps + P_BYTES);
             }
             fence_async_smem();   // P is read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + (i & 1));
             if (warp == 0) ATR(i, 6);
-            xsum[half * BM + row] = lsum;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
+            xsum[part * BM + row] = lsum;
+            asm volatile("bar.sync 1, 512;" ::: "memory");
             if (warp == 0) ATR(i, 7);
             if (ok && wact) {
-                l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(xsum[row], xsum[BM + row]));
+                l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(__fadd_rn(xsum[row], xsum[BM + row]),
+                                                                 __fadd_rn(xsum[2 * BM + row], xsum[3 * BM + row])));
                 m_i = m_new;
             }
             if (i >= 1) accumulate(i - 1, alpha_prev);
@@ -489,18 +497,18 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
         }
         if (n >= 1) accumulate(n - 1, alpha_prev);
 
-        const int qr = q0 + row, d0 = half * (D / 2);
+        const int qr = q0 + row, d0 = part * DP;
         if (ok && qr < S && nsplit > 1) {   // partial result of this key range, merged by the combine pass
             const size_t R = (size_t)(gridDim.z / nsplit) * S, rr = (size_t)split * R + (size_t)b * S + qr;
             float4* dst = reinterpret_cast<float4*>(opart + rr * E + h * D + d0);
 #pragma unroll
-            for (int d = 0; d < D / 2; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-            if (half == 0) reinterpret_cast<float2*>(mlpart)[rr * H + h] = make_float2(m_i, l_i);
+            for (int d = 0; d < DP; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+            if (part == 0) reinterpret_cast<float2*>(mlpart)[rr * H + h] = make_float2(m_i, l_i);
         } else if (ok && qr < S) {
             const float inv = __fdiv_rn(1.0f, l_i);
             float4* dst = reinterpret_cast<float4*>(out + ((size_t)b * S + qr) * E + h * D + d0);
 #pragma unroll
-            for (int d = 0; d < D / 2; d += 4)
+            for (int d = 0; d < DP; d += 4)
                 dst[d / 4] = make_float4(__fmul_rn(o[d], inv), __fmul_rn(o[d + 1], inv), __fmul_rn(o[d + 2], inv),
                                          __fmul_rn(o[d + 3], inv));
         }
@@ -511,7 +519,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
     if (trb && tid == 0)
         for (int j = 0; j < 40 * 10; j++) out[(size_t)(j / D) * E + j % D] = (float)trc[j];
 #endif
-    if (warp == 8) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }

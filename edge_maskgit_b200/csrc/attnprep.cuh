@@ -17,11 +17,11 @@ constexpr uint32_t P_BYTES = 2 * P_BLK;
 constexpr uint32_t PREP_ROW = Q_BYTES / BM + K_BYTES / BC + VT_BYTES / BC;   // 352 bytes per row
 // attention kernel shared memory: Q | K x2 | V^T x2 | (P_hi, P_lo) x2 | row max / sum exchange x2 | barriers
 constexpr uint32_t OFF_Q = 0, OFF_K = OFF_Q + Q_BYTES, OFF_V = OFF_K + 2 * K_BYTES, OFF_P = OFF_V + 2 * VT_BYTES,
-                   P_SET = 2 * P_BYTES, OFF_X = OFF_P + 2 * P_SET, X_SET = 4 * BM * 4, OFF_BAR = OFF_X + 2 * X_SET;
+                   P_SET = 2 * P_BYTES, OFF_X = OFF_P + 2 * P_SET, X_SET = 8 * BM * 4, OFF_BAR = OFF_X + 2 * X_SET;
 constexpr uint32_t SMEM = 1024 + OFF_BAR + 256;
 // TMEM: S x2 (128 columns each) at 0 / 128, O tile x2 (48 columns each) at 256 / 304
 constexpr uint32_t TMEM_COLS = 512, TM_O = 256;
-constexpr int THREADS = 288;   // 8 softmax warps + 1 MMA / copy warp
+constexpr int THREADS = 544;   // 16 softmax warps + 1 MMA / copy warp
 constexpr float LOG2E = 1.4426950408889634f;
 }  // namespace fa
 
