@@ -607,6 +607,15 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
     static const int cand8[4][2] = {{16, 4}, {32, 4}, {48, 6}, {64, 4}}, cand8p[4][2] = {{16, 2}, {32, 4}, {48, 6}, {64, 4}},
                      cand16[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
     const auto& cand = fused_quant ? cand16 : prep ? cand8p : cand8;
+    // Many waves (the CTAs will run persistent): the wave count no longer separates the widths;
+    // 32-wide tiles with four 8-column promotion warps and 8-block chunks measured fastest there
+    // (config 5: 73.7 -> 67.6 ms against the 64-wide tiles the wave rule picks).
+    if (!fused_quant && (long)((N + 63) / 64) * mt > 148L * MGC_QGEMM_MINB && K % 256 == 0) {
+        bn = 32;
+        cg = 4;
+        cb = chunk(bn, cg);
+        return;
+    }
     long best = -1;
     for (const auto& c : cand) {
         const int tiles_n = (N + c[0] - 1) / c[0];
