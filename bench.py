@@ -1,11 +1,20 @@
 """Headline benchmark: MaskGIT transformer steps/s (config 1: 24 layers, M=257, Q8_0, batch 1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--quant gq8|gq4] [--impl cuda|reference]
+                    [--workload c1|c4|c5|sweep]
 
 One process per GPU (torchrun for N>1); each rank runs its own replica of the config-1 step
 (the path shards by independent images, so there is no collective), timing is on the device
 with CUDA events, max over ranks, and `value` is the whole-job steps/s.  Rank 0 prints ONE
-JSON line.  `--impl reference` times the reference's own CPU implementation instead.
+JSON line.  The default run also reports, as extra keys, the batched decode of config 4
+(64 images sharded over the ranks) and the long-sequence step of config 5 (column-split over
+the ranks).  `--workload sweep` times the 30 isolated qGEMM cases of config 2.
+
+`--impl reference` times the reference's own CPU implementation (its scalar F32 executor,
+mg-cpu, built from the reference sources into oracle/_ref/libmgref.so) on the same workload:
+each step is one full 24-layer M=257 forward on the dequantised twin model, the steps run in
+parallel over the host's cores (one process per forward; mg-cpu itself is single-threaded).
+That arm never loads this repository's CUDA library.
 """
 from __future__ import annotations
 
@@ -84,7 +93,9 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- models
-def ensure_model(quant: str, n_layer: int = 24, twin: bool = False) -> tuple[Path, Path | None]:
+def ensure_model(quant: str, n_layer: int = 24, twin: bool = False, packers=None) -> tuple[Path, Path | None]:
+    """The config-1 GGUF (and its dequantised F32 twin), cached under MODEL_DIR.  `packers`
+    (see synth.make_model) lets a process that must not load the CUDA library build them."""
     from edge_maskgit_b200 import synth
     MODEL_DIR.mkdir(parents=True, exist_ok=True)
     path = MODEL_DIR / f"c1_{quant}_L{n_layer}.gguf"
@@ -92,7 +103,7 @@ def ensure_model(quant: str, n_layer: int = 24, twin: bool = False) -> tuple[Pat
     if not path.exists() or (twin and not tpath.exists()):
         tmp = path.with_suffix(f".tmp{os.getpid()}")
         ttmp = tpath.with_suffix(f".tmp{os.getpid()}") if twin else None
-        synth.make_model(tmp, synth.ModelSpec(n_layer=n_layer, quant=quant), dequant_twin=ttmp)
+        synth.make_model(tmp, synth.ModelSpec(n_layer=n_layer, quant=quant), dequant_twin=ttmp, packers=packers)
         os.replace(tmp, path)
         if twin:
             os.replace(ttmp, tpath)
@@ -100,76 +111,88 @@ def ensure_model(quant: str, n_layer: int = 24, twin: bool = False) -> tuple[Pat
 
 
 # ----------------------------------------------------------------------------- CPU baselines
-def reference_cpu_step_s(quant: str, reps: int = 1) -> tuple[float, str, str]:
-    """Seconds per config-1 forward of the reference's own CPU executor (mg-cpu, scalar F32,
-    single-threaded by construction) on the dequantised twin.  A bounded sample: 1- and
-    2-layer models are timed and the per-layer cost is extrapolated to 24 layers."""
+def _ref_forward_seconds(twin: str) -> float:
+    """One full reference forward (mg-cpu, 24 layers, M=257) on the F32 twin; seconds."""
     from edge_maskgit_b200 import synth
     from oracle import oracle as O
     tok = synth.config1_tokens()
-    if O.ref_available():
-        _, f1 = ensure_model(quant, 1, twin=True)
-        _, f2 = ensure_model(quant, 2, twin=True)
-        t = {}
-        for L, f in ((1, f1), (2, f2)):
-            best = 1e30
-            for _ in range(reps):
-                t0 = time.perf_counter()
-                O.ref_forward(f, tok, 768, L, 2025)
-                best = min(best, time.perf_counter() - t0)
-            t[L] = best
-        per_layer = t[2] - t[1]
-        step = t[1] + 23 * per_layer
-        return step, "reference", (f"mg-cpu F32 executor on the dequantised twin, M=257: 1-layer {t[1]:.2f}s, "
-                                   f"2-layer {t[2]:.2f}s, extrapolated to 24 layers")
-    # reference tree not built on this host: the oracle port, full model
-    p, _ = ensure_model(quant, 24)
-    m = O.OracleModel(p)
     t0 = time.perf_counter()
-    m.forward(tok)
-    return time.perf_counter() - t0, "port", "oracle int8-dot restatement, full 24-layer M=257 forward"
+    O.ref_forward(twin, tok, 768, 24, 2025)
+    return time.perf_counter() - t0
+
+
+def _oracle_packers():
+    """The oracle's packers (pinned byte-for-byte to the reference converter's quant_q8_0 /
+    quant_q4_k by tests/test_oracle.py): the reference arm builds its models with these, so it
+    never loads this repository's CUDA library."""
+    from oracle import oracle as O
+    return O
+
+
+def reference_cpu_step_s(quant: str) -> tuple[float, str, str]:
+    """Seconds of ONE full config-1 forward of the reference's own CPU executor (mg-cpu,
+    scalar F32, single-threaded by construction, mg-cpu.cpp:5,296) on the dequantised twin:
+    the bounded CPU sample of the CUDA arm's cpu_baseline (~25 s on one core)."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        raise RuntimeError("the reference CPU path (oracle/_ref/libmgref.so) is not built")
+    _, twin = ensure_model(quant, 24, twin=True, packers=_oracle_packers())
+    return (_ref_forward_seconds(str(twin)), "reference",
+            "one full 24-layer M=257 forward of mg-cpu (F32 executor) on the dequantised twin, 1 core")
 
 
 def run_reference_arm(args) -> None:
+    """The reference's own CPU implementation on the config-1 workload: each step is one full
+    24-layer M=257 mg-cpu forward; the W + K steps run on a pool of worker processes (one per
+    host core, at most one per step), W untimed, then K timed: value = K / wall seconds."""
+    import multiprocessing as mp
+    from concurrent.futures import ProcessPoolExecutor
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from edge_maskgit_b200 import synth
     from oracle import oracle as O
-    # calibrate once (1- vs 2-layer), then each step times the 1-layer sample and adds the
-    # 23 remaining layers at the calibrated per-layer cost
-    cal, kind, sample = reference_cpu_step_s(args.quant)
-    tok = synth.config1_tokens()
-    step_s = 0.0
-    if kind == "reference":
-        _, f1 = ensure_model(args.quant, 1, twin=True)
-        _, f2 = ensure_model(args.quant, 2, twin=True)
-        t0 = time.perf_counter(); O.ref_forward(f1, tok, 768, 1, 2025); t1 = time.perf_counter() - t0
-        per_layer = (cal - t1) / 23.0
-        for i in range(args.warmup + args.steps):
-            t0 = time.perf_counter()
-            O.ref_forward(f1, tok, 768, 1, 2025)
-            s = time.perf_counter() - t0 + 23 * per_layer
-            if i >= args.warmup:
-                step_s += s
-    else:
-        for i in range(args.warmup + args.steps):
-            s, kind, sample = reference_cpu_step_s(args.quant)
-            if i >= args.warmup:
-                step_s += s
-    step_s /= args.steps
-    v = 1.0 / step_s
+    base = {"impl": "reference", "metric": "transformer steps/s", "unit": "steps/s", "n_gpus": args.gpus,
+            "higher_is_better": True}
+    if not O.ref_available():
+        print(json.dumps({**base, "unavailable": "the reference CPU path (oracle/_ref/libmgref.so) is not built"}),
+              flush=True)
+        return
+    _, twin = ensure_model(args.quant, 24, twin=True, packers=_oracle_packers())
+    cores = os.cpu_count() or 1
+    try:
+        import psutil
+        mem_cap = max(1, int(psutil.virtual_memory().available // (2 << 30)))   # ~2 GB per forward
+    except Exception:
+        mem_cap = cores
+    workers = max(1, min(cores, mem_cap, max(args.steps, args.warmup), 64))
+    ctx = mp.get_context("fork")
+    with ProcessPoolExecutor(max_workers=workers, mp_context=ctx) as ex:
+        if args.warmup:
+            list(ex.map(_ref_forward_seconds, [str(twin)] * args.warmup))
+        t0 = time.perf_counter()
+        per = list(ex.map(_ref_forward_seconds, [str(twin)] * args.steps))
+        wall = time.perf_counter() - t0
+    v = args.steps / wall
+    sample = (f"{args.steps} full 24-layer M=257 forwards of mg-cpu (F32 executor, dequantised {args.quant} twin) "
+              f"on {workers} worker processes; mean single-forward latency {np.mean(per):.2f} s")
     print(json.dumps({
-        "impl": "reference", "metric": "transformer steps/s", "value": v, "unit": "steps/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config1 step-1 forward, 24 layers, M=257, {args.quant}, batch 1"},
-        "cpu_baseline": {"value": v, "unit": "steps/s", "cores": 1, "kind": kind, "sample": sample},
+        **base, "value": v, "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1e3 / args.steps,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config1 step-1 forward, 24 layers, M=257, {args.quant}, batch 1",
+                   "parallelism": f"{workers} host processes, one forward each"},
+        "latency_s_per_forward": float(np.mean(per)),
+        "cpu_baseline": {"value": v, "unit": "steps/s", "cores": workers, "kind": "reference", "sample": sample},
         "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
 # ----------------------------------------------------------------------------- CUDA arm
+def c1_config(quant: str) -> dict:
+    """The config dict of the headline line (identical in the CUDA and the reference arm)."""
+    return {"workload": f"config1 step-1 forward, 24 layers, M=257, {quant}, batch 1",
+            "l2": "inputs larger than L2 (the 190 MB of packed weights are streamed every step)"}
+
+
 def qgemm_algorithmic_bytes(quant: str, M: int = 257) -> tuple[float, int]:
     """Sum over one forward's quantized GEMM launches of the algorithmic bytes
     W_packed + 4*M*K (X f32) + 4*M*N (Y f32) + 4*N (bias) [+ 4*M*N residual]."""
@@ -182,23 +205,44 @@ def qgemm_algorithmic_bytes(quant: str, M: int = 257) -> tuple[float, int]:
     return total, len(shapes)
 
 
-def run_cuda_arm(args) -> None:
+def _dist():
+    """(world, rank, local rank), with the CUDA device set and NCCL up when world > 1."""
     import torch
     import torch.distributed as dist
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    from edge_maskgit_b200 import runtime as rt, synth
+    return world, rank, local
 
-    if rank == 0 or world == 1:
-        path, _ = ensure_model(args.quant)
+
+def _max_over_ranks(vals: list[float], world: int) -> list[float]:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def _barrier(world: int) -> None:
+    import torch.distributed as dist
     if world > 1:
         dist.barrier()
+
+
+def run_cuda_arm(args) -> None:
+    import torch
+
+    world, rank, local = _dist()
+    from edge_maskgit_b200 import runtime as rt, synth
+
+    if rank == 0:
         path, _ = ensure_model(args.quant)
+    _barrier(world)
+    path, _ = ensure_model(args.quant)
     S, V = 257, 2025
     r = rt.CudaRuntime(path, max_rows=S, device=local)
     stream = torch.cuda.ExternalStream(r.stream_handle, device=torch.device("cuda", local))
@@ -207,12 +251,12 @@ def run_cuda_arm(args) -> None:
     tok_dev = torch.from_numpy(tok_host).cuda()
     logits_dev = torch.empty((S, V), dtype=torch.float32, device="cuda")
 
-    # ---- per-kernel profile (eager, CUDA events around each launch): roofline of the qGEMM
+    # ---- per-op split of the step (eager profile, CUDA events around each launch): context only
     r.profile_enable(True)
-    for _ in range(3):
+    for _ in range(2):
         r.forward(tok_host)
     r.profile_reset()
-    for _ in range(5):
+    for _ in range(3):
         r.forward(tok_host)
     prof = {p.op: p for p in r.profile_report()}
     r.profile_enable(False)
@@ -224,8 +268,7 @@ def run_cuda_arm(args) -> None:
     r.sync()
     launches_per_fwd = r.kernel_count()   # kernels in the captured step graph
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk, torch.cuda.stream(stream):
         e0.record(stream)
@@ -242,20 +285,24 @@ def run_cuda_arm(args) -> None:
         t_e2e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = t_e2e0.elapsed_time(t_e2e1)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     r.sync()
-    ms = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    dev_ms, e2e_ms = ms.tolist()
+    # ---- the dominant kernel (qGEMM) as it runs inside the step: a graph of the step's 97
+    # qGEMM launches alone, replayed back to back on the runtime's stream (CUDA events there)
+    q_ms, q_n = r.time_op("MulMat(q)", 1, S, iters=max(20, args.steps))
+    dev_ms, e2e_ms, q_ms = _max_over_ranks([dev_ms, e2e_ms, q_ms], world)
+    extras = {}
+    if not args.no_extras:
+        for name, fn in (("config4", c4_measure), ("config5", c5_measure)):
+            try:
+                extras[name] = fn(max(2, min(args.steps, 3)), 1, world, rank, local)
+            except Exception as e:   # an extra workload must not cost the headline line
+                extras[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     if rank == 0:
         hbm, src = peaks()
         alg, n_q = qgemm_algorithmic_bytes(args.quant)
-        q = prof.get("MulMat(q)")
-        q_ms = q.ms / q.count if q else float("nan")
-        achieved = (alg / n_q) / (q_ms * 1e-3) / 1e9 if q else None
+        achieved = (alg / n_q) / (q_ms / q_n * 1e-3) / 1e9
         traffic = None
         tf = ROOT / "profiles" / f"qgemm_{args.quant}_traffic.txt"
         if tf.exists():
@@ -266,44 +313,45 @@ def run_cuda_arm(args) -> None:
             "metric": "transformer steps/s", "value": world * args.steps / (dev_ms * 1e-3), "unit": "steps/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32",
-            "data": "synthetic",
-            "config": {"workload": f"config1 step-1 forward, 24 layers, M=257, {args.quant}, batch 1 per GPU",
-                       "parallelism": f"replicas x{world} (independent images, no collective)",
-                       "l2": "inputs larger than L2 (190 MB of weights streamed per step)"},
+            "data": "synthetic (seeded N(0,0.02) weights, config-1 step-1 tokens)",
+            "config": c1_config(args.quant),
+            "parallelism": f"replicas x{world} (independent images, no collective)",
             "e2e": {"value": world * args.steps / (e2e_ms * 1e-3), "unit": "steps/s",
                     "h2d_bytes_per_step": int(tok_host.nbytes), "d2h_bytes_per_step": S * V * 4},
             "gpu_launches": launches_per_fwd * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": (achieved / hbm) if achieved else None, "traffic": traffic,
-                         "kernel": "qgemm (MulMat(q)), mean over the 97 launches of one step",
-                         "peak_source": src},
-            "kernel_ms_per_step": {k: p.ms / 5 for k, p in prof.items()},
+                         "frac": achieved / hbm, "traffic": traffic,
+                         "kernel": f"qgemm (MulMat(q)): a CUDA graph of the step's {q_n} qGEMM launches alone, "
+                                   f"{q_ms:.4f} ms per replay = {q_ms / q_n * 1e3:.2f} us per launch; algorithmic "
+                                   f"bytes {alg / n_q / 1e6:.3f} MB per launch (mean of the {n_q})",
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src},
+            "qgemm_ms_per_step": q_ms,
+            "eager_profile_ms_per_step": {k: p.ms / 3 for k, p in prof.items()},
             "clocks": clk.summary(),
+            **extras,
         }
         if world == 1 and not args.no_cpu_baseline:
-            s, kind, sample = reference_cpu_step_s(args.quant)
-            out["cpu_baseline"] = {"value": 1.0 / s, "unit": "steps/s", "cores": 1 if kind == "reference" else os.cpu_count(),
-                                   "kind": kind, "sample": sample}
+            try:
+                s_, kind, sample = reference_cpu_step_s(args.quant)
+                out["cpu_baseline"] = {"value": 1.0 / s_, "unit": "steps/s", "cores": 1, "kind": kind,
+                                       "sample": sample}
+            except Exception as e:
+                out["cpu_baseline"] = {"unavailable": str(e)}
         print(json.dumps(out), flush=True)
     r.close()
     if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
 
 
-def run_tp_workload(args) -> None:
+# ----------------------------------------------------------------------------- config 5
+def c5_measure(steps: int, warmup: int, world: int, rank: int, local: int) -> dict:
     """Config 5: step-1 forward at M=4097 (64x64 tokens + class), batch 4, Q4_K, column-split
-    over the ranks with NCCL all-gathers.  Total work is fixed, so scaling is strong."""
+    over the ranks with NCCL all-gathers; ms per step, max over ranks (strong scaling)."""
     import torch
-    import torch.distributed as dist
     from edge_maskgit_b200 import synth
     from edge_maskgit_b200.tp import TPForward
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     MODEL_DIR.mkdir(parents=True, exist_ok=True)
     path = MODEL_DIR / "c5_gq4_n4096.gguf"
     spec = synth.ModelSpec(n_tokens=4096, quant="gq4")
@@ -311,121 +359,200 @@ def run_tp_workload(args) -> None:
         tmp = path.with_suffix(f".tmp{os.getpid()}")
         synth.make_model(tmp, spec)
         os.replace(tmp, path)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     tp = TPForward(path, rank, world)
     tokens = np.tile(synth.config1_tokens(spec), (4, 1))
     tokens[:, 0] = 1024 + np.array([207, 1, 500, 999])
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         tp.forward(tokens)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        logits = tp.forward(tokens)
+    for _ in range(steps):
+        tp.forward(tokens)
     e1.record()
     torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
+    ms = _max_over_ranks([e0.elapsed_time(e1)], world)[0]
+    del tp
+    return {"workload": "config5 step-1 forward, 24 layers, M=4097, batch 4, gq4",
+            "parallelism": f"column-split tensor parallel x{world}, NCCL all-gather", "scaling": "strong",
+            "steps": steps, "ms_per_step": ms / steps, "steps_per_s": steps / (ms * 1e-3)}
+
+
+def run_tp_workload(args) -> None:
+    world, rank, local = _dist()
+    m = c5_measure(args.steps, args.warmup, world, rank, local)
     if rank == 0:
         print(json.dumps({
-            "metric": "transformer steps/s", "value": args.steps / (ms * 1e-3), "unit": "steps/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "metric": "transformer steps/s", "value": m["steps_per_s"], "unit": "steps/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
-            "data": "synthetic",
-            "config": {"workload": "config5 step-1 forward, 24 layers, M=4097, batch 4, gq4",
-                       "parallelism": f"column-split tensor parallel x{world}, NCCL all-gather"},
+            "data": "synthetic", "config": {"workload": m["workload"], "parallelism": m["parallelism"]},
         }), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
 
 
-def run_decode_workload(args) -> None:
-    """Config 4: batched decode of 64 images (classes from default_rng(7), seed 7+i), Q8_0, 8 steps,
-    sharded by image over the ranks (each rank batches its images into one forward per step);
-    one all-gather of the token grids at the end.  Total work is fixed: strong scaling.  Each
-    timed step is one full 8-step decode of the 64 images; timing is CUDA events on the runtime's
+# ----------------------------------------------------------------------------- config 4
+def c4_measure(steps: int, warmup: int, world: int, rank: int, local: int) -> dict:
+    """Config 4: batched decode of 64 images (classes from default_rng(7), seed 7+i), Q8_0, 8
+    steps, sharded by image over the ranks (each rank batches its images into one forward per
+    step); one all-gather of the token grids at the end.  Total work is fixed: strong scaling.
+    Each timed step is one full 8-step decode of the 64 images; CUDA events on the runtime's
     stream (the loop is host-driven, so host gaps count), max over ranks."""
     import torch
-    import torch.distributed as dist
     from edge_maskgit_b200 import runtime as rt, shard
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     if rank == 0:
-        path, _ = ensure_model("gq8")
-    if world > 1:
-        dist.barrier()
+        ensure_model("gq8")
+    _barrier(world)
     path, _ = ensure_model("gq8")
     n_img, S = 64, 257
     classes, seeds = shard.batch_classes(n_img), shard.batch_seeds(n_img)
     lo, hi = shard.shard_range(n_img, rank, world)
     r = rt.CudaRuntime(path, max_rows=S * max(1, hi - lo), device=local)
     stream = torch.cuda.ExternalStream(r.stream_handle, device=torch.device("cuda", local))
-    gen = lambda c, sd, steps, t: r.generate(c, sd, steps, t)
-    for _ in range(args.warmup):
+    gen = lambda c, sd, st, t: r.generate(c, sd, st, t)
+    for _ in range(warmup):
         shard.decode_shard(gen, classes, seeds, rank, world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         local_tok = shard.decode_shard(gen, classes, seeds, rank, world)
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        grids = shard.gather_tokens(local_tok, n_img, S)
-    else:
-        grids = local_tok
-    ms = float(ms.item())
+    ms = _max_over_ranks([e0.elapsed_time(e1)], world)[0]
+    grids = shard.gather_tokens(local_tok, n_img, S) if world > 1 else local_tok
+    r.close()
+    return {"workload": "config4 batched decode, 64 images x 8 steps, gq8, seq 257",
+            "parallelism": f"images sharded over {world} rank(s), one all-gather of the token grids",
+            "scaling": "strong", "steps": steps, "ms_per_decode": ms / steps,
+            "images_per_s": n_img * steps / (ms * 1e-3),
+            "tokens_checksum": int(np.asarray(grids, dtype=np.int64).sum())}
+
+
+def run_decode_workload(args) -> None:
+    world, rank, local = _dist()
+    m = c4_measure(args.steps, args.warmup, world, rank, local)
     if rank == 0:
         print(json.dumps({
-            "metric": "images/s", "value": n_img * args.steps / (ms * 1e-3), "unit": "images/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "metric": "images/s", "value": m["images_per_s"], "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_decode"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
             "data": "synthetic",
-            "config": {"workload": "config4 batched decode, 64 images x 8 steps, gq8, seq 257",
-                       "parallelism": f"images sharded over {world} rank(s), one all-gather of the token grids",
-                       "tokens_checksum": int(np.asarray(grids, dtype=np.int64).sum())},
+            "config": {"workload": m["workload"], "parallelism": m["parallelism"],
+                       "tokens_checksum": m["tokens_checksum"]},
         }), flush=True)
     if world > 1:
+        import torch.distributed as dist
         dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- config 2
+SWEEP_MS = (257, 1025, 4097)
+SWEEP_SHAPES = ((768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 2025))   # (K, N)
+
+
+def sweep_bytes(wtype: int, M: int, K: int, N: int) -> int:
+    """Algorithmic bytes of one isolated quantized linear (no bias): W_packed + 4MK + 4MN."""
+    wb = N * K * 34 // 32 if wtype == 8 else N * K * 144 // 256
+    return wb + 4 * M * K + 4 * M * N
+
+
+def run_sweep(args) -> None:
+    """Config 2: the 30 isolated qGEMM cases (M in {257,1025,4097} x 5 (K,N) x {Q8_0,Q4_K}), each
+    through the public entry point mgc_qgemm (f32 X in: quantizer + int8-dot GEMM, f32 Y out).
+    X = default_rng(0).standard_normal((M,K)), W = 0.02 * standard_normal((N,K)) from the same
+    generator.  L2 is defeated by rotating over enough copies of (W, X, Y) that one pass over
+    them exceeds 3x the 126 MB L2; the calls are captured in a CUDA graph (no host launch gaps)
+    and timed with CUDA events; us per call = graph time / calls."""
+    import torch
+    world, rank, local = _dist()
+    if rank != 0:
+        return
+    from edge_maskgit_b200 import runtime as rt
+    hbm, src = peaks()
+    tc_peak = 4500.0   # nominal dense int8 TOP/s of a B200 (no measured int8 figure exists here)
+    cases = []
+    for wtype in (8, 12):
+        for M in SWEEP_MS:
+            for K, N in SWEEP_SHAPES:
+                rng = np.random.default_rng(0)
+                X = rng.standard_normal((M, K), dtype=np.float32)
+                W = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+                blocks = rt.pack_q8_0(W) if wtype == 8 else rt.pack_q4_k(W)
+                set_bytes = sweep_bytes(wtype, M, K, N)
+                R = int(min(64, max(2, -(-3 * 126e6 // set_bytes))))
+                qws = [rt.QWeight(wtype, blocks, N, K) for _ in range(R)]
+                xs = [torch.from_numpy(X).cuda() for _ in range(R)]
+                ys = [torch.empty((M, N), dtype=torch.float32, device="cuda") for _ in range(R)]
+                for i in range(R):   # warm-up (grows the library's activation scratch outside the capture)
+                    qws[i].qgemm(xs[i], out=ys[i])
+                torch.cuda.synchronize()
+                calls = R * max(1, -(-40 // R))
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for c in range(calls):
+                        qws[c % R].qgemm(xs[c % R], out=ys[c % R])
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 3
+                e0.record()
+                for _ in range(reps):
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+                gbs = set_bytes / (us * 1e-6) / 1e9
+                tops = 2.0 * M * N * K / (us * 1e-6) / 1e12
+                cases.append({"wtype": "Q8_0" if wtype == 8 else "Q4_K", "M": M, "K": K, "N": N, "us": round(us, 3),
+                              "alg_bytes": set_bytes, "GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+                              "int8_TOPS": round(tops, 1), "tc_frac_nominal": round(tops / tc_peak, 4),
+                              "l2_rotation": R})
+                del g, qws, xs, ys
+                torch.cuda.empty_cache()
+    big = [c["hbm_frac"] for c in cases if c["M"] >= 1025]
+    print(json.dumps({
+        "metric": "qGEMM fraction of the HBM roofline (config-2 sweep, mean over M>=1025)",
+        "value": float(np.mean(big)), "unit": "fraction", "n_gpus": 1, "steps": 3, "warmup": 1,
+        "higher_is_better": True, "dtype": "int8-dot/f32", "data": "synthetic (config 2: seed 0)",
+        "config": {"workload": "config2 isolated qGEMM sweep, 30 cases, quantizer + GEMM per call",
+                   "l2": "rotated over >= 3x L2 of (W, X, Y) copies"},
+        "peak": {"hbm_gbs": hbm, "source": src, "int8_tops_nominal": tc_peak},
+        "mean_hbm_frac_m257": float(np.mean([c["hbm_frac"] for c in cases if c["M"] == 257])),
+        "cases": cases,
+    }), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None,
-                    help="timed steps (default: 300 for c1, 10 for c5, 20 for the reference arm)")
+                    help="timed steps (default: 300 for c1, 10 for c5, 3 for c4, 20 for the reference arm)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--quant", default="gq8", choices=["gq8", "gq4"])
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "c5"],
+    ap.add_argument("--no-extras", action="store_true", help="skip the config-4 / config-5 keys of the c1 line")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "c5", "sweep"],
                     help="c1: the headline config-1 step (default); c4: 64-image batched decode; "
-                         "c5: M=4097 tensor-parallel step")
+                         "c5: M=4097 tensor-parallel step; sweep: the 30 isolated qGEMM cases of config 2")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 20 if args.impl == "reference" else 10 if args.workload == "c5" else 3 if args.workload == "c4" else 300
-    if args.workload == "c5" and args.impl == "cuda":
-        run_tp_workload(args)
-        return
-    if args.workload == "c4" and args.impl == "cuda":
-        run_decode_workload(args)
-        return
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.workload == "c5":
+        run_tp_workload(args)
+    elif args.workload == "c4":
+        run_decode_workload(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_cuda_arm(args)
 

@@ -47,6 +47,7 @@ _SIGS = {
     "mgc_runtime_stream": (P, [P]),
     "mgc_generate": (I, [P, I, P, P, I, F, P]),
     "mgc_runtime_kernel_count": (I, [P]),
+    "mgc_runtime_time_op": (I, [P, C.c_char_p, I, I, I, C.POINTER(F), C.POINTER(I)]),
     "mgc_profile_enable": (I, [P, I]),
     "mgc_profile_reset": (I, [P]),
     "mgc_profile_report": (I, [P, C.c_char_p, C.c_size_t]),

@@ -321,14 +321,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const float c1 = scale * LOG2E;   // scores in the base-2 domain
-#ifdef MGC_ATTN_TRACE   // development trace: CTA (0,0,0) records per-tile phase stamps (SM cycles)
-    __shared__ int trc[40 * 10];
-    const long long t_0 = clock64();
-    const bool trb = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-#define ATR(i, k) do { if (trb && lane == 0 && (i) < 40) trc[(i) * 10 + (k)] = (int)(clock64() - t_0); } while (0)
-#else
-#define ATR(i, k) ((void)0)
-#endif
 
     if (warp == MMA_WARP) {
         // ------------------------------------------------------------------ MMA + copy warp
@@ -366,12 +358,10 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
                     for (int k = 0; k < D / 16; k++) mma_f16(tmem + (i & 1) * BC, dq + 2 * k, dk + 2 * k, idesc_s, k > 0);
                     mma_commit(s_full + (i & 1));
                     if (i == 0) more_loads();
-                    ATR(i, 0);
                 }
                 if (i >= 1) {
                     const int j = i - 1, nmma = (nvalid_of(j) + 15) & ~15;
                     if (!(ok = mbar_wait(p_full + (j & 1), (j >> 1) & 1, abort_flag, 25))) break;
-                    ATR(j, 1);
                     if (nk < n) load_k(nk++);   // S(j) has completed: its K buffer is free
                     if (!(ok = mbar_wait(v_full + (j & 1), (j >> 1) & 1, abort_flag, 26))) break;
                     if (j >= 2 && !(ok = mbar_wait(o_free + (j & 1), ((j - 2) >> 1) & 1, abort_flag, 27))) break;
@@ -394,7 +384,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
                     }
                     mma_commit(o_full + (j & 1));
                     mma_commit(v_free + (j & 1));
-                    ATR(j, 2);
                     if (nv < n) {   // V(j+2) into the buffer PV(j) read
                         if (!(ok = mbar_wait(v_free + (j & 1), (j >> 1) & 1, abort_flag, 28))) break;
                         load_v(nv++);
@@ -424,7 +413,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
         auto accumulate = [&](int j, float alpha) {
             ok = ok && mbar_wait(o_full + (j & 1), (j >> 1) & 1, abort_flag, 22);
             ok = __all_sync(0xffffffffu, ok);
-            if (warp == 0) ATR(j, 8);
             if (ok && wact) {
                 tc_fence_after();
                 const uint32_t tO = t_row + TM_O + (j & 1) * D + part * DP;
@@ -450,7 +438,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_free + (j & 1));
-            if (warp == 0) ATR(j, 9);
         };
         for (int i = 0; i < n; i++) {
             const int nvalid = nvalid_of(i), nmma = (nvalid + 15) & ~15, nch = (nmma + 31) / 32;
@@ -458,7 +445,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
             float* xsum = xmax + 4 * BM;                                             // [4][128]
             ok = ok && mbar_wait(s_full + (i & 1), (i >> 1) & 1, abort_flag, 21);
             ok = __all_sync(0xffffffffu, ok);
-            if (warp == 0) ATR(i, 3);
             tc_fence_after();
             float alpha = 1.0f, mloc = -INFINITY;
             uint32_t r[1][32];
@@ -467,10 +453,8 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
                 tmem_ld_wait();
                 mloc = tile_row_max<1>(r, part, nch, nvalid, c1);
             }
-            if (warp == 0) ATR(i, 4);
             xmax[part * BM + row] = mloc;
             asm volatile("bar.sync 1, 512;" ::: "memory");
-            if (warp == 0) ATR(i, 5);
             const float m_new = fmaxf(fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row])),
                                       fmaxf(xmax[2 * BM + row], xmax[3 * BM + row]));
             float lsum = 0.0f;
@@ -483,10 +467,8 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + (i & 1));
-            if (warp == 0) ATR(i, 6);
             xsum[part * BM + row] = lsum;
             asm volatile("bar.sync 1, 512;" ::: "memory");
-            if (warp == 0) ATR(i, 7);
             if (ok && wact) {
                 l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(__fadd_rn(xsum[row], xsum[BM + row]),
                                                                  __fadd_rn(xsum[2 * BM + row], xsum[3 * BM + row])));
@@ -515,10 +497,6 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
     }
     tc_fence_before();
     __syncthreads();
-#ifdef MGC_ATTN_TRACE
-    if (trb && tid == 0)
-        for (int j = 0; j < 40 * 10; j++) out[(size_t)(j / D) * E + j % D] = (float)trc[j];
-#endif
     if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);

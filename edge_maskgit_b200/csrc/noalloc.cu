@@ -40,6 +40,10 @@ extern "C" int mgc_qgemm_noalloc(const mgc_qweight* wq, const float* x_dev, int 
     if (w.wtype != MGC_Q8_0 && w.wtype != MGC_Q4_K) {
         return fail("mgc_qgemm_noalloc: weight must be Q8_0 or Q4_K");
     }
+    if (w.K % 128 != 0 || (w.wtype == MGC_Q4_K && w.K % 256 != 0)) {
+        return fail("mgc_qgemm_noalloc: unsupported shape K = " + std::to_string(w.K) +
+                    " (K must be a multiple of 128, 256 for Q4_K)");
+    }
     const int Mpad = mgc::round_up(M, 128);
     if ((size_t)Mpad * (size_t)w.K > kMaxElems) {
         return fail("mgc_qgemm_noalloc: round_up(M,128) * K = " + std::to_string((size_t)Mpad * w.K) +
@@ -53,7 +57,9 @@ extern "C" int mgc_qgemm_noalloc(const mgc_qweight* wq, const float* x_dev, int 
     {
         // First call on a device: resolve the scratch array's device address (the symbol's
         // host-side name is not a device pointer).  Make this first call before any stream
-        // capture.
+        // capture.  The address is cached for the life of the process: after a
+        // cudaDeviceReset the module is reloaded and the array may move, so the library must
+        // not be used across a device reset.
         std::lock_guard<std::mutex> lk(g_mu);
         if (!g_scratch_ptr[dev]) {
             void* p = nullptr;
@@ -69,10 +75,24 @@ extern "C" int mgc_qgemm_noalloc(const mgc_qweight* wq, const float* x_dev, int 
     a.Mpad = Mpad;
     a.q = (int8_t*)base;
     cudaStream_t st = (cudaStream_t)stream;
+    // An error left by earlier, unrelated work is reported as such, not as this call's failure.
+    const cudaError_t prior = cudaGetLastError();
+    if (prior != cudaSuccess) {
+        return fail(std::string("mgc_qgemm_noalloc: a CUDA error was pending before this call: ") +
+                    cudaGetErrorString(prior));
+    }
     mgc::launch_quant_act_tiled(x_dev, M, w.K, a, w.wtype == MGC_Q4_K, st);
-    if (cudaPeekAtLastError() != cudaSuccess ||
-        mgc::launch_qgemm(w, a, M, bias_dev, act, resid_dev, y_dev, st) != 0) {
-        return fail(std::string("mgc_qgemm_noalloc: launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+    const cudaError_t eq = cudaGetLastError();
+    if (eq != cudaSuccess) {
+        return fail(std::string("mgc_qgemm_noalloc: quantizer launch failed: ") + cudaGetErrorString(eq));
+    }
+    const int rc = mgc::launch_qgemm(w, a, M, bias_dev, act, resid_dev, y_dev, st);
+    if (rc == -2) {
+        return fail("mgc_qgemm_noalloc: unsupported GEMM configuration M = " + std::to_string(M) + ", N = " +
+                    std::to_string(w.N) + ", K = " + std::to_string(w.K));
+    }
+    if (rc != 0) {
+        return fail(std::string("mgc_qgemm_noalloc: GEMM launch failed: ") + cudaGetErrorString(cudaGetLastError()));
     }
     return 0;
 }

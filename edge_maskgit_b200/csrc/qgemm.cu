@@ -25,6 +25,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <algorithm>
+#include <atomic>
 
 #ifndef MGC_QGEMM_MINB
 #define MGC_QGEMM_MINB 1     // CTAs per SM the register budget is sized for
@@ -64,21 +65,6 @@ __device__ __forceinline__ float act_apply(float v, int a) {
     return v;
 }
 
-// Development trace (compile with -DMGC_QGEMM_TRACE): CTA (0,0) stores globaltimer stamps
-// into its own output tile instead of its outputs.  Per 4-block chunk: [0,128) producer
-// issue, [128,256) MMA start, [256,768) MMA committed, [768,1280) warp 2 sees the dot
-// tiles, [1280,1792) warp 2 done.
-#ifdef MGC_QGEMM_TRACE
-__device__ __forceinline__ void trace(const QGemmArgs& p, int idx, long long t0) {
-    if (blockIdx.x == 0 && blockIdx.y == 0 && idx < 1888) {
-        const long long t = clock64();   // SM cycles since kernel entry
-        p.y[(size_t)(idx / 32) * p.N + (idx % 32)] = (float)(t - t0);   // inside this CTA's tile
-    }
-}
-#define TRACE(i) trace(p, (i), t_start)
-#else
-#define TRACE(i) ((void)0)
-#endif
 
 template <int BN, int CG, bool Q4K, int CB>
 struct QGemmCfg {
@@ -146,10 +132,6 @@ qgemm_kernel(const QGemmArgs p) {
             mt_ = blockIdx.y;
         }
     };
-#ifdef MGC_QGEMM_TRACE
-    const long long t_start = clock64();
-    long long g_start; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(g_start));
-#endif
     const int nkc = p.K / (32 * CB);
     const int kz = blockIdx.z, kc0 = kz * p.cps, nloc = max(0, min(nkc, kc0 + p.cps) - kc0);
 
@@ -199,7 +181,6 @@ qgemm_kernel(const QGemmArgs p) {
             const int npre = nloc < NST ? nloc : NST;
             tile_of(0, n0, mt);
             for (int i = 0; i < npre; i++) {
-                TRACE(i);
                 mbar_arrive_expect_tx(&full[i], C::TX_BYTES);
                 copy_w(i, i);
                 last_it[i] = 0;
@@ -212,7 +193,6 @@ qgemm_kernel(const QGemmArgs p) {
                 for (int i = ti == 0 ? npre : 0; i < nloc; i++) {
                     const int gc = ti * nloc + i, s = gc % NST, it = gc / NST;
                     if (!(go = mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1))) break;
-                    TRACE(i);
                     mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
                     copy_w(i, gc);
                     copy_a(i, gc);
@@ -234,7 +214,6 @@ qgemm_kernel(const QGemmArgs p) {
                 if (!mbar_wait(&full[s], it & 1, abort_flag, 2)) break;
                 if (!mbar_wait(&tempty[g], (ug & 1) ^ 1, abort_flag, 3)) break;
                 tc_fence_after();
-                TRACE(128 + kc);
                 const uint32_t a_base = smem_u32(smem + s * C::STAGE), b_base = a_base + C::OFF_B;
                 // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
 #pragma unroll
@@ -245,7 +224,6 @@ qgemm_kernel(const QGemmArgs p) {
                 }
                 mma_commit(&tfull[g]);   // the chunk's 4 dot tiles are ready
                 mma_commit(&empty[s]);   // its shared-memory operands may be overwritten
-                TRACE(256 + kc);
             }
         }
         griddep_launch();
@@ -268,13 +246,11 @@ qgemm_kernel(const QGemmArgs p) {
         auto issue = [&](uint32_t (&I)[BATCH][CW], int t) {
             const int kc = t / BPC, jb = t % BPC, g = kc % NGRP;
             if (jb == 0) {
-                if (warp == 2 && lane == 0) TRACE(864 + kc);
                 bool w = mbar_wait(&full[kc % NST], (kc / NST) & 1, abort_flag, 4) &&
                          mbar_wait(&tfull[g], (kc / NGRP) & 1, abort_flag, 5);
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) return;
                 tc_fence_after();
-                if (warp == 2 && lane == 0) TRACE(768 + kc);
             }
 #pragma unroll
             for (int jj = 0; jj < BATCH; jj++) {
@@ -296,7 +272,6 @@ qgemm_kernel(const QGemmArgs p) {
         // wait for batch t's loads, pin the registers after the wait, release the TMEM group
         auto landed = [&](uint32_t (&I)[BATCH][CW], int t) {
             tmem_ld_wait();
-            if (warp == 2 && lane == 0 && t % BPC == 0) TRACE(800 + t / BPC);
 #pragma unroll
             for (int jj = 0; jj < BATCH; jj++)
 #pragma unroll
@@ -349,7 +324,6 @@ qgemm_kernel(const QGemmArgs p) {
                 }
             }
             if (jb == BPC - 1) {   // chunk done: its shared-memory stage may be refilled
-                if (warp == 2 && lane == 0) TRACE(1280 + kc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
@@ -370,18 +344,12 @@ qgemm_kernel(const QGemmArgs p) {
             landed(I, t);
             promote(I, t);
         }
-        if (lane == 0) TRACE(1800 + warp);
         griddep_launch();
         griddep_wait();   // the residual and the output buffers belong to the preceding kernels' chain
         // epilogue: bias -> act -> residual (mg-opencl.cpp:481-493)
         float acc[CW];
 #pragma unroll
         for (int c = 0; c < CW / 2; c++) unpack2(acc2[c], acc[2 * c], acc[2 * c + 1]);
-#ifdef MGC_QGEMM_TRACE
-        const bool keep_stamps = true;   // trace build: no output stores
-#else
-        constexpr bool keep_stamps = false;
-#endif
         if (p.nsplit > 1) {
             // split-K: publish this split's partial, then the last CTA of the tile sums all
             // partials in split order (deterministic) and runs the epilogue below
@@ -422,7 +390,7 @@ qgemm_kernel(const QGemmArgs p) {
                 }
             }
         }
-        const bool store = m < p.M && !*abort_flag && !keep_stamps;
+        const bool store = m < p.M && !*abort_flag;
         const int nbase = n0 + c0;
         float vals[CW];
         if (store) {
@@ -510,16 +478,6 @@ qgemm_kernel(const QGemmArgs p) {
         }   // tiles
     }
 
-    if (warp >= 2 && lane == 0) TRACE(1792 + warp);
-#ifdef MGC_QGEMM_TRACE
-    if (threadIdx.x == 64 && !(blockIdx.x == 0 && blockIdx.y == 0)) {   // per-CTA [start, end] stamps (low 32 bits)
-        long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        int n0, mt;
-        tile_of(0, n0, mt);
-        p.y[(size_t)mt * 128 * p.N + n0] = __int_as_float((int)(g_start & 0x7fffffff));
-        p.y[(size_t)mt * 128 * p.N + n0 + 1] = __int_as_float((int)(t & 0x7fffffff));
-    }
-#endif
 done:
     tc_fence_before();
     __syncthreads();
@@ -555,13 +513,17 @@ int qgemm_prepare() {
     return rc;
 }
 
-static int sm_count() {
-    static int n[64] = {};
+static int sm_count() {   // SMs of the current device (cached per device; concurrent first calls agree)
+    static std::atomic<int> n[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
-    if (n[dev] == 0 && cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n[dev] = 148;
-    return n[dev];
+    int v = n[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        n[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
 }
 
 template <int BN, int CG, bool Q4K, int CB>
@@ -584,19 +546,22 @@ static int run_qgemm(QGemmArgs a, cudaStream_t st) {
 // MGC_QGEMM_CFG="BN,CG[,CB]" overrides the heuristic (used to sweep shapes); MGC_QGEMM_CB=4
 // keeps 4-block chunks everywhere.
 static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, int& cg, int& cb) {
-    static int fbn = -1, fcg = 0, fcb = 0, cb_max = 8;
-    if (fbn < 0) {
-        fbn = 0;
-        if (const char* e = std::getenv("MGC_QGEMM_CFG")) std::sscanf(e, "%d,%d,%d", &fbn, &fcg, &fcb);
-        if (const char* e = std::getenv("MGC_QGEMM_CB")) cb_max = std::atoi(e) == 4 ? 4 : 8;
-    }
+    struct Overrides { int fbn = 0, fcg = 0, fcb = 0, cb_max = 8; };
+    static const Overrides ov = [] {   // read once (thread-safe static initialisation)
+        Overrides o;
+        if (const char* e = std::getenv("MGC_QGEMM_CFG")) std::sscanf(e, "%d,%d,%d", &o.fbn, &o.fcg, &o.fcb);
+        if (const char* e = std::getenv("MGC_QGEMM_CB")) o.cb_max = std::atoi(e) == 4 ? 4 : 8;
+        return o;
+    }();
+    const int fbn = ov.fbn, fcg = ov.fcg, fcb = ov.fcb, cb_max = ov.cb_max;
+    const long wave = (long)sm_count() * MGC_QGEMM_MINB;   // CTAs of one wave (the persistent grid)
     // 8-block chunks (half the pipeline hand-offs per block) where instantiated and K allows
     auto chunk = [&](int b, int g) { return cb_max == 8 && K % 256 == 0 && (b == 16 || (b == 32 && g >= 2)) ? 8 : 4; };
     if (fbn && (!fused_quant || (fbn % 32 == 0 && fbn / fcg == 16)) && (!prep || fbn / fcg == 8 || fbn / fcg == 16)) {
         bn = fbn; cg = fcg; cb = fcb ? fcb : chunk(bn, cg);
         return;
     }
-    // Pick the width whose tile grid fills the 148 SMs in the fewest waves, weighing a wave by
+    // Pick the width whose tile grid fills the SMs in the fewest waves, weighing a wave by
     // its per-CTA work (BN) plus a fixed per-chunk cost (~16 columns' worth).  Promotion warps
     // own 4-8 columns (several warps per SM sub-partition hide each other's latency), 16 where
     // the epilogue quantizes (a 32-block split over two warps).  Widths whose last tile would
@@ -610,7 +575,7 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
     // Many waves (the CTAs will run persistent): the wave count no longer separates the widths;
     // 32-wide tiles with four 8-column promotion warps and 8-block chunks measured fastest there
     // (config 5: 73.7 -> 67.6 ms against the 64-wide tiles the wave rule picks).
-    if (!fused_quant && (long)((N + 63) / 64) * mt > 148L * MGC_QGEMM_MINB && K % 256 == 0) {
+    if (!fused_quant && (long)((N + 63) / 64) * mt > wave && K % 256 == 0) {
         bn = 32;
         cg = 4;
         cb = chunk(bn, cg);
@@ -621,7 +586,7 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
         const int tiles_n = (N + c[0] - 1) / c[0];
         if (tiles_n * c[0] > npad) continue;
         if (fused_quant && c[0] % 32 != 0) continue;   // both halves of a 32-block in one CTA
-        const long waves = ((long)tiles_n * mt + 148 * MGC_QGEMM_MINB - 1) / (148 * MGC_QGEMM_MINB);
+        const long waves = ((long)tiles_n * mt + wave - 1) / wave;
         const long cost = waves * (c[0] + 16);
         if (best < 0 || cost < best) { best = cost; bn = c[0]; cg = c[1]; }
     }

@@ -473,6 +473,7 @@ struct mgc_runtime {
     bool prof = false;
     bool fuse = true;        // fused epilogue quantizers (MGC_NO_FUSE=1 runs them as separate kernels)
     int last_launches = 0;   // kernels enqueued by the last forward
+    std::string only_op;     // non-empty: enqueue_forward enqueues only this op class
     std::map<std::string, ProfRow> prof_rows;
 
     float* up_f32(const GgufTensor& t, size_t n) {
@@ -529,12 +530,8 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
     std::vector<Ev> evs;
     if (rt->prof) launch_spin(2000000, st);   // ~1 ms at 2 GHz
     auto op = [&](const char* name, auto&& fn) {
-#ifdef MGC_DEBUG_SKIP_OPS
-        // diagnostic builds only: MGC_SKIP="MulMat(q),Norm,..." drops op classes (wrong
-        // results) to attribute graph step time
-        if (const char* sk = std::getenv("MGC_SKIP"))
-            if (std::strstr(sk, name)) return;
-#endif
+        // op-class timing (mgc_runtime_time_op): enqueue only the launches of one op class
+        if (!rt->only_op.empty() && rt->only_op != name) return;
         if (!rt->prof) { fn(); return; }
         Ev e{name, nullptr, nullptr};
         CK(cudaEventCreate(&e.a)); CK(cudaEventCreate(&e.b));
@@ -920,6 +917,52 @@ int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_
 }
 
 int mgc_runtime_kernel_count(const mgc_runtime* rt) { return rt ? rt->last_launches : -1; }
+
+int mgc_runtime_time_op(mgc_runtime* rt, const char* op, int B, int S, int iters, float* ms_per_replay,
+                        int* launches) {
+    return guard([&] {
+        if (!rt || !op || !op[0] || B <= 0 || S <= 0 || iters <= 0 || !ms_per_replay)
+            throw Err("mgc_runtime_time_op: bad arguments");
+        if (B * S > rt->max_rows) throw Err("mgc_runtime_time_op: B*S exceeds max_rows");
+        CK(cudaSetDevice(rt->device));
+        ensure_attn_scratch(rt, B, S);
+        CK(cudaStreamSynchronize(rt->st));
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ex = nullptr;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        rt->only_op = op;
+        const bool prof = rt->prof;
+        rt->prof = false;
+        auto restore = [&] {
+            rt->only_op.clear();
+            rt->prof = prof;
+            if (ex) cudaGraphExecDestroy(ex);
+            if (e0) cudaEventDestroy(e0);
+            if (e1) cudaEventDestroy(e1);
+        };
+        try {
+            CK(cudaStreamBeginCapture(rt->st, cudaStreamCaptureModeThreadLocal));
+            try { enqueue_forward(rt, rt->tokens, B, S, rt->logits, nullptr); }
+            catch (...) { cudaStreamEndCapture(rt->st, &g); if (g) cudaGraphDestroy(g); throw; }
+            CK(cudaStreamEndCapture(rt->st, &g));
+            CK(cudaGraphInstantiate(&ex, g, 0));
+            cudaGraphDestroy(g);
+            if (launches) *launches = rt->last_launches;
+            CK(cudaEventCreate(&e0));
+            CK(cudaEventCreate(&e1));
+            for (int i = 0; i < 2; i++) CK(cudaGraphLaunch(ex, rt->st));   // warm-up
+            CK(cudaEventRecord(e0, rt->st));
+            for (int i = 0; i < iters; i++) CK(cudaGraphLaunch(ex, rt->st));
+            CK(cudaEventRecord(e1, rt->st));
+            CK(cudaEventSynchronize(e1));
+            float ms = 0;
+            CK(cudaEventElapsedTime(&ms, e0, e1));
+            *ms_per_replay = ms / iters;
+            check_dev_error();
+        } catch (...) { restore(); throw; }
+        restore();
+    });
+}
 
 int mgc_profile_enable(mgc_runtime* rt, int on) { if (!rt) return -1; rt->prof = on != 0; return 0; }
 int mgc_profile_reset(mgc_runtime* rt) { if (!rt) return -1; rt->prof_rows.clear(); return 0; }

@@ -205,6 +205,13 @@ class CudaRuntime:
         """Kernels enqueued by the last forward."""
         return int(lib.mgc_runtime_kernel_count(self._h))
 
+    def time_op(self, op: str, B: int, S: int, iters: int = 50) -> tuple[float, int]:
+        """(ms per replay, kernels per replay) of a CUDA graph holding only the forward's
+        launches of op class `op` (a profile_report name), replayed back to back."""
+        ms, n = C.c_float(), C.c_int()
+        check(lib.mgc_runtime_time_op(self._h, op.encode(), B, S, iters, C.byref(ms), C.byref(n)), "time_op")
+        return float(ms.value), int(n.value)
+
     def profile_report(self) -> list[OpProfile]:
         buf = C.create_string_buffer(1 << 14)
         check(lib.mgc_profile_report(self._h, buf, len(buf)))

@@ -10,6 +10,10 @@ converter does (convert_to_gguf.py:213-246).
 
 ``dequant_twin`` writes the same model with every packed weight dequantised back to F32 --
 the input the reference's scalar CPU executor needs (it reads weights as float only).
+
+The packers are the library's (``runtime.pack_q8_0`` / ``pack_q4_k`` / ``dequant``) unless the
+caller passes another implementation of the same three functions (``packers=``), e.g. a CPU
+process that must not load the CUDA library.
 """
 from __future__ import annotations
 
@@ -18,8 +22,6 @@ from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
-
-from . import runtime as rt
 
 ALIGN = 32
 _LINEAR = ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_o.weight",
@@ -142,8 +144,12 @@ def _write(path: Path, s: ModelSpec, quant_label: str, tensors) -> None:
             pos += len(data)
 
 
-def make_model(path, spec: ModelSpec | None = None, dequant_twin=None) -> Path:
-    """Write a synthetic GGUF (and optionally its dequantised F32 twin)."""
+def make_model(path, spec: ModelSpec | None = None, dequant_twin=None, packers=None) -> Path:
+    """Write a synthetic GGUF (and optionally its dequantised F32 twin).  `packers`: an object
+    with pack_q8_0(w), pack_q4_k(w) and dequant(wtype, blocks, N, K) (default: the library's)."""
+    if packers is None:
+        from . import runtime as packers
+    Q8_0, Q4_K = 8, 12
     s = spec or ModelSpec()
     rng = np.random.default_rng(s.seed)
     packed, twin = [], []
@@ -153,12 +159,12 @@ def make_model(path, spec: ModelSpec | None = None, dequant_twin=None) -> Path:
         if _is_linear(name) and s.quant in ("gq8", "gq4"):
             N, K = shape
             if s.quant == "gq8":
-                blob, typ = rt.pack_q8_0(a), rt.Q8_0
+                blob, typ = packers.pack_q8_0(a), Q8_0
             else:
-                blob, typ = rt.pack_q4_k(a), rt.Q4_K
+                blob, typ = packers.pack_q4_k(a), Q4_K
             packed.append((name, ne, typ, blob.tobytes()))
             if dequant_twin is not None:
-                twin.append((name, ne, 0, rt.dequant(typ, blob, N, K).tobytes()))
+                twin.append((name, ne, 0, packers.dequant(typ, blob, N, K).tobytes()))
         else:
             packed.append((name, ne, 0, a.tobytes()))
             if dequant_twin is not None:

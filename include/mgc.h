@@ -73,7 +73,8 @@ int mgc_qgemm(const mgc_qweight* w, const float* x_dev, int M, const float* bias
  * each device looks up the array's device address; make that first call before any
  * stream capture.  All calls share the one array and it keeps the previous call's
  * contents (nothing in it needs to start at zero), so calls that can overlap on the GPU --
- * different streams, or different host threads -- race on it: serialise them. */
+ * different streams, or different host threads -- race on it: serialise them.  The looked-up
+ * address is kept for the life of the process; do not call this after a cudaDeviceReset. */
 int mgc_qgemm_noalloc(const mgc_qweight* w, const float* x_dev, int M, const float* bias_dev,
                       int act, const float* resid_dev, float* y_dev, void* stream);
 
@@ -142,6 +143,15 @@ int mgc_generate(mgc_runtime* rt, int B, const int32_t* class_ids, const uint64_
 
 /* Number of kernels the runtime's last forward enqueued (all are this library's own). */
 int mgc_runtime_kernel_count(const mgc_runtime* rt);
+
+/* Times one op class of the forward as it runs inside the step: captures a CUDA graph of the
+ * forward's launches of that class only (op = a name of mgc_profile_report, e.g. "MulMat(q)"),
+ * on the runtime's own buffers (their contents are whatever the last forward left), replays it
+ * `iters` times between CUDA events and returns the mean milliseconds per replay; *launches
+ * (optional) = kernels per replay.  No counterpart in the reference (it is the live, in-graph
+ * counterpart of the per-op profile of mg-opencl.hpp:50-53). */
+int mgc_runtime_time_op(mgc_runtime* rt, const char* op, int B, int S, int iters, float* ms_per_replay,
+                        int* launches);
 
 /* Per-op-type profile (OpenCLRuntime::profile_enable/reset/report, mg-opencl.hpp:50-53).
  * When enabled, forwards run eagerly with CUDA events around each kernel. */

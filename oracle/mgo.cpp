@@ -198,9 +198,10 @@ void mgo_quantize_act(const float* x, int64_t M, int64_t K, int8_t* qx, float* d
 // k_mul_mat_q8_i8 (mg-opencl.cpp:440-494) and k_mul_mat_q4k_i8 (:504-590).  One output at
 // a time, blocks b ascending, exact int32 block dot, then the fused epilogue
 // bias -> act -> residual (mg-opencl.cpp:481-493).
-void mgo_qgemm(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
-               const int32_t* sumx, int64_t M, int64_t N, int64_t K,
-               const float* bias, int act, const float* resid, float* y, int32_t* idot_out) {
+static void qgemm_impl(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
+                       const int32_t* sumx, int64_t M, int64_t N, int64_t K,
+                       const float* bias, int act, const float* resid, float* y, int32_t* idot_out,
+                       bool q4k_ref_order) {
     const int64_t nb = K / 32, nsb = K / 256;
     // decode per-(n,b) weight scales once
     std::vector<float> sA((size_t)N * nb), sB((size_t)N * nb);
@@ -236,7 +237,15 @@ void mgo_qgemm(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
                 float d = dx[m * nb + b];
                 if (wtype == 8) {
                     acc = std::fmaf(sA[n * nb + b] * d, (float)idot, acc);
+                } else if (q4k_ref_order) {
+                    // mg-opencl.cpp:572  acc += scl*dxm*(float)idot - mnl*dxm*(float)sum_x:
+                    // the difference is formed first (the first product contracted into it,
+                    // as the Q8_0 line contracts into acc), then added to acc.
+                    const float t2 = (sB[n * nb + b] * d) * (float)sumx[m * nb + b];
+                    const float t = std::fmaf(sA[n * nb + b] * d, (float)idot, -t2);
+                    acc = acc + t;
                 } else {
+                    // the CUDA kernel's order: two fused multiply-adds into acc
                     acc = std::fmaf(sA[n * nb + b] * d, (float)idot, acc);
                     acc = std::fmaf(-sB[n * nb + b], d * (float)sumx[m * nb + b], acc);
                 }
@@ -248,6 +257,18 @@ void mgo_qgemm(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
             y[m * N + n] = v;
         }
     }
+}
+
+void mgo_qgemm(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
+               const int32_t* sumx, int64_t M, int64_t N, int64_t K,
+               const float* bias, int act, const float* resid, float* y, int32_t* idot_out) {
+    qgemm_impl(wtype, w, qx, dx, sumx, M, N, K, bias, act, resid, y, idot_out, true);
+}
+
+void mgo_qgemm_fused(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
+                     const int32_t* sumx, int64_t M, int64_t N, int64_t K,
+                     const float* bias, int act, const float* resid, float* y, int32_t* idot_out) {
+    qgemm_impl(wtype, w, qx, dx, sumx, M, N, K, bias, act, resid, y, idot_out, false);
 }
 
 // k_mul_mat_t (mg-opencl.cpp:57-98): F32 GEMM, k ascending, same epilogue.

@@ -42,12 +42,20 @@ void mgo_quantize_act(const float* x, int64_t M, int64_t K, int8_t* qx, float* d
  * wtype 8 = Q8_0, 12 = Q4_K.  y[m*N+n] = act(acc + bias[n]) + resid[m*N+n]; act 0 none,
  * 1 erf-GELU (mg-opencl.cpp:36-40), 2 SiLU.  bias / resid may be NULL.
  * Per block b (ascending):  Q8_0: acc = fmaf(dw*dx, (float)idot, acc)
- *                           Q4_K: acc = fmaf(scl*dx, (float)idot, acc);
- *                                 acc = fmaf(-mnl, dx*(float)sumx, acc)
+ *                           Q4_K (mg-opencl.cpp:572, difference first):
+ *                                 t = fmaf(scl*dx, (float)idot, -((mnl*dx)*(float)sumx));
+ *                                 acc = acc + t
  * idot_out (optional) receives the raw int32 block dots [M][N][K/32]. */
 void mgo_qgemm(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
                const int32_t* sumx, int64_t M, int64_t N, int64_t K,
                const float* bias, int act, const float* resid, float* y, int32_t* idot_out);
+/* The same GEMM in the order the CUDA kernel accumulates Q4_K (Q8_0 is identical):
+ *   acc = fmaf(scl*dx, (float)idot, acc); acc = fmaf(-mnl, dx*(float)sumx, acc)
+ * -- two roundings into acc instead of one.  Used to check the kernel bit for bit; the
+ * kernel is checked against mgo_qgemm within a tolerance. */
+void mgo_qgemm_fused(int wtype, const uint8_t* w, const int8_t* qx, const float* dx,
+                     const int32_t* sumx, int64_t M, int64_t N, int64_t K,
+                     const float* bias, int act, const float* resid, float* y, int32_t* idot_out);
 
 /* F32 GEMM with the same fused epilogue (k_mul_mat_t, mg-opencl.cpp:57-98): the MLM head.
  * w [N][K] f32 row-major.  acc = fmaf(w, x, acc) over k ascending. */

@@ -43,6 +43,7 @@ def mgo():
             "mgo_dequant": (None, [I, P, I64, I64, P]),
             "mgo_quantize_act": (None, [P, I64, I64, P, P, P]),
             "mgo_qgemm": (None, [I, P, P, P, P, I64, I64, I64, P, I, P, P, P]),
+            "mgo_qgemm_fused": (None, [I, P, P, P, P, I64, I64, I64, P, I, P, P, P]),
             "mgo_gemm_f32": (None, [P, P, I64, I64, I64, P, I, P, P]),
             "mgo_layernorm_affine": (None, [P, P, P, I64, I64, F, P]),
             "mgo_flash_attn": (None, [P, I64, I64, I64, I64, F, P]),
@@ -110,8 +111,10 @@ def quantize_act(x):
     return qx, dx, sx
 
 
-def qgemm(wtype, wblocks, x, N, bias=None, act=0, resid=None, want_idot=False):
-    """Full quantized linear on f32 x: quantize_act + int8-dot GEMM + epilogue."""
+def qgemm(wtype, wblocks, x, N, bias=None, act=0, resid=None, want_idot=False, order="reference"):
+    """Full quantized linear on f32 x: quantize_act + int8-dot GEMM + epilogue.
+    order "reference": Q4_K accumulated as mg-opencl.cpp:572 writes it (difference first);
+    "kernel": the CUDA kernel's two fused multiply-adds (Q8_0 is the same either way)."""
     x = np.ascontiguousarray(x, np.float32)
     M, K = x.shape
     qx, dx, sx = quantize_act(x)
@@ -120,7 +123,8 @@ def qgemm(wtype, wblocks, x, N, bias=None, act=0, resid=None, want_idot=False):
     wblocks = np.ascontiguousarray(wblocks, np.uint8)
     bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
     resid = None if resid is None else np.ascontiguousarray(resid, np.float32)
-    mgo().mgo_qgemm(wtype, _p(wblocks), _p(qx), _p(dx), _p(sx), M, N, K, _p(bias), act, _p(resid), _p(y),
+    fn = mgo().mgo_qgemm if order == "reference" else mgo().mgo_qgemm_fused
+    fn(wtype, _p(wblocks), _p(qx), _p(dx), _p(sx), M, N, K, _p(bias), act, _p(resid), _p(y),
                     _p(idot))
     return (y, idot) if want_idot else y
 

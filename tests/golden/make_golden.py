@@ -9,8 +9,10 @@ the reference tree; the tests only read the committed .npz).
   - the token grid of the reference's own generate() (src/mg-generate.cpp) driven by the
     oracle forward on the small Q8_0 model.
 
-usage: python tests/golden/make_golden.py [/path/to/reference]
+usage: python tests/golden/make_golden.py /path/to/reference
+   (or set MGC_REFERENCE_DIR; there is no default location)
 """
+import os
 import sys
 from pathlib import Path
 
@@ -18,7 +20,12 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) > 1:
+    REF = Path(sys.argv[1])
+elif os.environ.get("MGC_REFERENCE_DIR"):
+    REF = Path(os.environ["MGC_REFERENCE_DIR"])
+else:
+    sys.exit("usage: make_golden.py /path/to/reference  (or set MGC_REFERENCE_DIR)")
 sys.path.insert(0, str(REF / "tools"))
 
 import convert_to_gguf as cg  # noqa: E402  (the reference's packer)

@@ -34,6 +34,24 @@ def test_clock_summary_flags_throttle_reasons():
 def test_bench_cli_lists_the_workloads():
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--help"], capture_output=True, text=True,
                          timeout=120).stdout
-    for w in ("c1", "c4", "c5"):
+    for w in ("c1", "c4", "c5", "sweep"):
         assert w in out
     assert "--impl" in out
+
+
+def test_reference_arm_models_do_not_load_the_cuda_library(tmp_path):
+    """The reference arm builds its models with the oracle's packers: libmgcuda.so stays unmapped."""
+    code = f"""
+import os, sys
+sys.path.insert(0, {str(ROOT)!r})
+os.environ["MGC_BENCH_DIR"] = {str(tmp_path)!r}
+import bench
+bench.MODEL_DIR = bench.Path({str(tmp_path)!r})
+p, t = bench.ensure_model("gq8", 1, twin=True, packers=bench._oracle_packers())
+assert p.exists() and t.exists()
+maps = open("/proc/self/maps").read()
+assert "libmgcuda" not in maps, "the CUDA library was loaded"
+print("ok")
+"""
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
