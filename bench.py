@@ -360,23 +360,44 @@ def c5_measure(steps: int, warmup: int, world: int, rank: int, local: int) -> di
         synth.make_model(tmp, spec)
         os.replace(tmp, path)
     _barrier(world)
-    tp = TPForward(path, rank, world)
     tokens = np.tile(synth.config1_tokens(spec), (4, 1))
     tokens[:, 0] = 1024 + np.array([207, 1, 500, 999])
-    for _ in range(warmup):
-        tp.forward(tokens)
-    torch.cuda.synchronize()
-    _barrier(world)
+    B, S = tokens.shape
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        tp.forward(tokens)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = _max_over_ranks([e0.elapsed_time(e1)], world)[0]
-    del tp
+    if world == 1:
+        # one GPU: the runtime's fused step (one CUDA graph, device-resident tokens and logits)
+        from edge_maskgit_b200 import runtime as rt
+        r = rt.CudaRuntime(path, max_rows=B * S, device=local)
+        stream = torch.cuda.ExternalStream(r.stream_handle, device=torch.device("cuda", local))
+        tok_dev = torch.from_numpy(tokens).cuda()
+        logits_dev = torch.empty((B * S, spec.vocab_size), dtype=torch.float32, device="cuda")
+        for _ in range(warmup):
+            r.forward_dev(tok_dev, logits_dev, B, S)
+        r.sync()
+        e0.record(stream)
+        for _ in range(steps):
+            r.forward_dev(tok_dev, logits_dev, B, S)
+        e1.record(stream)
+        r.sync()
+        ms = e0.elapsed_time(e1)
+        r.close()
+        how = "one GPU: the runtime's CUDA-graph step"
+    else:
+        tp = TPForward(path, rank, world)
+        for _ in range(warmup):
+            tp.forward(tokens)
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0.record()
+        for _ in range(steps):
+            tp.forward(tokens)
+        e1.record()
+        torch.cuda.synchronize()
+        del tp
+        how = f"column-split tensor parallel x{world}, NCCL all-gather"
+    ms = _max_over_ranks([ms if world == 1 else e0.elapsed_time(e1)], world)[0]
     return {"workload": "config5 step-1 forward, 24 layers, M=4097, batch 4, gq4",
-            "parallelism": f"column-split tensor parallel x{world}, NCCL all-gather", "scaling": "strong",
+            "parallelism": how, "scaling": "strong",
             "steps": steps, "ms_per_step": ms / steps, "steps_per_s": steps / (ms * 1e-3)}
 
 

@@ -38,7 +38,7 @@ __device__ __forceinline__ uint8_t* prep_base(uint8_t* prep, int b, int h, int H
     return prep + ((size_t)b * H + h) * nt * (size_t)(128 * fa::PREP_ROW);
 }
 
-// Store NC (8 or 16) columns [n, n+NC) (n % NC == 0) of QKV row (image b, position s) as f16
+// Store NC (4, 8 or 16) columns [n, n+NC) (n % NC == 0) of QKV row (image b, position s) as f16
 // into the prep tiles: part 0/1/2 = q/k/v, head h, first dim d0.  NC columns never straddle a
 // head (48 = 3 x 16 = 6 x 8) nor the q | k | v boundary (E = 48 H).
 template <int NC>
@@ -49,6 +49,14 @@ __device__ __forceinline__ void prep_store_at(uint8_t* prep, int H, int nt, int 
     uint8_t* base = prep_base(prep, b, h, H, nt);
     if (part < 2) {
         uint8_t* blk = base + (part == 0 ? (size_t)t * Q_BYTES : (size_t)nt * Q_BYTES + (size_t)t * K_BYTES);
+        if constexpr (NC == 4) {   // 4 halves: the upper or lower half of one 16-byte chunk
+            const __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&h0);
+            u.y = *reinterpret_cast<const uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(blk + sw128_off(r, d0 * 2)) = u;
+            return;
+        }
 #pragma unroll
         for (int c = 0; c < NC / 8; c++) {
             __half2 hh[4];

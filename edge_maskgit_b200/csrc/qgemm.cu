@@ -21,6 +21,7 @@
 #include "kernels.h"
 #include "ptx.cuh"
 #include "attnprep.cuh"
+#include "qgemm_common.cuh"
 
 #include <cstdio>
 #include <cstdlib>
@@ -37,34 +38,6 @@
 
 
 namespace mgc {
-
-struct QGemmArgs {
-    const int8_t* aq; int Mpad;      // activation tiles (kernels.h ActQ)
-    const int8_t* wq; const float* ws; int Npad;   // weight codes / scale tiles
-    int M, N, K;
-    const float* bias; const float* resid; float* y; int act;
-    // split-K: CTA z of gridDim.z handles K chunks [z*cps, (z+1)*cps); partials go to
-    // part [nsplit][M][N], the last CTA of a tile (counters[tile] reaches nsplit) reduces them
-    float* part; int* counters; int nsplit, cps;
-    // fused output quantizer (optional): quantize y per 32-block into ActQ tiles qo (the next
-    // layer's activation); y may then be null.  Needs CW == 16 and BN % 32 == 0.
-    int8_t* qo; int qo_Mpad; int qo_c;
-    // fused attention prep (optional): also store y as the f16 Q/K/V tiles of attnprep.cuh
-    uint8_t* ap; int ap_S, ap_H, ap_nt;
-    // persistent mode (tiles_n > 0): a 1-D grid of CTAs walks the tiles t = blockIdx.x, +gridDim.x,
-    // ... (tile t = n-tile t % tiles_n of m-tile t / tiles_n); the pipeline runs on across tiles
-    int tiles_n, tiles_m;
-};
-
-// (-1.5 * 2^23, -1.5 * 2^23): |v| < 2^22 always holds (32 * 127 * 128 < 2^22)
-constexpr uint64_t kMagicNeg2 = 0xCB400000CB400000ull;
-
-__device__ __forceinline__ float act_apply(float v, int a) {
-    if (a == 1) return 0.5f * v * (1.0f + erff(v * 0.70710678f));
-    if (a == 2) return __fdiv_rn(v, 1.0f + expf(-v));
-    return v;
-}
-
 
 template <int BN, int CG, bool Q4K, int CB>
 struct QGemmCfg {
@@ -510,10 +483,10 @@ int qgemm_prepare() {
 #define X(BN, CG, CB) rc |= set_smem_attr<BN, CG, false, CB>(); rc |= set_smem_attr<BN, CG, true, CB>();
     MGC_QGEMM_CONFIGS(X)
 #undef X
-    return rc;
+    return rc | wide_prepare();
 }
 
-static int sm_count() {   // SMs of the current device (cached per device; concurrent first calls agree)
+int sm_count() {   // SMs of the current device (cached per device; concurrent first calls agree)
     static std::atomic<int> n[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -597,11 +570,23 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
                  const float* resid, float* y, cudaStream_t st, const SplitK* sk, const ActQ* qo, bool qo_c,
                  const AttnPrepOut* ap) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
+    if (ap && (w.N != 3 * ap->H * fa::D || M % ap->S != 0)) return -2;
+    if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
+    const bool q4 = w.wtype == 12;
+    const bool split_asked = sk && sk->part && sk->counters && std::getenv("MGC_QGEMM_SPLITK") &&
+                             std::atoi(std::getenv("MGC_QGEMM_SPLITK")) > 1;
+    if (const int wbn = split_asked ? 0 : pick_wide(M, w.N, w.K, qo != nullptr, ap != nullptr)) {
+        QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
+                    nullptr, nullptr, 1, w.K / 128,
+                    qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
+                    ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0, 1};
+        if (const char* e = std::getenv("MGC_WIDE_PREBIAS")) p.wide_prebias = std::atoi(e) != 0;
+        const int rc = launch_qgemm_wide(p, q4, wbn, st);
+        if (rc != -2) return rc;
+    }
     int bn, cg, cb;
     pick_cfg(M, w.N, w.K, qo != nullptr, ap != nullptr, bn, cg, cb);
     if (w.K % (32 * cb) != 0) return -2;
-    if (ap && (w.N != 3 * ap->H * fa::D || M % ap->S != 0)) return -2;
-    if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
     // Split-K (MGC_QGEMM_SPLITK=<n>) is off by default: on the config-1 shapes it measured
     // slower than one CTA per tile (ncu: attn_o 11 -> 26 us with 3 splits, ffn_down 22 -> 38 us
     // with 4), so the library only splits when asked.
@@ -617,8 +602,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
                 sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps,
                 qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
-                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0};
-    const bool q4 = w.wtype == 12;
+                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0, 0};
 #define X(BN, CG, CB) \
     if (bn == BN && cg == CG && cb == CB) return q4 ? run_qgemm<BN, CG, true, CB>(p, st) : run_qgemm<BN, CG, false, CB>(p, st);
     MGC_QGEMM_CONFIGS(X)

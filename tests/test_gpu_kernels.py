@@ -200,3 +200,27 @@ def test_no_device_error_left(dev):
     from edge_maskgit_b200 import runtime as rt
     torch.cuda.synchronize()
     assert rt.device_error() == 0
+
+
+@pytest.mark.parametrize("wide", ["32", "64", "128", "0"])
+@pytest.mark.parametrize("wtype", [8, 12])
+@pytest.mark.parametrize("act", [0, 1])
+def test_qgemm_wide_tiles_epilogue(dev, oracle_mod, monkeypatch, wide, wtype, act):
+    """The large-M kernel at each tile width (MGC_QGEMM_WIDE forces it; "0" = the narrow kernel)
+    with the full epilogue: bias -> act -> residual, bit-exact (act 0) against the oracle."""
+    from edge_maskgit_b200 import runtime as rt
+    monkeypatch.setenv("MGC_QGEMM_WIDE", wide)
+    rng = np.random.default_rng(12)
+    M, K, N = 1025, 768, 2304
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02).astype(np.float32)
+    b = rng.standard_normal(N, dtype=np.float32)
+    r = rng.standard_normal((M, N), dtype=np.float32)
+    blocks = rt.pack_q8_0(w) if wtype == 8 else rt.pack_q4_k(w)
+    qw = rt.QWeight(wtype, blocks, N, K)
+    y = qw.qgemm(_t(x, dev), bias=_t(b, dev), act=act, resid=_t(r, dev)).cpu().numpy()
+    ref = oracle_mod.qgemm(wtype, blocks, x, N, bias=b, act=act, resid=r, order="kernel")
+    if act == 0:
+        assert np.array_equal(y, ref), f"max diff {np.abs(y - ref).max()}"
+    else:
+        np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-6)

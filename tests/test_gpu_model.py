@@ -106,3 +106,34 @@ def test_fused_quantizers_match_separate_kernels(small_models, monkeypatch):
         sep = b.forward(tok)
         b.close()
         assert np.array_equal(fused, sep), q
+
+
+@pytest.mark.parametrize("q", ["gq8", "gq4"])
+def test_batched_large_m_fused_epilogues(tmp_path, monkeypatch, q):
+    """8 images of 257 tokens in one forward (2056 rows: the large-M GEMM kernel, whose epilogues
+    store the attention's f16 tiles and quantize the next layer's input): bit-identical to the
+    same forward with those consumers as separate kernels, and image by image within f32
+    rounding of single-image forwards (257 rows: the small-M kernel; the attention splits its
+    key range differently for 1 and 8 images, so the accumulation order differs there)."""
+    from edge_maskgit_b200 import runtime as rt, synth
+    spec = synth.ModelSpec(n_layer=2, quant=q)
+    path = synth.make_model(tmp_path / f"{q}.gguf", spec)
+    S = spec.n_tokens + 1
+    rng = np.random.default_rng(3)
+    toks = np.full((8, S), spec.vocab_size - 1, np.int32)
+    toks[:, 0] = 1024 + rng.integers(0, 1000, 8)
+    toks[:, 1:] = np.where(rng.random((8, S - 1)) < 0.5, rng.integers(0, 1024, (8, S - 1)), toks[:, 1:])
+    monkeypatch.delenv("MGC_NO_FUSE", raising=False)
+    r = rt.CudaRuntime(path, max_rows=8 * S)
+    both = r.forward(toks)
+    singles = [r.forward(toks[i]) for i in range(8)]
+    r.close()
+    monkeypatch.setenv("MGC_NO_FUSE", "1")
+    r = rt.CudaRuntime(path, max_rows=8 * S)
+    sep = r.forward(toks)
+    r.close()
+    assert np.array_equal(both, sep)
+    for i in range(8):
+        one = singles[i]
+        assert cosine(both[i * S:(i + 1) * S], one) > 0.9999999, i
+        np.testing.assert_allclose(both[i * S:(i + 1) * S], one, rtol=1e-3, atol=1e-5)
