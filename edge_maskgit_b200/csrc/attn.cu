@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(256) flash_attn_1t(const uint8_t* __restrict__
     using namespace fa;
     using fa1::OQ; using fa1::OK; using fa1::OV; using fa1::OP; using fa1::OX; using fa1::OBAR;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sm = align1024_smem(smem_raw);
     uint64_t* bar_in = (uint64_t*)(sm + OBAR);   // Q, K, V landed (tx)
     uint64_t* bar_s = bar_in + 1;
     uint64_t* bar_o = bar_in + 2;
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
                                                                float* __restrict__ mlpart) {
     using namespace fa;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sm = align1024_smem(smem_raw);
     uint64_t* bars = (uint64_t*)(sm + OFF_BAR);
     uint64_t* bar_q = bars;            // Q landed (tx)
     uint64_t* k_full = bars + 1;       // [2] K tile landed (tx)

@@ -13,9 +13,15 @@
 //     [18432, 20480)   dx * sum(qx) f32 [128][4] (written only for Q4_K consumers)
 //
 //   QWeight  quantized [N][K] weight, rows padded to Npad (multiple of 128)
-//     q : int8 (Q8_0) or u8 nibble values 0..15 (Q4_K), [K/128][Npad][128], same swizzle
-//     s : f32 scale tiles [K/128][Npad/4][T][4 blocks][4 columns], T = 1 for Q8_0 (d) and
-//         2 for Q4_K (scl = d*sc_j, then mnl = dmin*m_j) -- a BN-column tile is BN*4*T floats
+//     Q8_0  q : int8 codes [K/128][Npad][128], same swizzle as the activation codes
+//           s : f32 scale tiles [K/128][Npad/4][4 blocks][4 columns] (d) -- BN*4 floats a tile
+//     Q4_K  q : packed nibbles [K/128][Npad][64]: the GGUF bytes of each half super-block
+//               unchanged (0.5 byte per weight in HBM)
+//           s : 16 bytes per row and 128-K chunk, [K/128][Npad][16]: d, dmin (fp16 bits), the
+//               chunk's four 6-bit scales, its four 6-bit mins, 4 bytes pad
+//           The GEMM kernels unpack a stage in shared memory into the same operand layouts as
+//           Q8_0: u8 code tile (128-byte swizzle) and f32 scale tile [BN/4][2][4][4] holding
+//           scl = d*sc_j then mnl = dmin*m_j (exact products)
 //     f32: for wtype 0 the weight itself, [N][K] row-major
 #pragma once
 #include <cstdint>

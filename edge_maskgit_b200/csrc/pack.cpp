@@ -142,38 +142,48 @@ void dequant(int wtype, const uint8_t* w, int64_t N, int64_t K, float* out) {
     }
 }
 
-// GGUF blocks -> device streaming layout (see kernels.h).  Lossless: the int8 / nibble codes
-// are copied and the scales become exact f32 (fp16 -> f32; d*sc and dmin*m are exact products
-// of an 11-bit and a 6-bit significand).
+// GGUF blocks -> device streaming layout (see kernels.h).  Lossless.
+//  Q8_0: int8 codes, 128-byte-swizzled K-major rows, and exact f32 scales (fp16 -> f32).
+//  Q4_K: the packed nibbles stay packed -- each row's 64 bytes per 128-K chunk are the GGUF
+//        bytes of that half super-block unchanged -- plus 16 bytes per row and chunk: d and
+//        dmin (fp16 bits) and the four decoded 6-bit scales and mins of the chunk's
+//        sub-blocks (q4k_get_scale_min, mg-opencl.cpp:544-550), so the kernel forms the exact
+//        f32 products d*sc and dmin*m (11-bit x 6-bit significands).
 void repack(int wtype, const uint8_t* w, int N, int K, int Npad, std::vector<int8_t>& q, std::vector<float>& sc) {
-    const int nb = K / 32, T = wtype == 12 ? 2 : 1;
-    q.assign((size_t)K * Npad, 0);
-    sc.assign((size_t)nb * Npad * T, 0.0f);
-    for (int n = 0; n < N; ++n)
-        for (int b = 0; b < nb; ++b) {
-            int8_t codes[32];
-            const int kc = b >> 2, j = b & 3;
-            float* tile = sc.data() + (((size_t)kc * (Npad / 4) + n / 4) * T) * 16;
-            if (wtype == 8) {
-                const uint8_t* blk = w + ((size_t)n * nb + b) * 34;
-                tile[j * 4 + (n & 3)] = rdh(blk);
-                std::memcpy(codes, blk + 2, 32);
-            } else {
-                const uint8_t* blk = w + ((size_t)n * (K / 256) + b / 8) * 144;
-                const int sub = b & 7;
-                int s6, m6;
-                q4k_get_scale_min(blk + 4, sub, &s6, &m6);
-                tile[j * 4 + (n & 3)] = rdh(blk) * (float)s6;
-                tile[16 + j * 4 + (n & 3)] = rdh(blk + 2) * (float)m6;
-                for (int i = 0; i < 32; ++i) {
-                    const uint8_t byte = blk[16 + (sub >> 1) * 32 + i];
-                    codes[i] = (int8_t)((sub & 1) ? (byte >> 4) : (byte & 0xF));
+    const int nb = K / 32;
+    if (wtype == 12) {
+        const int nkc = K / 128;
+        q.assign((size_t)nkc * Npad * kQ4Row, 0);
+        sc.assign((size_t)nkc * Npad * kQ4Scl / sizeof(float), 0.0f);
+        uint8_t* s8 = reinterpret_cast<uint8_t*>(sc.data());
+        for (int n = 0; n < N; ++n)
+            for (int kc = 0; kc < nkc; ++kc) {
+                const uint8_t* blk = w + ((size_t)n * (K / 256) + kc / 2) * 144;
+                const int h = kc & 1;   // which half (sub-blocks 4h .. 4h+3) of the super-block
+                std::memcpy(q.data() + ((size_t)kc * Npad + n) * kQ4Row, blk + 16 + h * 64, 64);
+                uint8_t* o = s8 + ((size_t)kc * Npad + n) * kQ4Scl;
+                std::memcpy(o, blk, 4);   // d, dmin
+                for (int j = 0; j < 4; ++j) {
+                    int s6, m6;
+                    q4k_get_scale_min(blk + 4, 4 * h + j, &s6, &m6);
+                    o[4 + j] = (uint8_t)s6;
+                    o[8 + j] = (uint8_t)m6;
                 }
             }
+        return;
+    }
+    q.assign((size_t)K * Npad, 0);
+    sc.assign((size_t)nb * Npad, 0.0f);
+    for (int n = 0; n < N; ++n)
+        for (int b = 0; b < nb; ++b) {
+            const int kc = b >> 2, j = b & 3;
+            float* tile = sc.data() + ((size_t)kc * (Npad / 4) + n / 4) * 16;
+            const uint8_t* blk = w + ((size_t)n * nb + b) * 34;
+            tile[j * 4 + (n & 3)] = rdh(blk);
             int8_t* row = q.data() + ((size_t)kc * Npad + n) * 128;
             for (int i = 0; i < 32; ++i) {
                 const int k = j * 32 + i;
-                row[((((k >> 4) ^ (n & 7)) << 4) | (k & 15))] = codes[i];
+                row[((((k >> 4) ^ (n & 7)) << 4) | (k & 15))] = (int8_t)blk[2 + i];
             }
         }
 }

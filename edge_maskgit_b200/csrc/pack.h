@@ -4,6 +4,9 @@
 #include <vector>
 
 namespace mgc {
+// Q4_K device layout (see kernels.h): packed nibble bytes and compact scale bytes per row and
+// 128-K chunk
+constexpr int kQ4Row = 64, kQ4Scl = 16;
 uint16_t f32_to_f16(float f);
 float f16_to_f32(uint16_t h);
 void q4k_get_scale_min(const uint8_t* s12, int j, int* sc, int* mn);

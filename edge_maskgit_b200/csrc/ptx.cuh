@@ -13,6 +13,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
 
+// The dynamic shared-memory base rounded up to 1024 bytes (the 128-byte-swizzle atom).  Done
+// as pointer arithmetic on the __shared__ array itself, so the compiler keeps the shared state
+// space for every pointer derived from it (ld.shared, not generic loads).
+__device__ __forceinline__ uint8_t* align1024_smem(uint8_t* smem_raw) {
+    return smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // wait: block until the preceding kernel in the stream has completed and its writes are
 // visible (a no-op when the launch did not opt in); launch: let the next kernel start its
@@ -52,6 +59,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 #endif
     return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread may sleep up to ~hint_ns in the instruction
+// (it resumes as soon as the phase completes), so waiting loops spin far fewer times.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return ok != 0;
+}
 // Bounded wait: spins at most ~kWaitCycles SM clocks; on timeout records `code` in the
 // device error word and in *abort (shared), and returns false.  Also returns false early
 // once another thread of the CTA has set *abort.
@@ -61,7 +79,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 2000)) return true;
         if ((it & 255) == 0) {
             if (*abort_flag) return false;
             if (clock64() - t0 > kWaitCycles) {

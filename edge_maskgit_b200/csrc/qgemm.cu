@@ -56,23 +56,29 @@ struct QGemmCfg {
     // stage = [SUB activation tiles: codes | dx | (dx*sumx)] [SUB weight code tiles] [SUB scale tiles]
     static constexpr uint32_t T = Q4K ? 2 : 1;
     static constexpr uint32_t A_BYTES = Q4K ? 20480 : 18432, B_BYTES = BN * 128, S_BYTES = BN * 16 * T;
+    // Q4_K: the packed weight bytes land in a raw area (BN x 64 nibble bytes, BN x 16 scale
+    // bytes per 128-K tile) and the MMA warp unpacks them into the code and scale tiles
+    static constexpr uint32_t R_BYTES = Q4K ? BN * 80 : 0;
     static constexpr uint32_t OFF_DX = 16384, OFF_CX = 18432, OFF_B = SUB * A_BYTES, OFF_S = OFF_B + SUB * B_BYTES,
-                              STAGE = (OFF_S + SUB * S_BYTES + 1023) & ~1023u;
-    static constexpr uint32_t TX_BYTES = SUB * (A_BYTES + B_BYTES + S_BYTES);
+                              OFF_R = OFF_S + SUB * S_BYTES, STAGE = (OFF_R + SUB * R_BYTES + 1023) & ~1023u;
+    static constexpr uint32_t TX_BYTES = Q4K ? SUB * (A_BYTES + R_BYTES) : SUB * (A_BYTES + B_BYTES + S_BYTES);
 #ifdef MGC_NST
     static constexpr int NST = MGC_NST;
 #else
     // ~190 KB ring for 4-block chunks (deeper measured faster); 8-block chunks fill what fits
-    static constexpr int NST = CB == 4 ? (BN <= 32 ? 8 : BN <= 64 ? 6 : 4)
-                                       : ((225u * 1024u - 2048u) / STAGE > 8 ? 8 : (225u * 1024u - 2048u) / STAGE);
+    static constexpr int NST_PREF = CB == 4 ? (BN <= 32 ? 8 : BN <= 64 ? 6 : 4) : 8;
+    static constexpr int NST_FIT = (232448 - 1024 - 320 - 2 * NPW * 32 * 4) / STAGE;   // what fits
+    static constexpr int NST = NST_PREF < NST_FIT ? NST_PREF : NST_FIT;
 #endif
-    static constexpr uint32_t XCHG = NST * STAGE + 256;   // epilogue exchange: [2][NPW][32] f32
+    static constexpr uint32_t XCHG = NST * STAGE + 320;   // (barriers, then) epilogue exchange: [2][NPW][32] f32
     static constexpr uint32_t SMEM = 1024 + XCHG + 2 * NPW * 32 * 4;
     // allocation is a power of two >= 32 columns
     static constexpr uint32_t TMEM_NEED = CB * BN * NGRP,
                               TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
                                         : TMEM_NEED <= 256 ? 256 : 512;
     static_assert(NGRP >= 1 && TMEM_NEED <= 512, "TMEM ring exceeds 512 columns");
+    static_assert(SMEM <= 232448, "shared memory beyond the opt-in limit");
+    static_assert((3 * NST + 2 * NGRP) * 8 + 8 <= 320, "barrier area");
 };
 
 template <int BN, int CG, bool Q4K, int CB, bool PERSIST>
@@ -84,12 +90,13 @@ qgemm_kernel(const QGemmArgs p) {
     constexpr int IREGS = C::THREADS > 448 ? 32 : MGC_QGEMM_IREGS;
     constexpr int NST = C::NST, NGRP = C::NGRP, CW = C::CW, BATCH = CW >= IREGS ? 1 : IREGS / CW > 4 ? 4 : IREGS / CW;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* smem = align1024_smem(smem_raw);
     uint64_t* full = (uint64_t*)(smem + NST * C::STAGE);
     uint64_t* empty = full + NST;
     uint64_t* tfull = empty + NST;
     uint64_t* tempty = tfull + NGRP;
-    uint32_t* tmem_slot = (uint32_t*)(tempty + NGRP);
+    uint64_t* unpk = tempty + NGRP;   // Q4_K: stage s unpacked (the MMA warp's lane 0 arrives)
+    uint32_t* tmem_slot = (uint32_t*)(unpk + NST);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -111,6 +118,7 @@ qgemm_kernel(const QGemmArgs p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < NST; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + C::NPW); }
         for (int g = 0; g < NGRP; g++) { mbar_init(&tfull[g], 1); mbar_init(&tempty[g], C::NPW); }
+        for (int s = 0; s < NST; s++) mbar_init(&unpk[s], 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -135,9 +143,16 @@ qgemm_kernel(const QGemmArgs p) {
 #pragma unroll
                 for (int u = 0; u < SUB; u++) {
                     const size_t kk = (size_t)kc * SUB + u;
-                    bulk_g2s(st + C::OFF_B + u * C::B_BYTES, p.wq + (kk * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
-                    bulk_g2s(st + C::OFF_S + u * C::S_BYTES, p.ws + (kk * (p.Npad / 4) + n0 / 4) * 16 * C::T,
-                             C::S_BYTES, &full[s]);
+                    if constexpr (Q4K) {   // packed nibbles + compact scales into the raw area
+                        uint8_t* raw = st + C::OFF_R + u * C::R_BYTES;
+                        bulk_g2s(raw, p.wq + (kk * p.Npad + n0) * 64, BN * 64, &full[s]);
+                        bulk_g2s(raw + BN * 64, reinterpret_cast<const uint8_t*>(p.ws) + (kk * p.Npad + n0) * 16, BN * 16,
+                                 &full[s]);
+                    } else {
+                        bulk_g2s(st + C::OFF_B + u * C::B_BYTES, p.wq + (kk * p.Npad + n0) * 128, C::B_BYTES, &full[s]);
+                        bulk_g2s(st + C::OFF_S + u * C::S_BYTES, p.ws + (kk * (p.Npad / 4) + n0 / 4) * 16, C::S_BYTES,
+                                 &full[s]);
+                    }
                 }
             };
             auto copy_a = [&](int i, int gc) {
@@ -180,12 +195,25 @@ qgemm_kernel(const QGemmArgs p) {
         }
         griddep_launch();   // this CTA's loads are all issued: the next kernel may start its prologue
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_make(2, 1, Q4K ? 0 : 1, 128, BN);
-            for (int kc = 0; kc < my_tiles * nloc; kc++) {   // running chunk index over this CTA's tiles
-                const int s = kc % NST, it = kc / NST, g = kc % NGRP, ug = kc / NGRP;
-                if (!mbar_wait(&full[s], it & 1, abort_flag, 2)) break;
-                if (!mbar_wait(&tempty[g], (ug & 1) ^ 1, abort_flag, 3)) break;
+        // lane 0 issues the MMAs; for Q4_K the whole warp first unpacks the stage
+        constexpr uint32_t idesc = idesc_make(2, 1, Q4K ? 0 : 1, 128, BN);
+        for (int kc = 0; kc < my_tiles * nloc; kc++) {   // running chunk index over this CTA's tiles
+            const int s = kc % NST, it = kc / NST, g = kc % NGRP, ug = kc / NGRP;
+            bool go = true;
+            if constexpr (Q4K) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[s], it & 1, abort_flag, 2))) break;
+                uint8_t* st = smem + s * C::STAGE;
+#pragma unroll
+                for (int u = 0; u < SUB; u++)
+                    unpack_q4k_stage<BN>(st + C::OFF_R + u * C::R_BYTES, st + C::OFF_B + u * C::B_BYTES,
+                                         reinterpret_cast<float*>(st + C::OFF_S + u * C::S_BYTES), lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&unpk[s]);   // the promotion warps may read the scale tile
+            } else if (lane == 0) {
+                go = mbar_wait(&full[s], it & 1, abort_flag, 2);
+            }
+            if (lane == 0 && go) go = mbar_wait(&tempty[g], (ug & 1) ^ 1, abort_flag, 3);
+            if (lane == 0 && go) {
                 tc_fence_after();
                 const uint32_t a_base = smem_u32(smem + s * C::STAGE), b_base = a_base + C::OFF_B;
                 // one MMA per 32-block, each into its own TMEM buffer (no accumulation)
@@ -195,9 +223,10 @@ qgemm_kernel(const QGemmArgs p) {
                     mma_i8(tmem + (g * CB + j) * BN, sdesc_sw128(a_base + u * C::A_BYTES + 32 * jj),
                            sdesc_sw128(b_base + u * C::B_BYTES + 32 * jj), idesc, 0);
                 }
-                mma_commit(&tfull[g]);   // the chunk's 4 dot tiles are ready
+                mma_commit(&tfull[g]);   // the chunk's dot tiles are ready
                 mma_commit(&empty[s]);   // its shared-memory operands may be overwritten
             }
+            if (!__shfl_sync(0xffffffffu, go ? 1 : 0, 0)) break;   // the whole warp leaves together
         }
         griddep_launch();
     } else {
@@ -220,6 +249,7 @@ qgemm_kernel(const QGemmArgs p) {
             const int kc = t / BPC, jb = t % BPC, g = kc % NGRP;
             if (jb == 0) {
                 bool w = mbar_wait(&full[kc % NST], (kc / NST) & 1, abort_flag, 4) &&
+                         (!Q4K || mbar_wait(&unpk[kc % NST], (kc / NST) & 1, abort_flag, 6)) &&
                          mbar_wait(&tfull[g], (kc / NGRP) & 1, abort_flag, 5);
                 ok = __all_sync(0xffffffffu, w);
                 if (!ok) return;
@@ -483,7 +513,7 @@ int qgemm_prepare() {
 #define X(BN, CG, CB) rc |= set_smem_attr<BN, CG, false, CB>(); rc |= set_smem_attr<BN, CG, true, CB>();
     MGC_QGEMM_CONFIGS(X)
 #undef X
-    return rc | wide_prepare();
+    return rc;
 }
 
 int sm_count() {   // SMs of the current device (cached per device; concurrent first calls agree)
@@ -573,17 +603,6 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     if (ap && (w.N != 3 * ap->H * fa::D || M % ap->S != 0)) return -2;
     if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
     const bool q4 = w.wtype == 12;
-    const bool split_asked = sk && sk->part && sk->counters && std::getenv("MGC_QGEMM_SPLITK") &&
-                             std::atoi(std::getenv("MGC_QGEMM_SPLITK")) > 1;
-    if (const int wbn = split_asked ? 0 : pick_wide(M, w.N, w.K, qo != nullptr, ap != nullptr)) {
-        QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
-                    nullptr, nullptr, 1, w.K / 128,
-                    qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
-                    ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0, 1};
-        if (const char* e = std::getenv("MGC_WIDE_PREBIAS")) p.wide_prebias = std::atoi(e) != 0;
-        const int rc = launch_qgemm_wide(p, q4, wbn, st);
-        if (rc != -2) return rc;
-    }
     int bn, cg, cb;
     pick_cfg(M, w.N, w.K, qo != nullptr, ap != nullptr, bn, cg, cb);
     if (w.K % (32 * cb) != 0) return -2;
@@ -602,7 +621,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
                 sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps,
                 qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
-                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0, 0};
+                ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0};
 #define X(BN, CG, CB) \
     if (bn == BN && cg == CG && cb == CB) return q4 ? run_qgemm<BN, CG, true, CB>(p, st) : run_qgemm<BN, CG, false, CB>(p, st);
     MGC_QGEMM_CONFIGS(X)

@@ -28,3 +28,15 @@ def test_errors_are_reported_without_a_gpu():
         assert "multiple of 32" in str(e)
     else:
         raise AssertionError("expected MgcError")
+
+
+def test_reference_main_with_cuda_backend_links():
+    """oracle/_ref/mg_generate_cuda: the reference's own generate() + Model::load (unmodified
+    sources) driving the CUDA backend through include/mgc.hpp, as INTEGRATION.md's
+    `--backend cuda` branch does.  Here (no GPU) it must link against libmgcuda.so and run."""
+    import subprocess
+    exe = ROOT / "oracle" / "_ref" / "mg_generate_cuda"
+    if not exe.exists():
+        pytest.skip("built only where the reference tree exists")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2 and "usage" in r.stderr

@@ -105,3 +105,25 @@ def test_decode_tokens_identical_to_reference_generate(oracle_mod, full_models, 
     r.close()
     assert np.array_equal(grid, toks[0, 1:]), int((grid != toks[0, 1:]).sum())
     assert np.array_equal(grid_ref, toks[0, 1:]), int((grid_ref != toks[0, 1:]).sum())
+
+
+def test_reference_main_drives_cuda_backend(oracle_mod, full_models, tmp_path):
+    """The reference's own program path -- Model::load + generate() from the unmodified sources,
+    with the TransformerFwd built from include/mgc.hpp exactly as INTEGRATION.md's
+    `--backend cuda` branch -- produces the same token grid as the CUDA decode loop."""
+    import subprocess
+    from pathlib import Path
+    from edge_maskgit_b200 import runtime as rt
+    exe = Path(oracle_mod.__file__).parent / "_ref" / "mg_generate_cuda"
+    if not exe.exists():
+        pytest.skip("oracle/_ref/mg_generate_cuda is not built")
+    path, _, spec = full_models["gq8"]
+    out = tmp_path / "grid.bin"
+    p = subprocess.run([str(exe), str(path), "207", "42", "8", str(out)], capture_output=True, text=True,
+                       timeout=600)
+    assert p.returncode == 0, p.stderr
+    grid = np.fromfile(out, np.int32)
+    r = rt.CudaRuntime(path, max_rows=spec.n_tokens + 1)
+    toks = r.generate([207], [42], steps=8, temperature=4.5)
+    r.close()
+    assert np.array_equal(grid, toks[0, 1:])
