@@ -350,7 +350,6 @@ def c5_measure(steps: int, warmup: int, world: int, rank: int, local: int) -> di
     over the ranks with NCCL all-gathers; ms per step, max over ranks (strong scaling)."""
     import torch
     from edge_maskgit_b200 import synth
-    from edge_maskgit_b200.tp import TPForward
 
     MODEL_DIR.mkdir(parents=True, exist_ok=True)
     path = MODEL_DIR / "c5_gq4_n4096.gguf"
@@ -383,19 +382,29 @@ def c5_measure(steps: int, warmup: int, world: int, rank: int, local: int) -> di
         r.close()
         how = "one GPU: the runtime's CUDA-graph step"
     else:
-        tp = TPForward(path, rank, world)
+        # column-split tensor parallel runtime: NCCL all-gathers inside the step's CUDA graph
+        import torch.distributed as dist
+        from edge_maskgit_b200 import runtime as rt
+        obj = [rt.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        r = rt.CudaRuntime(path, max_rows=B * S, device=local, tp=(rank, world, obj[0]))
+        stream = torch.cuda.ExternalStream(r.stream_handle, device=torch.device("cuda", local))
+        tok_dev = torch.from_numpy(tokens).cuda()
+        logits_dev = torch.empty((B * S, spec.vocab_size), dtype=torch.float32, device="cuda")
         for _ in range(warmup):
-            tp.forward(tokens)
-        torch.cuda.synchronize()
+            r.forward_dev(tok_dev, logits_dev, B, S)
+        r.sync()
         _barrier(world)
-        e0.record()
-        for _ in range(steps):
-            tp.forward(tokens)
-        e1.record()
         torch.cuda.synchronize()
-        del tp
-        how = f"column-split tensor parallel x{world}, NCCL all-gather"
-    ms = _max_over_ranks([ms if world == 1 else e0.elapsed_time(e1)], world)[0]
+        e0.record(stream)
+        for _ in range(steps):
+            r.forward_dev(tok_dev, logits_dev, B, S)
+        e1.record(stream)
+        r.sync()
+        ms = e0.elapsed_time(e1)
+        r.close()
+        how = f"column-split tensor parallel x{world} (C++ runtime, NCCL all-gathers in the step graph)"
+    ms = _max_over_ranks([ms], world)[0]
     return {"workload": "config5 step-1 forward, 24 layers, M=4097, batch 4, gq4",
             "parallelism": how, "scaling": "strong",
             "steps": steps, "ms_per_step": ms / steps, "steps_per_s": steps / (ms * 1e-3)}

@@ -38,6 +38,8 @@ _SIGS = {
     "mgc_embed": (I, [P, I, P, I, P, I, I, P, P]),
     "mgc_runtime_create": (I, [C.c_char_p, I, I, C.POINTER(P)]),
     "mgc_runtime_destroy": (None, [P]),
+    "mgc_tp_unique_id": (I, [P]),
+    "mgc_runtime_create_tp": (I, [C.c_char_p, I, I, I, I, P, C.POINTER(P)]),
     "mgc_runtime_hparams": (I, [P, P]),
     "mgc_runtime_device_name": (C.c_char_p, [P]),
     "mgc_transformer_forward": (I, [P, P, I, I, P]),

@@ -261,7 +261,8 @@ __global__ void __launch_bounds__(128) rows_kernel(const float* __restrict__ x, 
                                                    int vocab, const float* __restrict__ pos,
                                                    const int32_t* __restrict__ tokens, int S, int rows,
                                                    const float* __restrict__ gamma, const float* __restrict__ beta,
-                                                   float eps, float* y, ActQ a, int quant, int want_c) {
+                                                   float eps, float* y, ActQ a, int quant, int want_c, int xw,
+                                                   long long xstride) {
     griddep_wait();
     griddep_launch();
     extern __shared__ float stage[];
@@ -280,6 +281,17 @@ __global__ void __launch_bounds__(128) rows_kernel(const float* __restrict__ x, 
         for (int i = 0; i < NC; i++)
 #pragma unroll
             for (int e = 0; e < 8; e++) v[i][e] = __fadd_rn(v[i][e], p[i][e]);
+    } else if (xw > 0) {
+        // column-blocked input (the all-gather layout of a column-split layer): columns
+        // [g*xw, (g+1)*xw) of every row sit in block g at x + g*xstride, rows xw apart
+#pragma unroll
+        for (int i = 0; i < NC; i++) {
+            const int k = 256 * i + 8 * lane, g = k / xw;
+            const float* src = x + (size_t)g * xstride + (size_t)m * xw + (k - g * xw);
+            const float4 u0 = reinterpret_cast<const float4*>(src)[0], u1 = reinterpret_cast<const float4*>(src)[1];
+            v[i][0] = u0.x; v[i][1] = u0.y; v[i][2] = u0.z; v[i][3] = u0.w;
+            v[i][4] = u1.x; v[i][5] = u1.y; v[i][6] = u1.z; v[i][7] = u1.w;
+        }
     } else {
         load_chunks<NC>(x + (size_t)m * D, v, lane);
     }
@@ -293,14 +305,14 @@ __global__ void __launch_bounds__(128) rows_kernel(const float* __restrict__ x, 
 template <int MODE>
 static bool launch_rows(int D, const float* x, const float* tok, int vocab, const float* pos, const int32_t* tokens,
                         int S, int rows, const float* gamma, const float* beta, float eps, float* y, const ActQ* a,
-                        bool want_c, cudaStream_t st) {
+                        bool want_c, cudaStream_t st, int xw = 0, long long xstride = 0) {
     const ActQ aa = a ? *a : ActQ{};
     const unsigned blocks = (unsigned)((rows + 3) / 4);
     const size_t sm = MODE == 2 ? 0 : (size_t)4 * D * sizeof(float);
 #define MGC_ROWS(NC)                                                                                       \
     case NC:                                                                                               \
         launch_k(rows_kernel<NC, MODE>, blocks, 128, sm, st, x, tok, vocab, pos, tokens, S, rows, gamma, beta, eps, y, \
-                                                       aa, a != nullptr, want_c);                          \
+                                                       aa, a != nullptr, want_c, xw, xstride);             \
         return true;
     switch (D % 256 == 0 ? D / 256 : 0) {
         MGC_ROWS(1) MGC_ROWS(2) MGC_ROWS(3) MGC_ROWS(4) MGC_ROWS(6) MGC_ROWS(8) MGC_ROWS(12)
@@ -354,6 +366,21 @@ void launch_embed_ln(const float* tok, int vocab, const float* pos, int E, const
     const unsigned blocks = (unsigned)((rows + 7) / 8);
     MGC_NV_SWITCH(E, (launch_k(embed_ln_kernel<NV>, blocks, 256, 0, st, tok, vocab, pos, tokens, S, rows, gamma,
                                                                   beta, eps, y, aa, 1, a != nullptr, want_c)));
+}
+
+bool launch_ln_blocked(const float* x, int xw, long long xstride, const float* gamma, const float* beta, int rows,
+                       int D, float eps, float* y, const ActQ* a, bool want_c, cudaStream_t st) {
+    ++g_launch_count;
+    return D <= 2048 && xw > 0 && xw % 8 == 0 &&
+           launch_rows<0>(D, x, nullptr, 0, nullptr, nullptr, 1, rows, gamma, beta, eps, y, a, want_c, st, xw, xstride);
+}
+
+bool launch_quant_blocked(const float* x, int xw, long long xstride, int M, int K, const ActQ& a, bool want_c,
+                          cudaStream_t st) {
+    ++g_launch_count;
+    return xw > 0 && xw % 8 == 0 &&
+           launch_rows<2>(K, x, nullptr, 0, nullptr, nullptr, 1, M, nullptr, nullptr, 0.0f, nullptr, &a, want_c, st, xw,
+                          xstride);
 }
 
 void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st) {

@@ -102,6 +102,13 @@ void launch_sample_codes(const float* logits, int rows, int vocab, int CB, const
                          cudaStream_t st);
 // quantizer: x [M][K] f32 -> tiled ActQ (want_c: also write the Q4_K correction term)
 void launch_quant_act_tiled(const float* x, int M, int K, const ActQ& a, bool want_c, cudaStream_t st);
+// LayerNorm (+quantizer) and quantizer over a column-blocked input -- the layout an all-gather
+// of column slices produces: columns [g*xw, (g+1)*xw) of row m at x[g*xstride + m*xw + ...].
+// false: unsupported width (D <= 2048 for LayerNorm, D % 256 == 0, xw % 8 == 0).
+bool launch_ln_blocked(const float* x, int xw, long long xstride, const float* gamma, const float* beta, int rows,
+                       int D, float eps, float* y, const ActQ* a, bool want_c, cudaStream_t st);
+bool launch_quant_blocked(const float* x, int xw, long long xstride, int M, int K, const ActQ& a, bool want_c,
+                          cudaStream_t st);
 // quantizer with plain outputs (kernel-level C ABI)
 void launch_quant_act_plain(const float* x, int M, int K, int8_t* qx, float* dx, int32_t* sumx,
                             cudaStream_t st);
@@ -127,9 +134,12 @@ struct SplitK {
 // to launch_quant_act_tiled on y; qo_c: write the Q4_K term); y may then be null.
 // destination of the attention prep tiles (f16 Q/K/V of B = M/S images, H heads, nt = ceil(S/128))
 struct AttnPrepOut { uint8_t* buf; int S, H, nt; };
+// resid_ld: row stride of resid (0 = N; a column slice of a wider matrix in tensor-parallel
+// layers); qo_n0: global column of this GEMM's first output column inside qo (its K).
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
                  const float* resid, float* y, cudaStream_t st, const SplitK* sk = nullptr,
-                 const ActQ* qo = nullptr, bool qo_c = false, const AttnPrepOut* ap = nullptr);
+                 const ActQ* qo = nullptr, bool qo_c = false, const AttnPrepOut* ap = nullptr,
+                 int resid_ld = 0, int qo_n0 = 0);
 // set the kernels' shared-memory limits on the current device (once per device)
 int qgemm_prepare();
 int attn_prepare();

@@ -411,7 +411,7 @@ qgemm_kernel(const QGemmArgs p) {
 #pragma unroll
                     for (int i = 0; i < 4; i++) v[i] = act_apply(v[i], p.act);
                     if (p.resid) {
-                        const float4 r4 = *reinterpret_cast<const float4*>(p.resid + (size_t)m * p.N + n);
+                        const float4 r4 = *reinterpret_cast<const float4*>(p.resid + (size_t)m * p.resid_ld + n);
                         v[0] = __fadd_rn(v[0], r4.x); v[1] = __fadd_rn(v[1], r4.y);
                         v[2] = __fadd_rn(v[2], r4.z); v[3] = __fadd_rn(v[3], r4.w);
                     }
@@ -423,7 +423,7 @@ qgemm_kernel(const QGemmArgs p) {
                         float x = v[i];
                         if (p.bias) x = __fadd_rn(x, p.bias[n + i]);
                         x = act_apply(x, p.act);
-                        if (p.resid) x = __fadd_rn(x, p.resid[(size_t)m * p.N + n + i]);
+                        if (p.resid) x = __fadd_rn(x, p.resid[(size_t)m * p.resid_ld + n + i]);
                         if (p.y) p.y[(size_t)m * p.N + n + i] = x;
                         v[i] = x;
                     }
@@ -469,9 +469,9 @@ qgemm_kernel(const QGemmArgs p) {
                     ActQ qa;
                     qa.q = p.qo;
                     qa.Mpad = p.qo_Mpad;
-                    const int kc = nbase >> 7, j = (nbase >> 5) & 3;
-                    *reinterpret_cast<int4*>(qa.q + act_code(qa, kc, m, nbase & 127)) = *reinterpret_cast<const int4*>(qv);
-                    if (((nbase >> 4) & 1) == 0) {   // the lower half writes the block's scales
+                    const int gn = p.qo_n0 + nbase, kc = gn >> 7, j = (gn >> 5) & 3;
+                    *reinterpret_cast<int4*>(qa.q + act_code(qa, kc, m, gn & 127)) = *reinterpret_cast<const int4*>(qv);
+                    if (((gn >> 4) & 1) == 0) {   // the lower half writes the block's scales
                         act_dx(qa, kc, m)[j] = d;
                         if (p.qo_c) act_cx(qa, kc, m)[j] = __fmul_rn(d, (float)sum);
                     }
@@ -598,10 +598,10 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
 
 int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int act,
                  const float* resid, float* y, cudaStream_t st, const SplitK* sk, const ActQ* qo, bool qo_c,
-                 const AttnPrepOut* ap) {
+                 const AttnPrepOut* ap, int resid_ld, int qo_n0) {
     if (w.K % 128 != 0 || M <= 0 || M > a.Mpad) return -2;
     if (ap && (w.N != 3 * ap->H * fa::D || M % ap->S != 0)) return -2;
-    if (qo && (w.N % 128 != 0 || M > qo->Mpad)) return -2;
+    if (qo && (w.N % 128 != 0 || qo_n0 % 128 != 0 || M > qo->Mpad)) return -2;
     const bool q4 = w.wtype == 12;
     int bn, cg, cb;
     pick_cfg(M, w.N, w.K, qo != nullptr, ap != nullptr, bn, cg, cb);
@@ -620,7 +620,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     nsplit = (nkc + cps - 1) / cps;   // no empty split
     QGemmArgs p{a.q, a.Mpad, w.q, w.s, w.Npad, M, w.N, w.K, bias, resid, y, act,
                 sk ? sk->part : nullptr, sk ? sk->counters : nullptr, nsplit, cps,
-                qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0,
+                qo ? qo->q : nullptr, qo ? qo->Mpad : 0, qo_c ? 1 : 0, qo_n0, resid_ld > 0 ? resid_ld : w.N,
                 ap ? ap->buf : nullptr, ap ? ap->S : 1, ap ? ap->H : 1, ap ? ap->nt : 1, 0, 0};
 #define X(BN, CG, CB) \
     if (bn == BN && cg == CG && cb == CB) return q4 ? run_qgemm<BN, CG, true, CB>(p, st) : run_qgemm<BN, CG, false, CB>(p, st);

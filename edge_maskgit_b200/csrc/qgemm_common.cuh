@@ -19,6 +19,8 @@ struct QGemmArgs {
     // fused output quantizer (optional): quantize y per 32-block into ActQ tiles qo (the next
     // layer's activation); y may then be null.  Needs CW == 16 and BN % 32 == 0.
     int8_t* qo; int qo_Mpad; int qo_c;
+    int qo_n0;     // global column of output column 0 inside qo (column-split layers)
+    int resid_ld;  // row stride of resid
     // fused attention prep (optional): also store y as the f16 Q/K/V tiles of attnprep.cuh
     uint8_t* ap; int ap_S, ap_H, ap_nt;
     // persistent mode (tiles_n > 0): a 1-D grid of CTAs walks the tiles t = blockIdx.x, +gridDim.x,

@@ -5,6 +5,7 @@
 #include "kernels.h"
 #include "pack.h"
 #include "ptx.cuh"
+#include "tp.h"
 
 #include <algorithm>
 #include <cmath>
@@ -474,6 +475,15 @@ struct mgc_runtime {
     bool fuse = true;        // fused epilogue quantizers (MGC_NO_FUSE=1 runs them as separate kernels)
     int last_launches = 0;   // kernels enqueued by the last forward
     std::string only_op;     // non-empty: enqueue_forward enqueues only this op class
+    // column-split tensor parallelism (mgc_runtime_create_tp): this rank's share of every layer
+    int tp_rank = 0, tp_world = 1;
+    ncclComm_t comm = nullptr;
+    int Eg = 0, Fg = 0, Hl = 0, Vg = 0;   // local widths: E/G, F/G, heads H/G, vocabulary slice
+    float* gbuf = nullptr;                 // [G][rows][Eg] all-gathered column slices
+    float* head_w = nullptr;               // [Vg][E] this rank's vocabulary rows (zero padded)
+    float* head_b = nullptr;               // [Vg]
+    float* lgbuf = nullptr;                // [G][rows][Vg] all-gathered logits slices
+    float* lg_loc = nullptr;               // [rows][Vg]
     std::map<std::string, ProfRow> prof_rows;
 
     float* up_f32(const GgufTensor& t, size_t n) {
@@ -486,18 +496,25 @@ struct mgc_runtime {
 
 namespace {
 
-QWeight load_linear(const Gguf& g, const std::vector<std::string>& names, int K, bool& any_q4k) {
-    // several [N_i][K] weights of one type stacked along N (q|k|v): rows are independent,
-    // so concatenating the GGUF bytes is the same as one [sum N_i][K] weight.
+// A run of rows [row0, row0 + nrows) of an [N][K] GGUF tensor (nrows < 0: all rows).
+struct RowRange { std::string name; int row0 = 0, nrows = -1; };
+
+QWeight load_linear(const Gguf& g, const std::vector<RowRange>& parts, int K, bool& any_q4k) {
+    // several [N_i][K] weights (or row ranges of them) of one type stacked along N (q|k|v):
+    // rows are independent and stored back to back, so concatenating their GGUF bytes is the
+    // same as one [sum N_i][K] weight.
     std::vector<uint8_t> bytes;
     int N = 0; uint32_t type = 0;
-    for (size_t i = 0; i < names.size(); i++) {
-        const GgufTensor& t = g.req(names[i]);
-        if (t.ne[0] != K) throw Err("tensor '" + names[i] + "' has unexpected K");
+    for (size_t i = 0; i < parts.size(); i++) {
+        const GgufTensor& t = g.req(parts[i].name);
+        if (t.ne[0] != K) throw Err("tensor '" + parts[i].name + "' has unexpected K");
         if (i == 0) type = t.type;
         else if (t.type != type) throw Err("fused weights of different types");
-        bytes.insert(bytes.end(), t.data, t.data + t.bytes);
-        N += (int)t.ne[1];
+        const int rows = (int)t.ne[1], r0 = parts[i].row0, nr = parts[i].nrows < 0 ? rows : parts[i].nrows;
+        if (r0 < 0 || r0 + nr > rows) throw Err("row range outside tensor '" + parts[i].name + "'");
+        const size_t row_bytes = t.bytes / (size_t)rows;
+        bytes.insert(bytes.end(), t.data + (size_t)r0 * row_bytes, t.data + (size_t)(r0 + nr) * row_bytes);
+        N += nr;
     }
     if (type == 12) any_q4k = true;
     return upload_weight((int)type, bytes.data(), N, K);
@@ -511,9 +528,80 @@ void linear(mgc_runtime* rt, const QWeight& w, const float* xin, const ActQ& a, 
         throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
 }
 
+// One column-split forward on this rank (tensor parallel over rt->tp_world GPUs, every rank
+// enqueueing the same sequence): the layer structure of enqueue_forward with each linear
+// computing this rank's output columns and NCCL all-gathers where a full row is needed next.
+// Every output element is computed as on one GPU (same K order, same quantized inputs), and
+// the attention of a head is the same kernel, so the logits equal the single-GPU forward's.
+//   q|k|v: this rank's heads (no exchange before attention) -> attention -> all-gather the
+//   head-merged slices -> quantizer over the gathered layout -> attn_o (E/G columns, residual
+//   slice read in place) -> all-gather -> LayerNorm over the gathered layout (full rows on
+//   every rank, + quantizer) -> ffn_up (F/G columns, GELU, quantizes into the full activation
+//   tiles at its own column offset) -> all-gather of those int8 tiles in place -> ffn_down ->
+//   all-gather -> LayerNorm.  output_proj and its LayerNorm run replicated; the MLM head is
+//   split by vocabulary rows and its logits all-gathered.
+void enqueue_forward_tp(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits) {
+    const int R = B * S, E = rt->E, G = rt->tp_world, g = rt->tp_rank, Eg = rt->Eg, Fg = rt->Fg, Vg = rt->Vg;
+    cudaStream_t st = rt->st;
+    const bool qc = rt->any_q4k;
+    const long long slice = (long long)R * Eg;   // floats per rank block of gbuf
+    auto gather = [&](const void* send, void* recv, size_t bytes) {
+        const std::string e = tp_all_gather(send, recv, bytes, rt->comm, st);
+        if (!e.empty()) throw Err(e);
+    };
+    auto q = [&](const QWeight& w, const ActQ& a, const float* bias, int act, const float* resid, int resid_ld,
+                 float* y, const ActQ* qo, int qo_n0, const AttnPrepOut* ap) {
+        if (w.wtype == 0) throw Err("tensor parallel needs quantized linears");
+        if (launch_qgemm(w, a, R, bias, act, resid, y, st, nullptr, qo, qc, ap, resid_ld, qo_n0) != 0)
+            throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+    };
+    const int launches0 = g_launch_count;
+    launch_embed_ln(rt->tok, rt->V, rt->pos, E, tokens, B, S, rt->g0, rt->b0, rt->eps, rt->x, &rt->aE, qc, st);
+    const float scale = 1.0f / std::sqrt((float)rt->Dh);
+    // ffn_up writes chunks [g*Fg/128, (g+1)*Fg/128) of the full activation tiles: one contiguous run
+    const size_t f_slice = (size_t)(Fg / 128) * (rt->Mpad / 128) * kActTile;
+    for (int l = 0; l < rt->n_layer; l++) {
+        const LayerW& L = rt->layers[l];
+        const AttnPrepOut ap = attn_prep_out(rt->attn_scratch, B, S, rt->Hl);
+        q(L.qkv, rt->aE, L.bqkv, 0, nullptr, 0, nullptr, nullptr, 0, &ap);
+        if (launch_flash_attn(nullptr, B, S, rt->Hl, rt->Dh, scale, rt->att, rt->attn_scratch, rt->attn_scratch_n, st,
+                              nullptr, false, nullptr, true) != 0)
+            throw Err("flash attention launch failed");
+        gather(rt->att, rt->gbuf, sizeof(float) * (size_t)slice);
+        if (!launch_quant_blocked(rt->gbuf, Eg, slice, R, E, rt->aE, qc, st)) throw Err("gathered quantizer failed");
+        q(L.o, rt->aE, L.bo, 0, rt->x + (size_t)g * Eg, E, rt->t, nullptr, 0, nullptr);
+        gather(rt->t, rt->gbuf, sizeof(float) * (size_t)slice);
+        if (!launch_ln_blocked(rt->gbuf, Eg, slice, L.g1, L.b1, R, E, rt->eps, rt->x, &rt->aE, qc, st))
+            throw Err("gathered LayerNorm failed");
+        q(L.up, rt->aE, L.bup, 1, nullptr, 0, nullptr, &rt->aF, g * Fg, nullptr);
+        gather(rt->aF.q + (size_t)g * f_slice, rt->aF.q, f_slice);
+        q(L.down, rt->aF, L.bdown, 0, rt->x + (size_t)g * Eg, E, rt->t, nullptr, 0, nullptr);
+        gather(rt->t, rt->gbuf, sizeof(float) * (size_t)slice);
+        if (!launch_ln_blocked(rt->gbuf, Eg, slice, L.g2, L.b2, R, E, rt->eps, rt->x, &rt->aE, qc, st))
+            throw Err("gathered LayerNorm failed");
+    }
+    if (launch_qgemm(rt->proj, rt->aE, R, rt->bproj, 1, nullptr, rt->t, st, nullptr) != 0)
+        throw Err(std::string("qgemm launch failed: ") + cudaGetErrorString(cudaGetLastError()));
+    launch_ln(rt->t, rt->gout, rt->bout, R, E, rt->eps, rt->x, nullptr, false, st);
+    launch_gemm_f32(rt->head_w, rt->x, R, Vg, E, rt->head_b, 0, nullptr, rt->lg_loc, st);
+    gather(rt->lg_loc, rt->lgbuf, sizeof(float) * (size_t)R * Vg);
+    launch_ungather_cols(rt->lgbuf, R, Vg, rt->V, logits, st);
+    CK(cudaPeekAtLastError());
+    rt->last_launches = g_launch_count - launches0;
+    (void)G;
+}
+
 // Enqueue one transformer forward (build_transformer, mg-transformer.cpp:32-111) on rt->st.
 // dump (device, optional) receives the 51 named tensors back to back.
 void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits, float* dump) {
+    if (rt->tp_world > 1) {
+        if (dump || rt->prof || !rt->only_op.empty())
+            throw Err("tensor-parallel runtime: no dump / per-op profile (use a single-GPU runtime)");
+        if (B * S > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
+        if (S > rt->n_pos) throw Err("forward: S exceeds n_positions");
+        enqueue_forward_tp(rt, tokens, B, S, logits);
+        return;
+    }
     const int R = B * S, E = rt->E, F = rt->F;
     if (R > rt->max_rows) throw Err("forward: B*S exceeds the runtime's max_rows");
     if (S > rt->n_pos) throw Err("forward: S exceeds n_positions");
@@ -607,7 +695,7 @@ void enqueue_forward(mgc_runtime* rt, const int32_t* tokens, int B, int S, float
 // Grow the attention scratch (prep tiles + key-split partials) for B images of S tokens; the
 // captured graphs hold the old pointer, so they are dropped.  Never called inside a capture.
 void ensure_attn_scratch(mgc_runtime* rt, int B, int S) {
-    const size_t need = attn_scratch_floats(B, S, rt->n_head);
+    const size_t need = attn_scratch_floats(B, S, rt->Hl);
     if (rt->attn_scratch_n >= need) return;
     CK(cudaStreamSynchronize(rt->st));
     for (auto& kv : rt->graphs) cudaGraphExecDestroy(kv.second);
@@ -654,6 +742,8 @@ void destroy_runtime(mgc_runtime* rt) {
     cudaSetDevice(rt->device);
     if (rt->st) cudaStreamSynchronize(rt->st);
     for (auto& kv : rt->graphs) cudaGraphExecDestroy(kv.second);
+    tp_comm_destroy(rt->comm);
+    cudaFree(rt->gbuf); cudaFree(rt->lgbuf); cudaFree(rt->lg_loc);
     for (auto& L : rt->layers) { free_weight(L.qkv); free_weight(L.o); free_weight(L.up); free_weight(L.down); }
     free_weight(rt->proj);
     for (float* p : rt->f32_allocs) cudaFree(p);
@@ -678,11 +768,19 @@ void destroy_runtime(mgc_runtime* rt) {
 
 extern "C" {
 
-int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime** out) {
-    return guard([&] {
+}  // extern "C"
+
+namespace {
+
+// Shared body of mgc_runtime_create (world == 1) and mgc_runtime_create_tp.
+void create_runtime(const char* path, int max_rows, int device, int rank, int world, const ncclUniqueId* id,
+                    mgc_runtime** out) {
         if (!path || !out || max_rows <= 0) throw Err("mgc_runtime_create: bad arguments");
+        if (world < 1 || rank < 0 || rank >= world) throw Err("mgc_runtime_create_tp: bad rank / world");
         std::unique_ptr<mgc_runtime, void (*)(mgc_runtime*)> rt(new mgc_runtime(), destroy_runtime);
         rt->device = device;
+        rt->tp_rank = rank;
+        rt->tp_world = world;
         if (const char* e = std::getenv("MGC_NO_FUSE")) rt->fuse = e[0] != '1';
         CK(cudaSetDevice(device));
         cudaDeviceProp prop;
@@ -713,31 +811,45 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->pos = rt->up_f32(pos, (size_t)E * rt->n_pos);
         rt->g0 = rt->up_f32(g.req("token_embd_norm.weight"), E);
         rt->b0 = rt->up_f32(g.req("token_embd_norm.bias"), E);
+        // column split over `world` ranks: whole heads of q|k|v, E/G rows of attn_o and
+        // ffn_down, F/G rows of ffn_up (each rank computes those output columns in full)
+        const int G = world;
+        if (G > 1 && (rt->n_head % G || F % (128 * G) || (E / G) % 32 || (E / G) % 8))
+            throw Err("tensor parallel: n_head and n_ffn/128 must divide by the world size");
+        rt->Eg = E / G; rt->Fg = F / G; rt->Hl = rt->n_head / G;
+        const int Eg = rt->Eg, Fg = rt->Fg;
+        auto bias_slice = [&](const GgufTensor& t, int n, int r0, int nr) {
+            if (t.type != 0 || (int)t.ne[0] != n) throw Err("unexpected bias tensor");
+            float* d = dupload((const float*)t.data + r0, (size_t)nr);
+            rt->f32_allocs.push_back(d);
+            return d;
+        };
         bool q4 = false;
         for (int l = 0; l < rt->n_layer; l++) {
             const std::string p = "blk." + std::to_string(l) + ".";
             LayerW L;
-            L.qkv = load_linear(g, {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, E, q4);
-            L.o = load_linear(g, {p + "attn_o.weight"}, E, q4);
-            L.up = load_linear(g, {p + "ffn_up.weight"}, E, q4);
-            L.down = load_linear(g, {p + "ffn_down.weight"}, F, q4);
+            L.qkv = load_linear(g, {{p + "attn_q.weight", rank * Eg, Eg}, {p + "attn_k.weight", rank * Eg, Eg},
+                                    {p + "attn_v.weight", rank * Eg, Eg}}, E, q4);
+            L.o = load_linear(g, {{p + "attn_o.weight", rank * Eg, Eg}}, E, q4);
+            L.up = load_linear(g, {{p + "ffn_up.weight", rank * Fg, Fg}}, E, q4);
+            L.down = load_linear(g, {{p + "ffn_down.weight", rank * Eg, Eg}}, F, q4);
             std::vector<float> bqkv;
             for (const char* nm : {"attn_q.bias", "attn_k.bias", "attn_v.bias"}) {
                 const GgufTensor& t = g.req(p + nm);
-                bqkv.insert(bqkv.end(), (const float*)t.data, (const float*)t.data + E);
+                bqkv.insert(bqkv.end(), (const float*)t.data + rank * Eg, (const float*)t.data + (rank + 1) * Eg);
             }
             L.bqkv = dupload(bqkv.data(), bqkv.size());
             rt->f32_allocs.push_back(L.bqkv);
-            L.bo = rt->up_f32(g.req(p + "attn_o.bias"), E);
-            L.bup = rt->up_f32(g.req(p + "ffn_up.bias"), F);
-            L.bdown = rt->up_f32(g.req(p + "ffn_down.bias"), E);
+            L.bo = bias_slice(g.req(p + "attn_o.bias"), E, rank * Eg, Eg);
+            L.bup = bias_slice(g.req(p + "ffn_up.bias"), F, rank * Fg, Fg);
+            L.bdown = bias_slice(g.req(p + "ffn_down.bias"), E, rank * Eg, Eg);
             L.g1 = rt->up_f32(g.req(p + "attn_norm.weight"), E);
             L.b1 = rt->up_f32(g.req(p + "attn_norm.bias"), E);
             L.g2 = rt->up_f32(g.req(p + "ffn_norm.weight"), E);
             L.b2 = rt->up_f32(g.req(p + "ffn_norm.bias"), E);
             rt->layers.push_back(L);
         }
-        rt->proj = load_linear(g, {"output_proj.weight"}, E, q4);
+        rt->proj = load_linear(g, {{"output_proj.weight"}}, E, q4);
         rt->bproj = rt->up_f32(g.req("output_proj.bias"), E);
         rt->gout = rt->up_f32(g.req("output_norm.weight"), E);
         rt->bout = rt->up_f32(g.req("output_norm.bias"), E);
@@ -754,7 +866,7 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         rt->aE = alloc_actq(rt->Mpad, E);
         rt->aF = alloc_actq(rt->Mpad, F);
         rt->sk = alloc_splitk(rt->Mpad, std::max(3 * E, F));
-        rt->attn_scratch_n = attn_scratch_floats(1, rt->Mpad, rt->n_head);
+        rt->attn_scratch_n = attn_scratch_floats(1, rt->Mpad, rt->Hl);
         rt->attn_scratch = dalloc<float>(rt->attn_scratch_n);
         CK(cudaMemset(rt->attn_scratch, 0, rt->attn_scratch_n * sizeof(float)));
         CK(cudaMallocHost(&rt->h_tokens, sizeof(int32_t) * R));
@@ -764,6 +876,23 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         CK(cudaMallocHost(&rt->h_sid, sizeof(int32_t) * R));
         CK(cudaMallocHost(&rt->h_psid, sizeof(float) * R));
         CK(cudaMallocHost(&rt->h_logits, sizeof(float) * R * rt->V));
+        if (G > 1) {
+            // the MLM head (token_embd as F32 weight) split by vocabulary rows, padded to Vg
+            const int V = rt->V, Vg = (V + G - 1) / G, v0 = std::min(V, rank * Vg), nv = std::min(V, v0 + Vg) - v0;
+            rt->Vg = Vg;
+            std::vector<float> hw((size_t)Vg * E, 0.0f), hb(Vg, 0.0f);
+            std::memcpy(hw.data(), (const float*)tok.data + (size_t)v0 * E, sizeof(float) * (size_t)nv * E);
+            std::memcpy(hb.data(), (const float*)g.req("output.bias").data + v0, sizeof(float) * nv);
+            rt->head_w = dupload(hw.data(), hw.size());
+            rt->head_b = dupload(hb.data(), hb.size());
+            rt->f32_allocs.push_back(rt->head_w);
+            rt->f32_allocs.push_back(rt->head_b);
+            rt->gbuf = dalloc<float>(R * E);
+            rt->lgbuf = dalloc<float>((size_t)G * R * Vg);
+            rt->lg_loc = dalloc<float>(R * Vg);
+            const std::string e = tp_comm_init(&rt->comm, G, *id, rank);
+            if (!e.empty()) throw Err(e);
+        }
         CK(cudaDeviceSynchronize());
         // one eager forward: sets every kernel's attributes outside any later stream capture
         CK(cudaMemsetAsync(rt->tokens, 0, sizeof(int32_t) * R, rt->st));
@@ -771,6 +900,34 @@ int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime**
         CK(cudaStreamSynchronize(rt->st));
         check_dev_error();
         *out = rt.release();
+}
+
+}  // namespace
+
+extern "C" {
+
+int mgc_runtime_create(const char* path, int max_rows, int device, mgc_runtime** out) {
+    return guard([&] { create_runtime(path, max_rows, device, 0, 1, nullptr, out); });
+}
+
+int mgc_tp_unique_id(uint8_t out[128]) {
+    return guard([&] {
+        static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+        if (!out) throw Err("mgc_tp_unique_id: bad arguments");
+        ncclUniqueId id;
+        const std::string e = tp_unique_id(&id);
+        if (!e.empty()) throw Err(e);
+        std::memcpy(out, &id, sizeof(id));
+    });
+}
+
+int mgc_runtime_create_tp(const char* path, int max_rows, int device, int rank, int world, const uint8_t id[128],
+                          mgc_runtime** out) {
+    return guard([&] {
+        if (!id) throw Err("mgc_runtime_create_tp: bad arguments");
+        ncclUniqueId uid;
+        std::memcpy(&uid, id, sizeof(uid));
+        create_runtime(path, max_rows, device, rank, world, &uid, out);
     });
 }
 

@@ -16,7 +16,7 @@ import numpy as np
 
 from ._lib import MgcError, check, lib
 
-__all__ = ["CudaRuntime", "QWeight", "MgcError", "pack_q8_0", "pack_q4_k", "dequant",
+__all__ = ["CudaRuntime", "QWeight", "MgcError", "pack_q8_0", "pack_q4_k", "dequant", "tp_unique_id",
            "quantize_act", "gemm_f32", "layernorm_affine", "flash_attn", "embed", "device_error",
            "F32", "Q8_0", "Q4_K"]
 
@@ -176,12 +176,29 @@ class OpProfile:   # include/mg-opencl.hpp:17-21
     ms: float
 
 
-class CudaRuntime:
-    """mg::OpenCLRuntime's counterpart for the MaskGIT transformer on one B200."""
+def tp_unique_id() -> bytes:
+    """128-byte NCCL id for a tensor-parallel runtime group (make it on one rank, share it)."""
+    buf = (C.c_uint8 * 128)()
+    check(lib.mgc_tp_unique_id(buf), "tp_unique_id")
+    return bytes(buf)
 
-    def __init__(self, gguf_path: str, max_rows: int = 257, device: int = 0):
+
+class CudaRuntime:
+    """mg::OpenCLRuntime's counterpart for the MaskGIT transformer on one B200.
+
+    tp=(rank, world, id) makes this process rank `rank` of a column-split tensor-parallel group
+    of `world` GPUs (id from tp_unique_id() on one rank); all ranks then run every forward with
+    the same inputs and each gets the full logits."""
+
+    def __init__(self, gguf_path: str, max_rows: int = 257, device: int = 0, tp=None):
         h = C.c_void_p()
-        check(lib.mgc_runtime_create(str(gguf_path).encode(), max_rows, device, C.byref(h)), "runtime_create")
+        if tp is None:
+            check(lib.mgc_runtime_create(str(gguf_path).encode(), max_rows, device, C.byref(h)), "runtime_create")
+        else:
+            rank, world, uid = tp
+            idb = (C.c_uint8 * 128).from_buffer_copy(uid)
+            check(lib.mgc_runtime_create_tp(str(gguf_path).encode(), max_rows, device, rank, world, idb, C.byref(h)),
+                  "runtime_create_tp")
         self._h = h
         hp = np.zeros(10, np.int32)
         check(lib.mgc_runtime_hparams(h, _ptr(hp)))

@@ -109,6 +109,18 @@ typedef struct mgc_runtime mgc_runtime;
  * CUDA stream and three host threads that copy logits out during mgc_transformer_forward. */
 int mgc_runtime_create(const char* gguf_path, int max_rows, int device, mgc_runtime** out);
 void mgc_runtime_destroy(mgc_runtime* rt);
+
+/* Column-split tensor parallelism over `world` GPUs, one process (or thread) per rank, all
+ * ranks creating their runtime concurrently and then calling every forward with the same
+ * arguments (the long-sequence step: batch 4 x 4097 tokens; no counterpart in the reference,
+ * which runs on one device).  Rank r holds heads [r*H/G, (r+1)*H/G) of q|k|v, rows
+ * [r*E/G, (r+1)*E/G) of attn_o and ffn_down, rows [r*F/G, ...) of ffn_up and a 1/G slice of
+ * the MLM head; NCCL all-gathers (loaded with dlopen on first use) join the slices.  Every rank
+ * returns the full logits, equal to the single-GPU runtime's.  n_head and n_ffn/128 must be
+ * divisible by world.  id: 128 bytes from mgc_tp_unique_id on one rank, shared by the host. */
+int mgc_tp_unique_id(uint8_t id_out[128]);
+int mgc_runtime_create_tp(const char* gguf_path, int max_rows, int device, int rank, int world,
+                          const uint8_t id[128], mgc_runtime** out);
 /* n_layer n_head n_embd n_ffn head_dim vocab n_tokens mask_id codebook wtype */
 int mgc_runtime_hparams(const mgc_runtime* rt, int32_t out[10]);
 const char* mgc_runtime_device_name(const mgc_runtime* rt);
