@@ -155,21 +155,38 @@ qgemm_kernel(const QGemmArgs p) {
                     }
                 }
             };
+            // Rows of the m-tile that hold data, rounded up to the 8-row swizzle atom: a partial
+            // last m-tile (M=257 leaves one row in the third) copies only those rows of codes,
+            // dx (and dx*sumx) -- rows past M are never stored, so the MMA may read whatever the
+            // stage held.  Every CTA of an m-tile re-reads its activation slab from L2, and that
+            // ingest is what bounds these kernels at small M.
+            auto a_rows = [&]() { const int r = p.M - mt * 128; return r >= 128 ? 128 : (r + 7) & ~7; };
+            auto tx_bytes = [&]() {
+                const int r = a_rows();
+                return r == 128 ? C::TX_BYTES : C::TX_BYTES - SUB * (C::A_BYTES - (uint32_t)r * (Q4K ? 160u : 144u));
+            };
             auto copy_a = [&](int i, int gc) {
-                const int kc = kc0 + i, s = gc % NST;
+                const int kc = kc0 + i, s = gc % NST, r = a_rows();
                 uint8_t* st = smem + s * C::STAGE;
 #pragma unroll
                 for (int u = 0; u < SUB; u++) {
                     const size_t kk = (size_t)kc * SUB + u;   // 128-K activation tile index
-                    bulk_g2s(st + u * C::A_BYTES, p.aq + (kk * (p.Mpad / 128) + mt) * kActTile, C::A_BYTES,
-                             &full[s]);
+                    const int8_t* src = p.aq + (kk * (p.Mpad / 128) + mt) * kActTile;
+                    uint8_t* dst = st + u * C::A_BYTES;
+                    if (r == 128) {
+                        bulk_g2s(dst, src, C::A_BYTES, &full[s]);
+                    } else {
+                        bulk_g2s(dst, src, (uint32_t)r * 128u, &full[s]);
+                        bulk_g2s(dst + C::OFF_DX, src + C::OFF_DX, (uint32_t)r * 16u, &full[s]);
+                        if constexpr (Q4K) bulk_g2s(dst + C::OFF_CX, src + C::OFF_CX, (uint32_t)r * 16u, &full[s]);
+                    }
                 }
             };
             // the first stages are free: their weights go out before the wait on the preceding kernel
             const int npre = nloc < NST ? nloc : NST;
             tile_of(0, n0, mt);
             for (int i = 0; i < npre; i++) {
-                mbar_arrive_expect_tx(&full[i], C::TX_BYTES);
+                mbar_arrive_expect_tx(&full[i], tx_bytes());
                 copy_w(i, i);
                 last_it[i] = 0;
             }
@@ -181,7 +198,7 @@ qgemm_kernel(const QGemmArgs p) {
                 for (int i = ti == 0 ? npre : 0; i < nloc; i++) {
                     const int gc = ti * nloc + i, s = gc % NST, it = gc / NST;
                     if (!(go = mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 1))) break;
-                    mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
+                    mbar_arrive_expect_tx(&full[s], tx_bytes());
                     copy_w(i, gc);
                     copy_a(i, gc);
                     last_it[s] = it;
