@@ -61,23 +61,25 @@ __global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, 
 // NCH 32-key chunks, chunk index ch = NCH * part + cc (r[cc][j] = key 32 ch + j, as f32 bits).
 // Row max of the raw scores (4 chains), scaled once: rounding is monotonic, so this equals the
 // max of the scaled scores.
-template <int NCH>
+// FULL: every key of the thread's chunks is valid (all but a key range's last tile), so the
+// per-key masking compiles away.
+template <int NCH, bool FULL = false>
 __device__ __forceinline__ float tile_row_max(const uint32_t (&r)[NCH][32], int part, int nch, int nvalid, float c1) {
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
     for (int cc = 0; cc < NCH; cc++) {
         const int ch = NCH * part + cc;
-        if (ch >= nch) break;
+        if (!FULL && ch >= nch) break;
 #pragma unroll
         for (int j = 0; j < 32; j++)
-            if (ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
+            if (FULL || ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
     }
     return __fmul_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), c1);
 }
 // p = 2^(s*c1 - m) on pairs (one packed FMA, two MUFU ex2), P_hi = f16(p), P_lo = f16(p - P_hi)
 // into the swizzled P blocks of the sets ph / pl (64 keys per block); returns the partial row
 // sum of these chunks (packed partials).
-template <int NCH>
+template <int NCH, bool FULL = false>
 __device__ __forceinline__ float tile_probs(const uint32_t (&r)[NCH][32], int part, int nch, int nvalid, float c1,
                                             float m_new, int row, uint8_t* ph, uint8_t* pl) {
     const uint64_t c1x2 = pack2(c1, c1), nm2 = pack2(-m_new, -m_new), neg1 = pack2(-1.0f, -1.0f);
@@ -85,8 +87,8 @@ __device__ __forceinline__ float tile_probs(const uint32_t (&r)[NCH][32], int pa
 #pragma unroll
     for (int cc = 0; cc < NCH; cc++) {
         const int ch = NCH * part + cc;
-        if (ch >= nch) break;
-        const bool full = ch * 32 + 32 <= nvalid;
+        if (!FULL && ch >= nch) break;
+        const bool full = FULL || ch * 32 + 32 <= nvalid;
         uint8_t* bh = ph + (ch >> 1) * fa::P_BLK;
         uint8_t* bl = pl + (ch >> 1) * fa::P_BLK;
 #pragma unroll
@@ -399,7 +401,9 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
     } else {
         // ------------------------------------------------------------------ softmax warps
         // warps w, w+4, w+8, w+12 share TMEM lanes 32(w%4).. (query row per lane); warp part p
-        // = w / 4 owns keys [32p, 32p+32) of each tile and output dims [12p, 12p+12)
+        // = w / 4 owns keys [32p, 32p+32) of each tile and output dims [12p, 12p+12).  Only the
+        // four warps of a row quarter exchange the row max and sum, so each quarter synchronises
+        // on its own named barrier and the quarters run independently.
         const int row = (warp & 3) * 32 + lane;
         const uint32_t t_row = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const bool wact = q0 + (warp & 3) * 32 < S;   // warp-uniform: owns at least one real query row
@@ -451,24 +455,26 @@ __global__ void __launch_bounds__(fa::THREADS, 1) flash_attn_tc(const uint8_t* _
             if (ok && wact) {
                 if (part < nch) tmem_ld32(t_row + (i & 1) * BC + part * 32, r[0]);
                 tmem_ld_wait();
-                mloc = tile_row_max<1>(r, part, nch, nvalid, c1);
+                mloc = nvalid == BC ? tile_row_max<1, true>(r, part, nch, nvalid, c1)
+                                    : tile_row_max<1>(r, part, nch, nvalid, c1);
             }
             xmax[part * BM + row] = mloc;
-            asm volatile("bar.sync 1, 512;" ::: "memory");
+            named_bar_sync(2 + (warp & 3), 128);   // the 4 warps of this query-row quarter
             const float m_new = fmaxf(fmaxf(m_i, fmaxf(xmax[row], xmax[BM + row])),
                                       fmaxf(xmax[2 * BM + row], xmax[3 * BM + row]));
             float lsum = 0.0f;
             if (ok && wact) {
                 alpha = exp2f(m_i - m_new);
                 uint8_t* ps = sm + OFF_P + (i & 1) * P_SET;
-                lsum = tile_probs<1>(r, part, nch, nvalid, c1, m_new, row, ps, ps + P_BYTES);
+                lsum = nvalid == BC ? tile_probs<1, true>(r, part, nch, nvalid, c1, m_new, row, ps, ps + P_BYTES)
+                                    : tile_probs<1>(r, part, nch, nvalid, c1, m_new, row, ps, ps + P_BYTES);
             }
             fence_async_smem();   // P is read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + (i & 1));
             xsum[part * BM + row] = lsum;
-            asm volatile("bar.sync 1, 512;" ::: "memory");
+            named_bar_sync(2 + (warp & 3), 128);   // the 4 warps of this query-row quarter
             if (ok && wact) {
                 l_i = __fadd_rn(__fmul_rn(alpha, l_i), __fadd_rn(__fadd_rn(xsum[row], xsum[BM + row]),
                                                                  __fadd_rn(xsum[2 * BM + row], xsum[3 * BM + row])));

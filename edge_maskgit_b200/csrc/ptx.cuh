@@ -91,6 +91,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads, bulk copies).
 __device__ __forceinline__ void fence_async_smem() {
