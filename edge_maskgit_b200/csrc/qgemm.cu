@@ -565,7 +565,7 @@ static int run_qgemm(QGemmArgs a, cudaStream_t st) {
 // Tile shape (BN columns, CG column groups of promotion warps, CB 32-blocks per chunk).
 // MGC_QGEMM_CFG="BN,CG[,CB]" overrides the heuristic (used to sweep shapes); MGC_QGEMM_CB=4
 // keeps 4-block chunks everywhere.
-static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, int& cg, int& cb) {
+static void pick_cfg(int M, int N, int K, bool q4k, bool fused_quant, bool prep, int& bn, int& cg, int& cb) {
     struct Overrides { int fbn = 0, fcg = 0, fcb = 0, cb_max = 8; };
     static const Overrides ov = [] {   // read once (thread-safe static initialisation)
         Overrides o;
@@ -592,13 +592,17 @@ static void pick_cfg(int M, int N, int K, bool fused_quant, bool prep, int& bn, 
     static const int cand8[4][2] = {{16, 4}, {32, 4}, {48, 6}, {64, 4}}, cand8p[4][2] = {{16, 2}, {32, 4}, {48, 6}, {64, 4}},
                      cand16[4][2] = {{16, 1}, {32, 2}, {48, 3}, {64, 4}};
     const auto& cand = fused_quant ? cand16 : prep ? cand8p : cand8;
-    // Many waves (the CTAs will run persistent): the wave count no longer separates the widths;
-    // 32-wide tiles with four 8-column promotion warps and 8-block chunks measured fastest there
-    // (config 5: 73.7 -> 67.6 ms against the 64-wide tiles the wave rule picks).
+    // Many waves (the CTAs will run persistent): the wave count no longer separates the widths.
+    // Measured at M = 4097 and 16388 (768 <-> 3072 shapes): Q8_0 runs fastest with 48-wide tiles
+    // of three 16-column groups and 4-block chunks (87.8 vs 92.7 us for 4097 x 768 -> 3072 with
+    // 32-wide tiles), Q4_K with 32-wide tiles of two 16-column groups and 8-block chunks (125.6
+    // vs 130.0 us); both keep the activation re-reads per promotion below the 16- and 32-wide
+    // tiles with more column groups, which are bound by the L2 ingest of those re-reads.
     if (!fused_quant && (long)((N + 63) / 64) * mt > wave && K % 256 == 0) {
-        bn = 32;
-        cg = 4;
-        cb = chunk(bn, cg);
+        if (q4k) { bn = 32; cg = 2; cb = chunk(bn, cg); }
+        else { bn = 48; cg = 3; cb = 4; }
+        if ((long)((N + bn - 1) / bn) * bn <= npad) return;
+        bn = 32; cg = 4; cb = chunk(bn, cg);   // (48 would read past the padded weight rows)
         return;
     }
     long best = -1;
@@ -621,7 +625,7 @@ int launch_qgemm(const QWeight& w, const ActQ& a, int M, const float* bias, int 
     if (qo && (w.N % 128 != 0 || qo_n0 % 128 != 0 || M > qo->Mpad)) return -2;
     const bool q4 = w.wtype == 12;
     int bn, cg, cb;
-    pick_cfg(M, w.N, w.K, qo != nullptr, ap != nullptr, bn, cg, cb);
+    pick_cfg(M, w.N, w.K, w.wtype == 12, qo != nullptr, ap != nullptr, bn, cg, cb);
     if (w.K % (32 * cb) != 0) return -2;
     // Split-K (MGC_QGEMM_SPLITK=<n>) is off by default: on the config-1 shapes it measured
     // slower than one CTA per tile (ncu: attn_o 11 -> 26 us with 3 splits, ffn_down 22 -> 38 us
