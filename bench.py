@@ -293,7 +293,7 @@ def run_cuda_arm(args) -> None:
     dev_ms, e2e_ms, q_ms = _max_over_ranks([dev_ms, e2e_ms, q_ms], world)
     extras = {}
     if not args.no_extras:
-        for name, fn in (("config4", c4_measure), ("config5", c5_measure)):
+        for name, fn in (("config4", c4_measure), ("config5", c5_measure), ("vqgan", vqgan_measure)):
             try:
                 extras[name] = fn(max(2, min(args.steps, 3)), 1, world, rank, local)
             except Exception as e:   # an extra workload must not cost the headline line
@@ -482,6 +482,153 @@ def run_decode_workload(args) -> None:
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- VQGAN decoder
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 148 SMs x 128 FP32 lanes x FMA at max clock
+
+
+def vqgan_flops(spec) -> float:
+    """Conv FLOPs of one decode (2 * k^2 * IC * OC * H * W summed over the decoder's convs,
+    src/mg-vqgan.cpp:67-108); GroupNorm / SiLU / gather are O(activations) and not counted."""
+    from edge_maskgit_b200 import synth
+    v = spec.vqgan
+    L = spec.latent
+    mult, nrb = list(v.channel_multipliers), v.num_res_blocks
+    side = {}
+    res = L
+    side["vqgan.decoder.conv_in"] = res
+    for l in range(nrb):
+        side[f"vqgan.decoder.res_blocks.0.{l}."] = res
+    for bi, i in enumerate(range(len(mult) - 1, -1, -1), start=1):
+        for l in range(nrb):
+            side[f"vqgan.decoder.res_blocks.{bi}.{l}."] = res
+        if i > 0:
+            res *= 2
+            side[f"vqgan.decoder.res_blocks.{bi}.{nrb + 1}"] = res
+    side["vqgan.decoder.conv_out"] = res
+    total = 0.0
+    for name, shape, kind in synth.vqgan_tensor_list(spec):
+        if kind != "conv":
+            continue
+        base = name[: -len(".weight")]
+        key = base if base in side else base[: base.rfind(".") + 1]
+        r = side[key]
+        oc, ic, k, _ = shape
+        total += 2.0 * k * k * ic * oc * r * r
+    return total
+
+
+def ensure_vqgan_model(small: bool = False) -> tuple[Path, object]:
+    from edge_maskgit_b200 import synth
+    vq = synth.VqganSpec(filters=32, embedding_dim=32) if small else synth.VqganSpec()
+    spec = synth.vqgan_spec(vq, n_tokens=16 if small else 256)
+    path = MODEL_DIR / ("vqgan_small.gguf" if small else "vqgan.gguf")
+    if not path.exists():
+        MODEL_DIR.mkdir(parents=True, exist_ok=True)
+        tmp = path.with_suffix(f".tmp{os.getpid()}")
+        synth.make_model(tmp, spec)
+        os.replace(tmp, path)
+    return path, spec
+
+
+def reference_vqgan_s() -> tuple[float, str]:
+    """The reference's own decoder (libmgref: build_vqgan_decoder on mg-cpu, one thread) on the
+    small decoder, scaled to the MaskGIT decoder by conv FLOPs (its scalar direct conv runs at a
+    fixed FLOP rate; the full decoder takes several minutes)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    if not O.ref_available():
+        raise RuntimeError("oracle/_ref/libmgref.so is not built")
+    sp, sspec = ensure_vqgan_model(small=True)
+    _, fspec = ensure_vqgan_model()
+    grid = np.random.default_rng(7).integers(0, 1024, sspec.n_tokens).astype(np.int32)
+    t0 = time.perf_counter()
+    O.ref_vqgan(sp, grid, sspec.resolution)
+    dt = time.perf_counter() - t0
+    scale = vqgan_flops(fspec) / vqgan_flops(sspec)
+    return dt * scale, (f"reference decoder (libmgref, mg-cpu, 1 thread) on the filters-32 64x64 decoder: "
+                        f"{dt:.2f} s, x{scale:.1f} by conv FLOPs to the 256x256 decoder")
+
+
+def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, batch: int = 8) -> dict:
+    """VQGAN decode of seeded token grids on each rank (replicas: each rank decodes its own
+    images, no collective).  Device timing: the decode graph on device buffers (CUDA events on
+    its stream); e2e: mgc_vqgan_decode with host grids in and the host HWC image out."""
+    import torch
+    from edge_maskgit_b200 import runtime as rt
+
+    if rank == 0:
+        ensure_vqgan_model()
+    _barrier(world)
+    path, spec = ensure_vqgan_model()
+    dec = rt.VqganDecoder(path, max_images=batch, device=local)
+    R = dec.resolution
+    grids = np.random.default_rng(100 + rank).integers(0, 1024, (batch, spec.n_tokens)).astype(np.int32)
+    g_dev = torch.from_numpy(grids).cuda()
+    out1 = torch.empty((1, R, R, 3), dtype=torch.float32, device="cuda")
+    outb = torch.empty((batch, R, R, 3), dtype=torch.float32, device="cuda")
+    host_img = np.empty((1, R, R, 3), np.float32)
+    res = {}
+    for n, out in ((1, out1), (batch, outb)):
+        for _ in range(warmup):
+            dec.decode_device(g_dev, out, n)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        e0.record()
+        for _ in range(steps):
+            dec.decode_device(g_dev, out, n)
+        e1.record()
+        torch.cuda.synchronize()
+        res[n] = _max_over_ranks([e0.elapsed_time(e1) / steps], world)[0]
+    launches = dec.launches()
+    for _ in range(warmup):
+        dec.decode(grids[0], out=host_img)
+    _barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        dec.decode(grids[0], out=host_img)
+    e2e_ms = _max_over_ranks([(time.perf_counter() - t0) * 1e3 / steps], world)[0]
+    dec.close()
+    fl = vqgan_flops(spec)
+    ach = fl / (res[1] * 1e-3) / 1e12
+    return {"workload": "VQGAN decode, MaskGIT decoder (filters 128, mult 1,1,2,2,4, 16x16 -> 256x256), f32",
+            "parallelism": f"replicas x{world}", "scaling": "weak",
+            "ms_per_image": res[1], "images_per_s": world * 1e3 / res[1],
+            f"ms_per_batch{batch}": res[batch], f"images_per_s_batch{batch}": world * batch * 1e3 / res[batch],
+            "e2e_ms_per_image": e2e_ms, "gpu_launches_per_decode": launches,
+            "conv_gflop_per_image": fl / 1e9,
+            "roofline": {"bound": "fp32", "achieved": ach, "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
+                         "frac": ach / FP32_NOMINAL_TFLOPS,
+                         "note": "whole decode at 1 image (conv FLOPs / decode time) against the nominal "
+                                 "FP32 FMA rate at max clock"}}
+
+
+def run_vqgan_workload(args) -> None:
+    world, rank, local = _dist()
+    m = vqgan_measure(args.steps, args.warmup, world, rank, local)
+    if rank == 0:
+        out = {"metric": "VQGAN images/s", "value": m["images_per_s"], "unit": "images/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_image"],
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+               "data": "synthetic (seeded decoder weights and token grids)",
+               "config": {"workload": m["workload"], "parallelism": m["parallelism"],
+                          "l2": "activations 32 MB per image per layer at 256x256; weights 100 MB"},
+               "e2e": {"value": world * 1e3 / m["e2e_ms_per_image"], "unit": "images/s",
+                       "h2d_bytes_per_step": 256 * 4, "d2h_bytes_per_step": 256 * 256 * 3 * 4},
+               "gpu_launches": m["gpu_launches_per_decode"] * args.steps, "roofline": m["roofline"], "detail": m}
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                s_, sample = reference_vqgan_s()
+                out["cpu_baseline"] = {"value": 1.0 / s_, "unit": "images/s", "cores": 1, "kind": "reference",
+                                       "sample": sample}
+            except Exception as e:
+                out["cpu_baseline"] = {"unavailable": str(e)}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- config 2
 SWEEP_MS = (257, 1025, 4097)
 SWEEP_SHAPES = ((768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 2025))   # (K, N)
@@ -569,12 +716,14 @@ def main():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config-4 / config-5 keys of the c1 line")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "c5", "sweep"],
+    ap.add_argument("--workload", default="c1", choices=["c1", "c4", "c5", "sweep", "vqgan"],
                     help="c1: the headline config-1 step (default); c4: 64-image batched decode; "
-                         "c5: M=4097 tensor-parallel step; sweep: the 30 isolated qGEMM cases of config 2")
+                         "c5: M=4097 tensor-parallel step; sweep: the 30 isolated qGEMM cases of config 2; "
+                         "vqgan: the VQGAN decoder")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 20 if args.impl == "reference" else 10 if args.workload == "c5" else 3 if args.workload == "c4" else 300
+        args.steps = 20 if args.impl == "reference" else 10 if args.workload in ("c5", "vqgan") else \
+            3 if args.workload == "c4" else 300
     if args.impl == "reference":
         run_reference_arm(args)
     elif args.workload == "c5":
@@ -583,6 +732,8 @@ def main():
         run_decode_workload(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "vqgan":
+        run_vqgan_workload(args)
     else:
         run_cuda_arm(args)
 

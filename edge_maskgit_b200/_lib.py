@@ -53,6 +53,12 @@ _SIGS = {
     "mgc_profile_enable": (I, [P, I]),
     "mgc_profile_reset": (I, [P]),
     "mgc_profile_report": (I, [P, C.c_char_p, C.c_size_t]),
+    "mgc_vqgan_create": (I, [C.c_char_p, I, I, C.POINTER(P)]),
+    "mgc_vqgan_info": (I, [P, P, P, P]),
+    "mgc_vqgan_decode": (I, [P, P, I, P]),
+    "mgc_vqgan_decode_device": (I, [P, P, I, P, P]),
+    "mgc_vqgan_launches": (I, [P]),
+    "mgc_vqgan_destroy": (None, [P]),
 }
 
 for _name, (_res, _args) in _SIGS.items():

@@ -16,7 +16,7 @@ import numpy as np
 
 from ._lib import MgcError, check, lib
 
-__all__ = ["CudaRuntime", "QWeight", "MgcError", "pack_q8_0", "pack_q4_k", "dequant", "tp_unique_id",
+__all__ = ["CudaRuntime", "VqganDecoder", "QWeight", "MgcError", "pack_q8_0", "pack_q4_k", "dequant", "tp_unique_id",
            "quantize_act", "gemm_f32", "layernorm_affine", "flash_attn", "embed", "device_error",
            "F32", "Q8_0", "Q4_K"]
 
@@ -292,6 +292,51 @@ class CudaRuntime:
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib.mgc_runtime_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class VqganDecoder:
+    """The VQGAN decoder (build_vqgan_decoder, include/mg-vqgan.hpp:12) on one B200.
+
+    ``decode(grid)`` is the reference's VqganFwd callback (include/mg-generate.hpp:17): a token
+    grid [n_tokens] (or a batch [n][n_tokens]) -> HWC float image [R][R][3] (or [n][R][R][3])."""
+
+    def __init__(self, gguf_path: str, max_images: int = 1, device: int = 0):
+        h = C.c_void_p()
+        check(lib.mgc_vqgan_create(str(gguf_path).encode(), max_images, device, C.byref(h)), "vqgan_create")
+        self._h = h
+        info = [C.c_int(), C.c_int(), C.c_int()]
+        check(lib.mgc_vqgan_info(h, *[C.byref(v) for v in info]))
+        self.n_tokens, self.resolution, self.codebook_size = (v.value for v in info)
+        self.max_images = max_images
+
+    def decode(self, grid, out: np.ndarray | None = None) -> np.ndarray:
+        g = np.ascontiguousarray(grid, np.int32)
+        single = g.ndim == 1
+        g = g.reshape(-1, self.n_tokens)
+        R = self.resolution
+        if out is None:
+            out = np.empty((g.shape[0], R, R, 3), np.float32)
+        check(lib.mgc_vqgan_decode(self._h, _ptr(g), g.shape[0], _ptr(out)), "vqgan_decode")
+        return out[0] if single else out
+
+    def decode_device(self, grid_dev, out_dev, n_images: int) -> None:
+        """Device tensors (int32 [n][n_tokens], float32 [n][R][R][3]) on the current torch stream."""
+        check(lib.mgc_vqgan_decode_device(self._h, _ptr(grid_dev), n_images, _ptr(out_dev), _stream()),
+              "vqgan_decode_device")
+
+    def launches(self) -> int:
+        return lib.mgc_vqgan_launches(self._h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib.mgc_vqgan_destroy(self._h)
             self._h = None
 
     def __del__(self):

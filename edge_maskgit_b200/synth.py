@@ -8,6 +8,12 @@ ffn_up/down, output_proj) are packed Q8_0 ("gq8") or Q4_K ("gq4") by the library
 or kept F32 ("f32"); token_embd / pos_embd / LayerNorm / biases stay F32, as the reference
 converter does (convert_to_gguf.py:213-246).
 
+With ``vqgan=VqganSpec(...)`` the file also carries a VQGAN decoder (the ``vqgan.*`` tensors of
+export_weights.py and the ``maskgit.vqgan.*`` keys of convert_to_gguf.py:203-208), every conv
+weight F32 as the converter keeps them (convert_to_gguf.py:217-247): conv weights
+``N(0,1)/sqrt(fan_in)``, conv biases ``0.02*N(0,1)``, GroupNorm weight ``1 + 0.1*N(0,1)`` and bias
+``0.1*N(0,1)``, codebook ``N(0,1)``, drawn from the same stream after the transformer tensors.
+
 ``dequant_twin`` writes the same model with every packed weight dequantised back to F32 --
 the input the reference's scalar CPU executor needs (it reads weights as float only).
 
@@ -29,6 +35,16 @@ _LINEAR = ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_o.weight",
 
 
 @dataclass
+class VqganSpec:
+    """The decoder of maskgit/nets/vqgan_tokenizer.py as mg-vqgan.cpp builds it."""
+    embedding_dim: int = 256
+    filters: int = 128
+    num_res_blocks: int = 2
+    channel_multipliers: tuple = (1, 1, 2, 2, 4)
+    group_norm_groups: int = 32
+
+
+@dataclass
 class ModelSpec:
     n_layer: int = 24
     n_embd: int = 768
@@ -39,6 +55,20 @@ class ModelSpec:
     codebook: int = 1024
     quant: str = "gq8"        # gq8 | gq4 | f32
     seed: int = 42
+    vqgan: VqganSpec | None = None
+
+    @property
+    def latent(self) -> int:
+        L = 1
+        while L * L < self.n_tokens:
+            L += 1
+        return L
+
+    @property
+    def resolution(self) -> int:
+        if self.vqgan is None:
+            return 256
+        return self.latent * 2 ** (len(self.vqgan.channel_multipliers) - 1)
 
     @property
     def head_dim(self) -> int:
@@ -62,6 +92,61 @@ def tensor_list(s: ModelSpec):
     out += [("output_proj.weight", (E, E)), ("output_proj.bias", (E,)),
             ("output_norm.weight", (E,)), ("output_norm.bias", (E,)), ("output.bias", (V,))]
     return out
+
+
+def vqgan_tensor_list(s: ModelSpec):
+    """(name, numpy shape, kind) of the decoder, in the order mg-vqgan.cpp:67-108 uses them.
+    kind: conv | bias | gn_w | gn_b | codebook."""
+    v = s.vqgan
+    out = [("vqgan.quantizer.codebook.weight", (s.codebook, v.embedding_dim), "codebook")]
+    d = "vqgan.decoder."
+    mult, nrb = list(v.channel_multipliers), v.num_res_blocks
+
+    def conv(name, oc, ic, k, bias):
+        out.append((name + ".weight", (oc, ic, k, k), "conv"))
+        if bias:
+            out.append((name + ".bias", (oc,), "bias"))
+
+    def gn(name, c):
+        out.extend([(name + ".weight", (c,), "gn_w"), (name + ".bias", (c,), "gn_b")])
+
+    def resblock(pfx, cin, cout):
+        gn(pfx + "norm0", cin)
+        conv(pfx + "conv0", cout, cin, 3, False)
+        gn(pfx + "norm1", cout)
+        conv(pfx + "conv1", cout, cout, 3, False)
+        if cin != cout:
+            conv(pfx + "conv_res", cout, cout, 1, False)   # applied to the processed h
+
+    curr = v.filters * mult[-1]
+    conv(d + "conv_in", curr, v.embedding_dim, 3, True)
+    for l in range(nrb):
+        resblock(f"{d}res_blocks.0.{l}.", curr, curr)
+    prev = curr
+    for bi, i in enumerate(range(len(mult) - 1, -1, -1), start=1):
+        curr = v.filters * mult[i]
+        for l in range(nrb):
+            resblock(f"{d}res_blocks.{bi}.{l}.", prev, curr)
+            prev = curr
+        if i > 0:
+            conv(f"{d}res_blocks.{bi}.{nrb + 1}", curr, curr, 3, True)
+    gn(d + "norm_out", curr)
+    conv(d + "conv_out", 3, curr, 3, True)
+    return out
+
+
+def _vqgan_values(rng, shape, kind):
+    z = rng.standard_normal(shape, dtype=np.float32)
+    if kind == "conv":
+        fan_in = int(np.prod(shape[1:]))
+        return (z / np.float32(np.sqrt(fan_in))).astype(np.float32)
+    if kind == "bias":
+        return (z * np.float32(0.02)).astype(np.float32)
+    if kind == "gn_w":
+        return (np.float32(1.0) + z * np.float32(0.1)).astype(np.float32)
+    if kind == "gn_b":
+        return (z * np.float32(0.1)).astype(np.float32)
+    return z
 
 
 def _is_linear(name: str) -> bool:
@@ -91,14 +176,20 @@ def _metadata(s: ModelSpec, quant_label: str) -> tuple[bytes, int]:
         nonlocal n
         kv.s(key)
         kv.u32(typ)
-        {4: kv.u32, 5: kv.i32, 6: kv.f32, 8: kv.s}[typ](val)
+        if typ == 9:   # array of i32
+            kv.u32(5)
+            kv.u64(len(val))
+            for x in val:
+                kv.i32(int(x))
+        else:
+            {4: kv.u32, 5: kv.i32, 6: kv.f32, 8: kv.s}[typ](val)
         n += 1
 
     put("general.architecture", 8, "maskgit")
     put("general.name", 8, f"synthetic maskgit (seed {s.seed})")
     put("general.alignment", 4, ALIGN)
     put("general.file_type", 4, 0)
-    put("maskgit.resolution", 4, 256)
+    put("maskgit.resolution", 4, s.resolution)
     put("maskgit.n_layer", 4, s.n_layer)
     put("maskgit.n_head", 4, s.n_head)
     put("maskgit.n_embd", 4, s.n_embd)
@@ -110,6 +201,13 @@ def _metadata(s: ModelSpec, quant_label: str) -> tuple[bytes, int]:
     put("maskgit.mask_token_id", 5, s.vocab_size - 1)
     put("maskgit.layernorm_eps", 6, 1e-12)
     put("maskgit.vqgan.codebook_size", 4, s.codebook)
+    if s.vqgan is not None:
+        v = s.vqgan
+        put("maskgit.vqgan.embedding_dim", 4, v.embedding_dim)
+        put("maskgit.vqgan.filters", 4, v.filters)
+        put("maskgit.vqgan.num_res_blocks", 4, v.num_res_blocks)
+        put("maskgit.vqgan.group_norm_groups", 4, v.group_norm_groups)
+        put("maskgit.vqgan.channel_multipliers", 9, list(v.channel_multipliers))
     put("maskgit.sampling.choice_temperature", 6, 4.5)
     put("maskgit.quant", 8, quant_label)
     return bytes(kv.b), n
@@ -147,10 +245,10 @@ def _write(path: Path, s: ModelSpec, quant_label: str, tensors) -> None:
 def make_model(path, spec: ModelSpec | None = None, dequant_twin=None, packers=None) -> Path:
     """Write a synthetic GGUF (and optionally its dequantised F32 twin).  `packers`: an object
     with pack_q8_0(w), pack_q4_k(w) and dequant(wtype, blocks, N, K) (default: the library's)."""
-    if packers is None:
+    s = spec or ModelSpec()
+    if packers is None and s.quant != "f32":
         from . import runtime as packers
     Q8_0, Q4_K = 8, 12
-    s = spec or ModelSpec()
     rng = np.random.default_rng(s.seed)
     packed, twin = [], []
     for name, shape in tensor_list(s):
@@ -169,11 +267,25 @@ def make_model(path, spec: ModelSpec | None = None, dequant_twin=None, packers=N
             packed.append((name, ne, 0, a.tobytes()))
             if dequant_twin is not None:
                 twin.append((name, ne, 0, a.tobytes()))
+    if s.vqgan is not None:
+        for name, shape, kind in vqgan_tensor_list(s):
+            a = _vqgan_values(rng, shape, kind)
+            ent = (name, list(reversed(shape)), 0, a.tobytes())
+            packed.append(ent)
+            if dequant_twin is not None:
+                twin.append(ent)
     path = Path(path)
     _write(path, s, s.quant, packed)
     if dequant_twin is not None:
         _write(Path(dequant_twin), s, "f32", twin)
     return path
+
+
+def vqgan_spec(vq: VqganSpec | None = None, n_tokens: int = 256, seed: int = 42) -> ModelSpec:
+    """A model whose VQGAN decoder is `vq` (default: the MaskGIT decoder, 256 x 256 output) next
+    to a one-layer F32 transformer (the decoder tests do not need the transformer)."""
+    return ModelSpec(n_layer=1, n_embd=64, n_head=2, n_ffn=128, n_tokens=n_tokens, quant="f32", seed=seed,
+                     vqgan=vq or VqganSpec())
 
 
 def config1_tokens(spec: ModelSpec | None = None, class_id: int = 207) -> np.ndarray:

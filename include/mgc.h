@@ -172,6 +172,29 @@ int mgc_profile_reset(mgc_runtime* rt);
 /* Writes "name count ms\n" lines (descending by ms) into buf (NUL-terminated). */
 int mgc_profile_report(mgc_runtime* rt, char* buf, size_t buflen);
 
+/* ---------------------------------------------------------------- VQGAN decoder
+ * The CUDA counterpart of build_vqgan_decoder + compute (include/mg-vqgan.hpp:12,
+ * src/mg-vqgan.cpp:67-108) behind the reference's VqganFwd callback
+ * (include/mg-generate.hpp:17: grid [n_tokens] -> HWC float [R][R][3]).  The GGUF must carry
+ * the vqgan.* tensors (F32) and the maskgit.vqgan.* keys (tools/convert_to_gguf.py:203-208).
+ * Activations are NHWC f32 on the device; the whole decode is one CUDA graph per image count. */
+typedef struct mgc_vqgan mgc_vqgan;
+/* Loads the decoder onto `device` with buffers for up to max_images grids per call. */
+int mgc_vqgan_create(const char* gguf_path, int max_images, int device, mgc_vqgan** out);
+/* n_tokens of one grid, output resolution R, codebook size (any pointer may be null). */
+int mgc_vqgan_info(const mgc_vqgan* v, int* n_tokens, int* resolution, int* codebook_size);
+/* Host grid [n_images][n_tokens] (ids in [0, codebook_size), else -1 and nothing runs) ->
+ * host image [n_images][R][R][3] f32, unclamped (mg-generate.cpp:141-144 clamps when it makes
+ * bytes).  Synchronous.  Grid cell p = y * sqrt(n_tokens) + x. */
+int mgc_vqgan_decode(mgc_vqgan* v, const int32_t* grid, int n_images, float* image_hwc);
+/* The same on device buffers, enqueued on `stream` (null = legacy default stream) without a
+ * sync; ids outside the codebook decode as a zero latent. */
+int mgc_vqgan_decode_device(mgc_vqgan* v, const int32_t* grid_dev, int n_images, float* image_dev,
+                            void* stream);
+/* Kernels the last decode launched (all this library's own). */
+int mgc_vqgan_launches(const mgc_vqgan* v);
+void mgc_vqgan_destroy(mgc_vqgan* v);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,5 +44,34 @@ private:
     mgc_runtime* rt_ = nullptr;
 };
 
+// The VQGAN decoder on one GPU (mgc_vqgan_*).
+class Vqgan {
+public:
+    Vqgan(const std::string& gguf_path, int max_images = 1, int device = 0) {
+        check(mgc_vqgan_create(gguf_path.c_str(), max_images, device, &v_), "vqgan_create");
+        check(mgc_vqgan_info(v_, &n_tokens_, &resolution_, nullptr), "vqgan_info");
+    }
+    ~Vqgan() { mgc_vqgan_destroy(v_); }
+    Vqgan(const Vqgan&) = delete;
+    Vqgan& operator=(const Vqgan&) = delete;
+
+    // grid [n][n_tokens] -> image [n][R][R][3] HWC f32, host memory, synchronous.
+    void decode(const int32_t* grid, float* image_hwc, int n = 1) {
+        check(mgc_vqgan_decode(v_, grid, n, image_hwc), "vqgan_decode");
+    }
+    // A callable with the shape of mg::VqganFwd (std::function<void(const int32_t*, float*)>,
+    // include/mg-generate.hpp:17); the Vqgan must outlive it.
+    std::function<void(const int32_t*, float*)> vqgan_fwd() {
+        return [this](const int32_t* grid, float* hwc) { decode(grid, hwc, 1); };
+    }
+    int resolution() const { return resolution_; }
+    int n_tokens() const { return n_tokens_; }
+    mgc_vqgan* handle() { return v_; }
+
+private:
+    mgc_vqgan* v_ = nullptr;
+    int n_tokens_ = 0, resolution_ = 0;
+};
+
 }  // namespace mgc
 #endif

@@ -5,7 +5,10 @@
 // tests run it and compare its grid with mgc_generate's.  It shows that the C ABI (through
 // include/mgc.hpp) links into, and drives, the reference program unchanged.
 //
-//   mg_generate_cuda MODEL.gguf CLASS SEED STEPS OUT.bin   -> OUT.bin = the n_tokens grid (int32)
+//   mg_generate_cuda MODEL.gguf CLASS SEED STEPS OUT.bin [IMAGE.bin]
+//     OUT.bin   = the n_tokens grid (int32)
+//     IMAGE.bin = the decoded image, HWC f32 [R][R][3], from the CUDA VQGAN decoder as the
+//                 VqganFwd callback (given only for a GGUF that carries the decoder)
 #include "mg-generate.hpp"
 #include "mg-model.hpp"
 #include "mg-tensor.hpp"
@@ -19,8 +22,8 @@
 #include <vector>
 
 int main(int argc, char** argv) {
-    if (argc != 6) {
-        std::fprintf(stderr, "usage: %s MODEL.gguf CLASS SEED STEPS OUT.bin\n", argv[0]);
+    if (argc != 6 && argc != 7) {
+        std::fprintf(stderr, "usage: %s MODEL.gguf CLASS SEED STEPS OUT.bin [IMAGE.bin]\n", argv[0]);
         return 2;
     }
     try {
@@ -32,7 +35,18 @@ int main(int argc, char** argv) {
         mgc::Runtime rt(argv[1], S, 0);
         mg::TransformerFwd fwd = rt.transformer_fwd(S);
         std::vector<int32_t> grid(n_tok);
-        mg::VqganFwd vfwd = [&](const int32_t* g, float*) { std::memcpy(grid.data(), g, sizeof(int32_t) * n_tok); };
+        // and, with IMAGE.bin, the VQGAN decoder's VqganFwd
+        std::unique_ptr<mgc::Vqgan> vq;
+        if (argc == 7) vq.reset(new mgc::Vqgan(argv[1], 1, 0));
+        std::vector<float> image;
+        mg::VqganFwd vq_fwd = vq ? vq->vqgan_fwd() : mg::VqganFwd();
+        mg::VqganFwd vfwd = [&](const int32_t* g, float* hwc) {
+            std::memcpy(grid.data(), g, sizeof(int32_t) * n_tok);
+            if (vq_fwd) {
+                vq_fwd(g, hwc);
+                image.assign(hwc, hwc + (size_t)vq->resolution() * vq->resolution() * 3);
+            }
+        };
         mg::GenConfig cfg;
         cfg.class_id = std::atoi(argv[2]);
         cfg.seed = std::strtoull(argv[3], nullptr, 10);
@@ -45,6 +59,14 @@ int main(int argc, char** argv) {
             return 1;
         }
         std::fclose(f);
+        if (vq) {
+            FILE* fi = std::fopen(argv[6], "wb");
+            if (!fi || std::fwrite(image.data(), sizeof(float), image.size(), fi) != image.size()) {
+                std::fprintf(stderr, "cannot write %s\n", argv[6]);
+                return 1;
+            }
+            std::fclose(fi);
+        }
         std::printf("transformer_ms %.3f steps %d\n", stats.transformer_ms, stats.steps);
         return 0;
     } catch (const std::exception& e) {

@@ -73,6 +73,8 @@ def mgref():
         L.mgref_forward.argtypes = [C.c_char_p, P, I, I, P, P, I]
         L.mgref_generate.restype = I
         L.mgref_generate.argtypes = [C.c_char_p, FWD_FN, P, I, C.c_ulonglong, I, F, P]
+        L.mgref_vqgan.restype = I
+        L.mgref_vqgan.argtypes = [C.c_char_p, P, P]
         _ref = L
     return _ref
 
@@ -263,3 +265,139 @@ def ref_generate(gguf, fwd, vocab, n_tokens, class_id=207, seed=42, steps=8, tem
     if mgref().mgref_generate(str(gguf).encode(), cb, None, class_id, seed, steps, temperature, _p(grid)) != 0:
         raise RuntimeError(mgref().mgref_last_error().decode())
     return grid
+
+
+def ref_vqgan(gguf, grid, resolution):
+    """The reference's own VQGAN decoder (src/mg-vqgan.cpp on mg-cpu) -> [R][R][3] HWC float."""
+    grid = np.ascontiguousarray(grid, np.int32)
+    out = np.empty((resolution, resolution, 3), np.float32)
+    if mgref().mgref_vqgan(str(gguf).encode(), _p(grid), _p(out)) != 0:
+        raise RuntimeError(mgref().mgref_last_error().decode())
+    return out
+
+
+# ------------------------------------------------------------------ VQGAN decoder (numpy)
+def read_gguf(path):
+    """Minimal GGUF v3 reader (the format of mg-model.cpp:139-201): scalar / string / array
+    metadata and F32 tensors as numpy arrays (numpy shape = reversed ne)."""
+    import struct
+    b = Path(path).read_bytes()
+    p = 0
+
+    def take(fmt):
+        nonlocal p
+        v = struct.unpack_from("<" + fmt, b, p)
+        p += struct.calcsize("<" + fmt)
+        return v[0]
+
+    def string():
+        nonlocal p
+        n = take("Q")
+        s = b[p:p + n].decode()
+        p += n
+        return s
+
+    scal = {0: "B", 1: "b", 2: "H", 3: "h", 4: "I", 5: "i", 6: "f", 7: "?", 10: "Q", 11: "q", 12: "d"}
+
+    def value(t):
+        if t == 8:
+            return string()
+        if t == 9:
+            sub, n = take("I"), take("Q")
+            return [value(sub) for _ in range(n)]
+        return take(scal[t])
+
+    assert take("I") == 0x46554747 and take("I") == 3
+    nt, nkv = take("Q"), take("Q")
+    kv = {}
+    for _ in range(nkv):
+        k = string()
+        kv[k] = value(take("I"))
+    infos = []
+    for _ in range(nt):
+        name = string()
+        ne = [take("Q") for _ in range(take("I"))]
+        infos.append((name, ne, take("I"), take("Q")))
+    align = kv.get("general.alignment", 32)
+    data0 = (p + align - 1) // align * align
+    tensors = {}
+    for name, ne, typ, off in infos:
+        if typ == 0:
+            n = int(np.prod(ne))
+            tensors[name] = np.frombuffer(b, np.float32, n, data0 + off).reshape(tuple(reversed(ne)))
+    return kv, tensors
+
+
+def _gn_affine_silu(x, w, b, groups=32, eps=1e-5):
+    """x [C][H][W]; mg-cpu.cpp:124-147 (group stats in double, two passes) + :265-276."""
+    C = x.shape[0]
+    cpg = C // groups
+    out = np.empty_like(x)
+    for g in range(groups):
+        xs = x[g * cpg:(g + 1) * cpg].astype(np.float64)
+        mean = xs.mean()
+        var = ((xs - mean) ** 2).mean()
+        inv = np.float32(1.0) / np.sqrt(np.float32(var) + np.float32(eps))
+        out[g * cpg:(g + 1) * cpg] = (xs - mean).astype(np.float32) * inv
+    xn = out * w[:, None, None] + b[:, None, None]
+    return (xn / (np.float32(1.0) + np.exp(-xn))).astype(np.float32)
+
+
+def _conv(x, w, bias=None):
+    """x [IC][H][W], w [OC][IC][k][k], stride 1, pad k//2 (mg-cpu.cpp:166-187) via im2col."""
+    IC, H, W = x.shape
+    OC, _, k, _ = w.shape
+    pd = k // 2
+    xp = np.pad(x, ((0, 0), (pd, pd), (pd, pd)))
+    cols = np.empty((IC, k, k, H, W), np.float32)
+    for kh in range(k):
+        for kw in range(k):
+            cols[:, kh, kw] = xp[:, kh:kh + H, kw:kw + W]
+    y = (w.reshape(OC, -1) @ cols.reshape(IC * k * k, H * W)).reshape(OC, H, W)
+    if bias is not None:
+        y = y + bias[:, None, None]
+    return y.astype(np.float32)
+
+
+def vqgan_decode(gguf, grid):
+    """CPU restatement of build_vqgan_decoder (src/mg-vqgan.cpp:67-108) -> [R][R][3] HWC."""
+    kv, t = read_gguf(gguf)
+    filters = kv["maskgit.vqgan.filters"]
+    mult = kv["maskgit.vqgan.channel_multipliers"]
+    nrb = kv["maskgit.vqgan.num_res_blocks"]
+    n_tok = kv["maskgit.n_tokens"]
+    L = 1
+    while L * L < n_tok:
+        L += 1
+    d = "vqgan.decoder."
+    cb = t["vqgan.quantizer.codebook.weight"]
+    x = cb[np.asarray(grid)].reshape(L, L, -1).transpose(2, 0, 1)     # [C][H][W], token y*L+x
+
+    def gas(name, h):
+        return _gn_affine_silu(h, t[name + ".weight"], t[name + ".bias"])
+
+    def resblock(pfx, h, cin, cout):
+        res = h
+        h = _conv(gas(pfx + "norm0", h), t[pfx + "conv0.weight"])
+        h = _conv(gas(pfx + "norm1", h), t[pfx + "conv1.weight"])
+        if cin != cout:
+            res = _conv(h, t[pfx + "conv_res.weight"])                # applied to the processed h
+        return h + res
+
+    curr = filters * mult[-1]
+    x = _conv(x, t[d + "conv_in.weight"], t[d + "conv_in.bias"])
+    for l in range(nrb):
+        x = resblock(f"{d}res_blocks.0.{l}.", x, curr, curr)
+    prev = curr
+    for bi, i in enumerate(range(len(mult) - 1, -1, -1), start=1):
+        curr = filters * mult[i]
+        for l in range(nrb):
+            x = resblock(f"{d}res_blocks.{bi}.{l}.", x, prev, curr)
+            prev = curr
+        if i > 0:
+            x = x.repeat(2, axis=1).repeat(2, axis=2)                 # nearest, mg-cpu.cpp:190-196
+            up = f"{d}res_blocks.{bi}.{nrb + 1}"
+            x = _conv(x, t[up + ".weight"], t[up + ".bias"])
+    x = gas(d + "norm_out", x)
+    x = _conv(x, t[d + "conv_out.weight"], t[d + "conv_out.bias"])
+    return np.ascontiguousarray(x.transpose(1, 2, 0))

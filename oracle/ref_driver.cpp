@@ -8,12 +8,16 @@
 //                  Its weights must be F32 (mg-cpu cannot read Q8_0/Q4_K), so callers
 //                  pass the dequantised twin GGUF.  Named tensors are dumped like
 //                  tools/verify-opencl-transformer.cpp:67-85.
+//  mgref_vqgan   : Model::load + build_vqgan_decoder (src/mg-vqgan.cpp) + mg::compute on one
+//                  token grid; the {W,H,3} image is returned HWC, the order of the VqganFwd
+//                  callback (src/mg-generate.cpp:137-140, tools/main.cpp:147-151).
 //  mgref_generate: mg::generate (src/mg-generate.cpp) with a caller-supplied transformer
 //                  callback and a VQGAN callback that only captures the token grid.
 #include "mg-generate.hpp"
 #include "mg-model.hpp"
 #include "mg-tensor.hpp"
 #include "mg-transformer.hpp"
+#include "mg-vqgan.hpp"
 
 #include <cstring>
 #include <exception>
@@ -55,6 +59,26 @@ int mgref_forward(const char* gguf, const int32_t* tokens, int B, int S, float* 
                         break;
                     }
         }
+        return 0;
+    } catch (const std::exception& e) { g_ref_err = e.what(); return -1; }
+}
+
+int mgref_vqgan(const char* gguf, const int32_t* grid, float* hwc) {
+    try {
+        mg::Context wctx(64 << 20);
+        auto model = mg::Model::load(gguf, wctx);
+        const int n_tok = model->hparams().n_tokens;
+        mg::Context vctx(3ull << 30);
+        mg::Tensor* gt = vctx.tensor1d(mg::Type::I32, n_tok);
+        std::memcpy(gt->data, grid, sizeof(int32_t) * n_tok);
+        mg::Tensor* img = mg::build_vqgan_decoder(vctx, *model, gt);
+        mg::Graph g; g.build_forward(img);
+        mg::compute(vctx, g, 1);
+        const int64_t W = img->ne[0], H = img->ne[1];
+        const float* o = static_cast<const float*>(img->data);
+        for (int64_t y = 0; y < H; y++)
+            for (int64_t x = 0; x < W; x++)
+                for (int c = 0; c < 3; c++) hwc[(y * W + x) * 3 + c] = o[x + W * (y + H * c)];
         return 0;
     } catch (const std::exception& e) { g_ref_err = e.what(); return -1; }
 }
