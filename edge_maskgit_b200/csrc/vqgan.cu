@@ -1,54 +1,96 @@
 // vqgan.cu -- the MaskGIT VQGAN decoder on the GPU: the graph of src/mg-vqgan.cpp:67-108
 // (codebook lookup, conv_in, ResBlocks with the shortcut conv applied to the processed tensor,
 // nearest 2x upsampling + conv, GroupNorm(32) + affine + SiLU, conv_out) run as a fixed program of
-// kernels over one or more token grids.
+// kernels over one or more token grids, captured once per image count as a CUDA graph.
 //
-// Layout.  Activations are NHWC f32, [image][y][x][channel]: a pixel's channels are one
-// contiguous run, so the codebook lookup is a row copy, a 3x3 conv is an implicit GEMM whose
-// K dimension (tap, channel) reads contiguous channel runs of shifted pixels, and the last conv
-// (3 output channels) writes the HWC image of the VqganFwd callback (include/mg-generate.hpp:17)
-// directly.  Conv weights are re-laid on load from GGUF [OC][IC][KH][KW] to [tap][IC][OC].
+// Layout.  Activations are NHWC, [image][y][x][channel]: a pixel's channels are one contiguous
+// run, so the codebook lookup is a row copy, a 3x3 conv is an implicit GEMM whose K dimension
+// (tap, channel) reads contiguous channel runs of shifted pixels, and the last conv (3 output
+// channels) writes the HWC image of the VqganFwd callback (include/mg-generate.hpp:17)
+// directly.  Every conv writes f32; every conv READS a pair of bf16 tensors (hi, lo) with
+// hi = bf16(v), lo = bf16(v - hi), so hi + lo carries v to ~2^-17 relative.  GroupNorm writes
+// that pair directly; a split kernel makes it (with the nearest 2x upsample folded in) for the
+// up-convs and the shortcut conv.
+//
+// Convs.  The tensor-core conv (conv_tc_kernel) computes out = sum over (tap, channel) of
+// x * w as three bf16 MMAs per K step -- hi*hi + hi*lo + lo*hi -- into an f32 TMEM accumulator
+// (tcgen05.mma kind::f16, M = 128 pixels, N = 128 / 256 output channels); the dropped lo*lo
+// term and the two roundings leave ~2^-16 relative per product, far inside the decoder gate.
+// Its A operand (128 pixels x 64 channels of one tap) is one 4-D TMA load from the (hi or lo)
+// activation tensor at the tap's shifted pixel origin: the zero padding of the conv is the
+// TMA's out-of-bounds fill.  B (weights) is pre-tiled on load so a (k-block, n-tile) is one
+// contiguous 128-byte-swizzled run moved by one bulk copy.  Shapes it does not tile (channel
+// counts not multiples of 64 / 128, images narrower than 16 pixels) run on a SIMT f32
+// implicit GEMM; MGC_VQGAN_SIMT=1 at create time forces that path for every conv.
 //
 // Numerics follow mg-cpu (src/mg-cpu/mg-cpu.cpp): GroupNorm statistics in double
 // (:124-147, variance as E[x^2] - mean^2 over per-chunk double sums), normalisation
 // (float)(x - mean) * inv, then xn = o * gamma + beta and xn / (1 + exp(-xn)) (:265-276) with
-// separately rounded multiply and add; convs accumulate in f32 (tap-major instead of
-// (ic, kh, kw), the only reordering).
+// separately rounded multiply and add; convs accumulate in f32 in another order.
 #include "../../include/mgc.h"
 #include "gguf.h"
 #include "kernels.h"
+#include "ptx.cuh"
 #include "qgemm_common.cuh"
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
 namespace mgc {
 namespace {
 
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float2 bf2_to_f2(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+}
+// 4 consecutive channels of (hi, lo) -> f32
+__device__ __forceinline__ float4 load_pair4(const bf16* hi, const bf16* lo, size_t off) {
+    const uint2 h = __ldg(reinterpret_cast<const uint2*>(hi + off));
+    const uint2 l = __ldg(reinterpret_cast<const uint2*>(lo + off));
+    const float2 h0 = bf2_to_f2(h.x), h1 = bf2_to_f2(h.y), l0 = bf2_to_f2(l.x), l1 = bf2_to_f2(l.y);
+    return make_float4(h0.x + l0.x, h0.y + l0.y, h1.x + l1.x, h1.y + l1.y);
+}
+__device__ __forceinline__ void split_store4(bf16* hi, bf16* lo, size_t off, const float (&v)[4]) {
+    __align__(8) bf16 h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        h[j] = __float2bfloat16_rn(v[j]);
+        l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+    }
+    *reinterpret_cast<uint2*>(hi + off) = *reinterpret_cast<const uint2*>(h);
+    *reinterpret_cast<uint2*>(lo + off) = *reinterpret_cast<const uint2*>(l);
+}
+
 // ------------------------------------------------------------------------------------------
-// Implicit-GEMM 3x3 / 1x1 conv, SIMT f32.  Rows = output pixels (M = images * H * W), columns =
-// output channels, K = taps * IC (IC a multiple of 8, OC of 4).  CTA tile 128 x 128 x 8, 256 threads, 8 x 8 outputs a thread,
-// register-prefetched double buffer.  With UP the input is the half-resolution tensor and the
-// nearest 2x upsample (mg-cpu.cpp:190-196) is folded into the pixel address.
+// SIMT implicit-GEMM conv (f32 FMA).  Rows = output pixels (M = images * H * W), columns =
+// output channels, K = taps * IC (IC a multiple of 8, OC of 4).  CTA tile 128 x 128 x 8, 256
+// threads, 8 x 8 outputs a thread, register-prefetched double buffer.
 struct ConvArgs {
-    const float* x;       // [N][Hin][Win][IC]
-    const float* w;       // [T][IC][OC]
+    const bf16* xh;       // [N][H][W][IC] hi
+    const bf16* xl;       //               lo
+    const float* w;       // [T][IC][OC] f32
     const float* bias;    // [OC] or null
     const float* resid;   // [M][OC] or null (added after the conv)
     float* y;             // [M][OC]
     float* part;          // [nsplit][M][OC] when nsplit > 1
-    int H, W, IC, OC, ks, up, M;
+    int H, W, IC, OC, ks, M;
     int kper;             // K iterations (8 channels of one tap) per split
     int kiters;
 };
 
 constexpr int CBM = 128, CBN = 128, CBK = 8, CPAD = 4;
 
-template <bool UP>
 __global__ void __launch_bounds__(256, 2) conv_simt_kernel(ConvArgs a) {
     __shared__ __align__(16) float As[2][CBK][CBM + CPAD];
     __shared__ __align__(16) float Bs[2][CBK][CBN];
@@ -56,13 +98,11 @@ __global__ void __launch_bounds__(256, 2) conv_simt_kernel(ConvArgs a) {
     const int m0 = blockIdx.x * CBM, n0 = blockIdx.y * CBN;
     const int it0 = blockIdx.z * a.kper, it1 = min(a.kiters, it0 + a.kper);
     const int icg = a.IC / CBK;
-    // this thread's A row (pixel) and channel quad
-    const int pr = tid >> 1, cq = (tid & 1) * 4;
+    const int pr = tid >> 1, cq = (tid & 1) * 4;   // this thread's A row (pixel) and channel quad
     const int m = m0 + pr;
     const int HW = a.H * a.W;
     const int img = m / HW, rem = m - img * HW, py = rem / a.W, px = rem - py * a.W;
-    const int Hin = UP ? a.H >> 1 : a.H, Win = UP ? a.W >> 1 : a.W;
-    const float* xbase = a.x + (size_t)img * Hin * Win * a.IC + cq;
+    const size_t xbase = (size_t)img * HW * a.IC + cq;
     const int br = tid >> 5, bc = (tid & 31) * 4;
     const int half = a.ks >> 1;
 
@@ -70,8 +110,7 @@ __global__ void __launch_bounds__(256, 2) conv_simt_kernel(ConvArgs a) {
         const int tap = it / icg, c0 = (it - tap * icg) * CBK;
         const int yy = py + tap / a.ks - half, xx = px + tap % a.ks - half;
         if (m >= a.M || yy < 0 || yy >= a.H || xx < 0 || xx >= a.W) return make_float4(0.f, 0.f, 0.f, 0.f);
-        const int sy = UP ? yy >> 1 : yy, sx = UP ? xx >> 1 : xx;
-        return __ldg(reinterpret_cast<const float4*>(xbase + ((size_t)sy * Win + sx) * a.IC + c0));
+        return load_pair4(a.xh, a.xl, xbase + ((size_t)yy * a.W + xx) * a.IC + c0);
     };
     auto load_b = [&](int it) -> float4 {
         const int tap = it / icg, c0 = (it - tap * icg) * CBK;
@@ -171,9 +210,10 @@ __global__ void conv_splitk_reduce_kernel(const float* __restrict__ part, int ns
 // Conv with few output channels (conv_out, OC = 3): one thread a pixel, weights in shared
 // memory as [tap][IC][4].
 constexpr int kSmallOC = 4;
-__global__ void __launch_bounds__(128) conv_small_oc_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                            const float* __restrict__ bias, float* __restrict__ y,
-                                                            int M, int H, int W, int IC, int OC, int ks) {
+__global__ void __launch_bounds__(128) conv_small_oc_kernel(const bf16* __restrict__ xh, const bf16* __restrict__ xl,
+                                                            const float* __restrict__ w, const float* __restrict__ bias,
+                                                            float* __restrict__ y, int M, int H, int W, int IC, int OC,
+                                                            int ks) {
     extern __shared__ float ws[];   // [T][IC][4]
     const int T = ks * ks;
     for (int i = threadIdx.x; i < T * IC * kSmallOC; i += blockDim.x) {
@@ -189,10 +229,10 @@ __global__ void __launch_bounds__(128) conv_small_oc_kernel(const float* __restr
     for (int tap = 0; tap < T; tap++) {
         const int yy = py + tap / ks - half, xx = px + tap % ks - half;
         if (yy < 0 || yy >= H || xx < 0 || xx >= W) continue;
-        const float4* src = reinterpret_cast<const float4*>(x + ((size_t)(img * H + yy) * W + xx) * IC);
+        const size_t src = ((size_t)(img * H + yy) * W + xx) * IC;
         const float4* wt = reinterpret_cast<const float4*>(ws + (size_t)tap * IC * kSmallOC);
         for (int c4 = 0; c4 < IC / 4; c4++) {
-            const float4 v = __ldg(src + c4);
+            const float4 v = load_pair4(xh, xl, src + c4 * 4);
             const float xv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -206,9 +246,208 @@ __global__ void __launch_bounds__(128) conv_small_oc_kernel(const float* __restr
 }
 
 // ------------------------------------------------------------------------------------------
+// Tensor-core conv.  Persistent CTAs (one per SM, 192 KB of stages), warp roles:
+//   warp 0 lane 0  producer: per k-block (one tap, 64 input channels) two 4-D TMA loads (A hi,
+//                  A lo: 128 pixels x 128 B, 128-byte swizzle) and two bulk copies (B hi, B lo)
+//   warp 1 lane 0  MMA issuer: 4 K steps x 3 MMAs per k-block into a TMEM accumulator
+//   warps 2..5     epilogue: TMEM -> registers -> (+ bias, + residual) -> f32 out (or the
+//                  split-K partials); TMEM accumulators are double-buffered so a tile's
+//                  epilogue overlaps the next tile's MMAs.
+// Work unit = (m-tile, n-tile, K split), m-tile fastest so concurrent CTAs share weight tiles
+// in L2.  An m-tile is a BH x BW pixel rectangle of one image (BW = min(W, 128)); TMEM lane r
+// of the accumulator is pixel (y0 + r / BW, x0 + r % BW), the row order of the TMA box.
+constexpr int TC_BM = 128, TC_BK = 64;
+constexpr int TC_A_BYTES = TC_BM * 128;
+
+template <int BN>
+struct TcCfg {
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE = 2 * TC_A_BYTES + 2 * B_BYTES;
+    static constexpr int NST = BN == 256 ? 2 : 3;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = 1024 + NST * STAGE + BAR_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static_assert(SMEM <= 232448, "shared memory");
+    static_assert(TMEM_COLS <= 512, "tmem");
+    static_assert((2 * NST + 4) * 8 + 8 <= BAR_BYTES, "barrier area");
+};
+
+struct TcArgs {
+    const uint8_t* wh;    // pre-tiled B hi: [OC/BN][kblocks][BN rows x 128 B swizzled]
+    const uint8_t* wl;    // lo
+    const float* bias;
+    const float* resid;
+    float* y;
+    float* part;
+    int H, W, IC, OC, ks, M;
+    int BW, BH, tiles_x, tiles_per_img;
+    int m_tiles, n_tiles, kblocks, kper, nsplit, n_units;
+};
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+          "r"(smem_u32(bar)) : "memory");
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__ CUtensorMap map_hi,
+                                                          const __grid_constant__ CUtensorMap map_lo, TcArgs p) {
+    using C = TcCfg<BN>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = align1024_smem(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NST * C::STAGE);
+    uint64_t* empty = full + C::NST;
+    uint64_t* afull = empty + C::NST;    // [2]
+    uint64_t* aempty = afull + 2;        // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::NST; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int a = 0; a < 2; a++) { mbar_init(&afull[a], 1); mbar_init(&aempty[a], 128); }
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int icb = p.IC / TC_BK, half = p.ks >> 1;
+
+    auto unit_of = [&](int u, int& mt, int& nt, int& ks) {
+        mt = u % p.m_tiles;
+        const int r = u / p.m_tiles;
+        nt = r % p.n_tiles;
+        ks = r / p.n_tiles;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int gc = 0;
+            int last_it[C::NST];
+            for (int s = 0; s < C::NST; s++) last_it[s] = -1;
+            bool go = true;
+            for (int u = blockIdx.x; go && u < p.n_units; u += gridDim.x) {
+                int mt, nt, ks;
+                unit_of(u, mt, nt, ks);
+                const int img = mt / p.tiles_per_img, r = mt % p.tiles_per_img;
+                const int y0 = (r / p.tiles_x) * p.BH, x0 = (r % p.tiles_x) * p.BW;
+                const int kb0 = ks * p.kper, kb1 = min(p.kblocks, kb0 + p.kper);
+                for (int kb = kb0; kb < kb1; kb++, gc++) {
+                    const int s = gc % C::NST, it = gc / C::NST;
+                    if (!(go = mbar_wait(&empty[s], (it & 1) ^ 1, abort_flag, 21))) break;
+                    uint8_t* st = smem + s * C::STAGE;
+                    const int tap = kb / icb, c0 = (kb - tap * icb) * TC_BK;
+                    const int dy = tap / p.ks - half, dx = tap % p.ks - half;
+                    mbar_arrive_expect_tx(&full[s], C::STAGE);
+                    // x (innermost) = channel c0, a multiple of 64: 128-byte aligned
+                    tma_load_4d(st, &map_hi, c0, x0 + dx, y0 + dy, img, &full[s]);
+                    tma_load_4d(st + TC_A_BYTES, &map_lo, c0, x0 + dx, y0 + dy, img, &full[s]);
+                    const size_t boff = ((size_t)nt * p.kblocks + kb) * C::B_BYTES;
+                    bulk_g2s(st + 2 * TC_A_BYTES, p.wh + boff, C::B_BYTES, &full[s]);
+                    bulk_g2s(st + 2 * TC_A_BYTES + C::B_BYTES, p.wl + boff, C::B_BYTES, &full[s]);
+                    last_it[s] = it;
+                }
+            }
+            if (*abort_flag) {   // let copies already in flight land before the CTA exits
+                volatile int never = 0;
+                for (int s = 0; s < C::NST; s++)
+                    if (last_it[s] >= 0) mbar_wait(&full[s], last_it[s] & 1, &never, 29);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_make(1, 1, 1, TC_BM, BN);
+            int gc = 0, i = 0;
+            bool go = true;
+            for (int u = blockIdx.x; go && u < p.n_units; u += gridDim.x, i++) {
+                int mt, nt, ks;
+                unit_of(u, mt, nt, ks);
+                const int kb0 = ks * p.kper, kb1 = min(p.kblocks, kb0 + p.kper);
+                const int a = i & 1;
+                if (!(go = mbar_wait(&aempty[a], ((i >> 1) & 1) ^ 1, abort_flag, 22))) break;
+                tc_fence_after();
+                const uint32_t d = tmem + a * BN;
+                for (int kb = kb0; kb < kb1; kb++, gc++) {
+                    const int s = gc % C::NST, it = gc / C::NST;
+                    if (!(go = mbar_wait(&full[s], it & 1, abort_flag, 23))) break;
+                    tc_fence_after();
+                    const uint32_t ah = smem_u32(smem + s * C::STAGE), al = ah + TC_A_BYTES;
+                    const uint32_t bh = ah + 2 * TC_A_BYTES, bl = bh + C::B_BYTES;
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 16; k++) {
+                        const uint32_t acc = (kb == kb0 && k == 0) ? 0u : 1u;
+                        mma_f16(d, sdesc_sw128(ah + 32 * k), sdesc_sw128(bh + 32 * k), idesc, acc);
+                        mma_f16(d, sdesc_sw128(ah + 32 * k), sdesc_sw128(bl + 32 * k), idesc, 1);
+                        mma_f16(d, sdesc_sw128(al + 32 * k), sdesc_sw128(bh + 32 * k), idesc, 1);
+                    }
+                    mma_commit(&empty[s]);   // the stage may be refilled once these MMAs are done
+                }
+                if (go) mma_commit(&afull[a]);   // the accumulator is complete
+            }
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (one pixel a thread)
+        const int q = warp & 3, row = q * 32 + lane;
+        int i = 0;
+        for (int u = blockIdx.x; u < p.n_units; u += gridDim.x, i++) {
+            int mt, nt, ks;
+            unit_of(u, mt, nt, ks);
+            const int a = i & 1;
+            if (!mbar_wait(&afull[a], (i >> 1) & 1, abort_flag, 24)) break;
+            tc_fence_after();
+            const int img = mt / p.tiles_per_img, r = mt % p.tiles_per_img;
+            const int y = (r / p.tiles_x) * p.BH + row / p.BW, x = (r % p.tiles_x) * p.BW + row % p.BW;
+            const size_t m = ((size_t)img * p.H + y) * p.W + x;
+            const bool split = p.nsplit > 1;
+            float* dst = split ? p.part + (size_t)ks * p.M * p.OC : p.y;
+            const uint32_t t_row = tmem + a * BN + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; c++) {
+                uint32_t v[32];
+                tmem_ld32(t_row + c * 32, v);
+                tmem_ld_wait();
+                const int col = nt * BN + c * 32;
+                float* o = dst + m * p.OC + col;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float4 f = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                           __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                    if (!split) {
+                        if (p.bias) {
+                            const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + col + j));
+                            f.x += b.x; f.y += b.y; f.z += b.z; f.w += b.w;
+                        }
+                        if (p.resid) {
+                            const float4 rr = __ldg(reinterpret_cast<const float4*>(p.resid + m * p.OC + col + j));
+                            f.x += rr.x; f.y += rr.y; f.z += rr.z; f.w += rr.w;
+                        }
+                    }
+                    *reinterpret_cast<float4*>(o + j) = f;
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&aempty[a]);   // the MMA warp may reuse this accumulator
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // GroupNorm + affine + SiLU over NHWC.  Pass 1: per (image, pixel chunk) per-channel double
 // sums of x and x^2 (fixed-order reductions, so the result is deterministic).  Pass 2: per
-// (image, group) mean and 1/sqrt(var + eps).  Pass 3: the elementwise apply.
+// (image, group) mean and 1/sqrt(var + eps).  Pass 3: the elementwise apply, writing the
+// (hi, lo) pair the next conv reads.
 constexpr int kGnThreads = 256;
 
 __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const float* __restrict__ x, int HW, int C,
@@ -263,7 +502,7 @@ __global__ void gn_finalize_kernel(const double* __restrict__ part, int nch, int
 
 __global__ void gn_apply_silu_kernel(const float* __restrict__ x, const GnStat* __restrict__ st,
                                      const float* __restrict__ gamma, const float* __restrict__ beta, int HW, int C,
-                                     int G, size_t n4, float* __restrict__ y) {
+                                     int G, size_t n4, bf16* __restrict__ yh, bf16* __restrict__ yl) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const size_t e = i * 4;
@@ -281,13 +520,35 @@ __global__ void gn_apply_silu_kernel(const float* __restrict__ x, const GnStat* 
         const float xn = __fadd_rn(__fmul_rn(nrm, gamma[c]), beta[c]);
         o[j] = xn / (1.0f + expf(-xn));
     }
-    reinterpret_cast<float4*>(y)[i] = make_float4(o[0], o[1], o[2], o[3]);
+    split_store4(yh, yl, e, o);
+}
+
+// f32 NHWC -> (hi, lo) pair, optionally nearest-upsampled 2x (mg-cpu.cpp:190-196): output
+// pixel (y, x) reads input (y / 2, x / 2).  H, W: the input's size.
+__global__ void split_kernel(const float* __restrict__ x, int H, int W, int C, int up, size_t n4,
+                             bf16* __restrict__ yh, bf16* __restrict__ yl) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const int C4 = C / 4;
+    const int c = (int)(i % C4) * 4;
+    const size_t pix = i / C4;   // output pixel
+    size_t src = pix;
+    if (up) {
+        const int Wo = W * 2, Ho = H * 2;
+        const size_t img = pix / ((size_t)Ho * Wo);
+        const int r = (int)(pix - img * Ho * Wo), yo = r / Wo, xo = r - yo * Wo;
+        src = (img * H + (yo >> 1)) * W + (xo >> 1);
+    }
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x + src * C + c));
+    const float o[4] = {v.x, v.y, v.z, v.w};
+    split_store4(yh, yl, i * 4, o);
 }
 
 // Codebook lookup (get_rows, mg-vqgan.cpp:79-81): pixel p of image n is token grid[n][p]
-// (p = y * L + x), its channels the codebook row.  Ids outside [0, codebook) decode as zeros.
+// (p = y * L + x), its channels the codebook row, written as the (hi, lo) pair.  Ids outside
+// [0, codebook) decode as zeros.
 __global__ void vq_gather_kernel(const int32_t* __restrict__ grid, const float* __restrict__ cb, int n_codes, int E,
-                                 size_t n4, float* __restrict__ y) {
+                                 size_t n4, bf16* __restrict__ yh, bf16* __restrict__ yl) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const int E4 = E / 4;
@@ -295,24 +556,13 @@ __global__ void vq_gather_kernel(const int32_t* __restrict__ grid, const float* 
     const int c4 = (int)(i % E4);
     const int id = grid[pix];
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (id >= 0 && id < n_codes) v = reinterpret_cast<const float4*>(cb + (size_t)id * E)[c4];
-    reinterpret_cast<float4*>(y)[i] = v;
+    if (id >= 0 && id < n_codes) v = __ldg(reinterpret_cast<const float4*>(cb + (size_t)id * E) + c4);
+    const float o[4] = {v.x, v.y, v.z, v.w};
+    split_store4(yh, yl, i * 4, o);
 }
 
 // ------------------------------------------------------------------------------------------
 // Host side.
-struct Conv { int ic = 0, oc = 0, ks = 0; float* w = nullptr; float* b = nullptr; };
-struct Norm { int c = 0; float* g = nullptr; float* b = nullptr; };
-
-// One step of the decoder program.  Buffers: 0 = x (stream), 1 = t (normed), 2 = u, 3 = h.
-struct Step {
-    enum Kind { Gather, GnSilu, ConvOp, ConvOut, SwapXH } kind;
-    int src = 0, dst = 0, resid = -1;   // buffer ids (resid -1 = none)
-    int conv = -1, norm = -1;
-    int H = 0, W = 0, C = 0;            // output spatial size; channels of the step's input
-    bool up = false;
-};
-
 void ck(cudaError_t e, const char* what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -324,6 +574,75 @@ T* dalloc(size_t n) {
     return (T*)p;
 }
 
+// f32 -> bf16 bits, round to nearest even (finite inputs)
+uint16_t bf16_bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+float bf16_float(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    if (!fn) throw std::runtime_error("vqgan: cuTensorMapEncodeTiled is not available");
+    return fn;
+}
+
+// 4-D map over an NHWC bf16 tensor [N][H][W][C]: box = 64 channels x BW x BH x 1, 128-byte
+// swizzle, zero fill outside the tensor (the conv's padding).
+CUtensorMap make_act_map(const bf16* base, int N, int H, int W, int C, int BW, int BH) {
+    CUtensorMap m;
+    const cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
+    const cuuint64_t strides[3] = {(cuuint64_t)C * 2, (cuuint64_t)W * C * 2, (cuuint64_t)H * W * C * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)TC_BK, (cuuint32_t)BW, (cuuint32_t)BH, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<bf16*>(base), dims, strides,
+                                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("vqgan: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return m;
+}
+
+struct Conv {
+    int ic = 0, oc = 0, ks = 0;
+    float* w = nullptr;       // [T][IC][OC] f32 (SIMT and small-OC convs)
+    float* b = nullptr;
+    int bn = 0;               // tensor-core n-tile (128 / 256); 0 = channels not tensor-core shaped
+    uint8_t* wh = nullptr;    // pre-tiled bf16 hi / lo (tensor-core convs)
+    uint8_t* wl = nullptr;
+};
+struct Norm { int c = 0; float* g = nullptr; float* b = nullptr; };
+
+// One step of the decoder program.  F32 buffers: 0 = x (the running tensor), 2 = u, 3 = h;
+// every conv reads the (hi, lo) pair.
+struct Step {
+    enum Kind { Gather, GnSilu, Split, ConvOp, ConvOut, SwapXH } kind;
+    int src = 0, dst = 0, resid = -1;   // f32 buffer ids (resid -1 = none)
+    int conv = -1, norm = -1;
+    int H = 0, W = 0, C = 0;            // output spatial size; channels of the step's input
+    bool up = false;
+    // bound by reserve():
+    const float* p_src = nullptr;
+    float* p_dst = nullptr;
+    const float* p_res = nullptr;
+    bool tc = false;
+    CUtensorMap mh{}, ml{};
+};
+
 }  // namespace
 }  // namespace mgc
 
@@ -332,6 +651,7 @@ using namespace mgc;
 struct mgc_vqgan {
     int device = 0, max_images = 0;
     int n_tokens = 0, L = 0, R = 0, E = 0, n_codes = 0, groups = 32;
+    bool simt_only = false;
     cudaStream_t st = nullptr;
     float* codebook = nullptr;
     std::vector<Conv> convs;
@@ -339,8 +659,9 @@ struct mgc_vqgan {
     std::vector<Step> prog;
     size_t buf_floats = 0;       // per image
     float* buf[4] = {nullptr, nullptr, nullptr, nullptr};
-    size_t part_floats = 0;      // split-K partials, all images
-    float* part = nullptr;
+    bf16* ph = nullptr;          // the conv-input pair
+    bf16* pl = nullptr;
+    float* part = nullptr;       // split-K partials
     int gn_chunks = 0;
     double* gn_part = nullptr;
     GnStat* gn_stat = nullptr;
@@ -351,22 +672,35 @@ struct mgc_vqgan {
 
     ~mgc_vqgan() {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
-        for (auto& c : convs) { cudaFree(c.w); cudaFree(c.b); }
+        for (auto& c : convs) { cudaFree(c.w); cudaFree(c.b); cudaFree(c.wh); cudaFree(c.wl); }
         for (auto& n : norms) { cudaFree(n.g); cudaFree(n.b); }
         for (float* b : buf) cudaFree(b);
+        cudaFree(ph); cudaFree(pl);
         cudaFree(codebook); cudaFree(part); cudaFree(gn_part); cudaFree(gn_stat); cudaFree(d_grid); cudaFree(d_img);
         if (st) cudaStreamDestroy(st);
     }
 
-    int conv_split(int M, int OC, int kiters) const {
+    // ---- split-K choices (deterministic functions of the shape and image count)
+    int simt_split(int M, int OC, int kiters) const {
         const int tiles = ((M + CBM - 1) / CBM) * ((OC + CBN - 1) / CBN);
         const int target = 2 * sm_count();
         if (tiles >= target) return 1;
-        int s = (target + tiles - 1) / tiles;
-        return std::max(1, std::min(s, kiters / 4));
+        return std::max(1, std::min((target + tiles - 1) / tiles, kiters / 4));
+    }
+    int tc_split(int tiles, int kblocks) const {
+        const int target = sm_count();
+        if (tiles >= target) return 1;
+        return std::max(1, std::min((target + tiles - 1) / tiles, kblocks / 2));
+    }
+    static bool tc_shape_ok(const Conv& c, int H, int W) {
+        if (!c.bn) return false;
+        const int BW = std::min(W, 128);
+        if (BW < 16 || (BW & (BW - 1)) || W % BW) return false;
+        return H % (TC_BM / BW) == 0;
     }
 
     void load(const char* path) {
+        simt_only = [] { const char* e = std::getenv("MGC_VQGAN_SIMT"); return e && e[0] == '1'; }();
         Gguf g;
         g.open(path);
         n_tokens = g.geti("maskgit.n_tokens", 256);
@@ -380,6 +714,7 @@ struct mgc_vqgan {
         auto it = g.int_arrays.find("maskgit.vqgan.channel_multipliers");
         if (E <= 0 || filters <= 0 || nrb <= 0 || it == g.int_arrays.end() || it->second.empty())
             throw std::runtime_error("vqgan: the GGUF has no VQGAN decoder hyperparameters");
+        if (E % 8) throw std::runtime_error("vqgan: embedding_dim must be a multiple of 8");
         const std::vector<int64_t> mult = it->second;
         const int nb = (int)mult.size();
         R = L << (nb - 1);
@@ -396,17 +731,42 @@ struct mgc_vqgan {
             const GgufTensor& t = g.req(name + ".weight");
             if (t.type != 0 || t.ne[0] != ks || t.ne[1] != ks || t.ne[2] != ic || t.ne[3] != oc)
                 throw std::runtime_error("vqgan: unexpected shape or type of " + name + ".weight");
-            // [OC][IC][KH][KW] -> [tap][IC][OC]
-            const float* src = (const float*)t.data;
+            const float* src = (const float*)t.data;   // [OC][IC][KH][KW]
             const int T = ks * ks;
-            std::vector<float> w((size_t)T * ic * oc);
-            for (int o = 0; o < oc; o++)
-                for (int i = 0; i < ic; i++)
-                    for (int k = 0; k < T; k++) w[((size_t)k * ic + i) * oc + o] = src[((size_t)o * ic + i) * T + k];
             Conv c;
             c.ic = ic; c.oc = oc; c.ks = ks;
-            c.w = dalloc<float>(w.size());
-            ck(cudaMemcpy(c.w, w.data(), w.size() * 4, cudaMemcpyHostToDevice), "upload conv");
+            {   // [tap][IC][OC] f32
+                std::vector<float> w((size_t)T * ic * oc);
+                for (int o = 0; o < oc; o++)
+                    for (int i = 0; i < ic; i++)
+                        for (int k = 0; k < T; k++) w[((size_t)k * ic + i) * oc + o] = src[((size_t)o * ic + i) * T + k];
+                c.w = dalloc<float>(w.size());
+                ck(cudaMemcpy(c.w, w.data(), w.size() * 4, cudaMemcpyHostToDevice), "upload conv");
+            }
+            c.bn = (ic % TC_BK == 0) ? (oc % 256 == 0 ? 256 : oc % 128 == 0 ? 128 : 0) : 0;
+            if (c.bn) {   // pre-tiled bf16 pair: [OC/BN][T * IC/64][BN rows x 64 bf16, 128-byte swizzle]
+                const int kbl = T * ic / TC_BK, ntl = oc / c.bn;
+                const size_t bytes = (size_t)ntl * kbl * c.bn * 128;
+                std::vector<uint8_t> hi(bytes), lo(bytes);
+                for (int nt = 0; nt < ntl; nt++)
+                    for (int kb = 0; kb < kbl; kb++) {
+                        const int tap = kb / (ic / TC_BK), c0 = (kb % (ic / TC_BK)) * TC_BK;
+                        uint8_t* th = hi.data() + ((size_t)nt * kbl + kb) * c.bn * 128;
+                        uint8_t* tl = lo.data() + ((size_t)nt * kbl + kb) * c.bn * 128;
+                        for (int r = 0; r < c.bn; r++)
+                            for (int j = 0; j < TC_BK; j++) {
+                                const float v = src[((size_t)(nt * c.bn + r) * ic + c0 + j) * T + tap];
+                                const uint16_t h = bf16_bits(v), l = bf16_bits(v - bf16_float(h));
+                                const uint32_t off = sw128_off(r, j * 2);
+                                std::memcpy(th + off, &h, 2);
+                                std::memcpy(tl + off, &l, 2);
+                            }
+                    }
+                c.wh = dalloc<uint8_t>(bytes);
+                c.wl = dalloc<uint8_t>(bytes);
+                ck(cudaMemcpy(c.wh, hi.data(), bytes, cudaMemcpyHostToDevice), "upload conv");
+                ck(cudaMemcpy(c.wl, lo.data(), bytes, cudaMemcpyHostToDevice), "upload conv");
+            }
             if (bias) {
                 const GgufTensor& b = g.req(name + ".bias");
                 if (b.type != 0 || b.ne[0] != oc) throw std::runtime_error("vqgan: bad " + name + ".bias");
@@ -431,26 +791,33 @@ struct mgc_vqgan {
             norms.push_back(n);
             return (int)norms.size() - 1;
         };
+        auto step = [&](Step::Kind k, int src, int dst, int resid, int conv, int norm, int H, int W, int C, bool up) {
+            Step s{};
+            s.kind = k; s.src = src; s.dst = dst; s.resid = resid; s.conv = conv; s.norm = norm;
+            s.H = H; s.W = W; s.C = C; s.up = up;
+            prog.push_back(s);
+        };
 
-        // the program (mg-vqgan.cpp:67-108); buffers 0 = x, 1 = t, 2 = u, 3 = h
+        // the program (mg-vqgan.cpp:67-108)
         int H = L, W = L, cur = (int)(filters * mult[nb - 1]);
         size_t maxf = (size_t)H * W * E;
         auto note = [&](int c) { maxf = std::max(maxf, (size_t)H * W * c); };
-        prog.push_back(Step{Step::Gather, -1, 1, -1, -1, -1, H, W, E, false});
-        prog.push_back(Step{Step::ConvOp, 1, 0, -1, add_conv("vqgan.decoder.conv_in", E, cur, 3, true), -1, H, W, E, false});
+        step(Step::Gather, -1, -1, -1, -1, -1, H, W, E, false);
+        step(Step::ConvOp, -1, 0, -1, add_conv("vqgan.decoder.conv_in", E, cur, 3, true), -1, H, W, E, false);
         note(cur);
         auto resblock = [&](const std::string& pfx, int cin, int cout) {
-            prog.push_back(Step{Step::GnSilu, 0, 1, -1, -1, add_norm(pfx + "norm0", cin), H, W, cin, false});
-            prog.push_back(Step{Step::ConvOp, 1, 2, -1, add_conv(pfx + "conv0", cin, cout, 3, false), -1, H, W, cin, false});
-            prog.push_back(Step{Step::GnSilu, 2, 1, -1, -1, add_norm(pfx + "norm1", cout), H, W, cout, false});
+            step(Step::GnSilu, 0, -1, -1, -1, add_norm(pfx + "norm0", cin), H, W, cin, false);
+            step(Step::ConvOp, -1, 2, -1, add_conv(pfx + "conv0", cin, cout, 3, false), -1, H, W, cin, false);
+            step(Step::GnSilu, 2, -1, -1, -1, add_norm(pfx + "norm1", cout), H, W, cout, false);
             if (cin == cout) {
-                prog.push_back(Step{Step::ConvOp, 1, 3, 0, add_conv(pfx + "conv1", cout, cout, 3, false), -1, H, W, cout, false});
+                step(Step::ConvOp, -1, 3, 0, add_conv(pfx + "conv1", cout, cout, 3, false), -1, H, W, cout, false);
             } else {   // the shortcut conv reads the processed h (mg-vqgan.cpp:57-60)
-                prog.push_back(Step{Step::ConvOp, 1, 2, -1, add_conv(pfx + "conv1", cout, cout, 3, false), -1, H, W, cout, false});
-                prog.push_back(Step{Step::ConvOp, 2, 3, 2, add_conv(pfx + "conv_res", cout, cout, 1, false), -1, H, W, cout, false});
+                step(Step::ConvOp, -1, 2, -1, add_conv(pfx + "conv1", cout, cout, 3, false), -1, H, W, cout, false);
+                step(Step::Split, 2, -1, -1, -1, -1, H, W, cout, false);
+                step(Step::ConvOp, -1, 3, 2, add_conv(pfx + "conv_res", cout, cout, 1, false), -1, H, W, cout, false);
             }
             note(cin); note(cout);
-            prog.push_back(Step{Step::SwapXH});
+            step(Step::SwapXH, -1, -1, -1, -1, -1, H, W, cout, false);
         };
         for (int l = 0; l < nrb; l++) resblock("vqgan.decoder.res_blocks.0." + std::to_string(l) + ".", cur, cur);
         int prev = cur, bi = 1;
@@ -465,52 +832,28 @@ struct mgc_vqgan {
                 note(cur);
                 const int c = add_conv("vqgan.decoder.res_blocks." + std::to_string(bi) + "." + std::to_string(nrb + 1),
                                        cur, cur, 3, true);
-                prog.push_back(Step{Step::ConvOp, 0, 3, -1, c, -1, H, W, cur, true});
-                prog.push_back(Step{Step::SwapXH});
+                step(Step::Split, 0, -1, -1, -1, -1, H, W, cur, true);
+                step(Step::ConvOp, -1, 3, -1, c, -1, H, W, cur, false);
+                step(Step::SwapXH, -1, -1, -1, -1, -1, H, W, cur, false);
             }
         }
-        prog.push_back(Step{Step::GnSilu, 0, 1, -1, -1, add_norm("vqgan.decoder.norm_out", cur), H, W, cur, false});
+        step(Step::GnSilu, 0, -1, -1, -1, add_norm("vqgan.decoder.norm_out", cur), H, W, cur, false);
         const GgufTensor& co = g.req("vqgan.decoder.conv_out.weight");
         if (co.ne[3] > kSmallOC) throw std::runtime_error("vqgan: conv_out must have at most 4 output channels");
-        prog.push_back(Step{Step::ConvOut, 1, -1, -1, add_conv("vqgan.decoder.conv_out", cur, (int)co.ne[3], 3, true), -1,
-                            H, W, cur, false});
+        step(Step::ConvOut, -1, -1, -1, add_conv("vqgan.decoder.conv_out", cur, (int)co.ne[3], 3, true), -1, H, W, cur,
+             false);
         const size_t co_smem = (size_t)9 * cur * kSmallOC * 4;
         if (co_smem > 200 * 1024) throw std::runtime_error("vqgan: conv_out input has too many channels");
         ck(cudaFuncSetAttribute(conv_small_oc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)co_smem),
            "conv_out smem");
+        ck(cudaFuncSetAttribute(conv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::SMEM),
+           "conv smem");
+        ck(cudaFuncSetAttribute(conv_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::SMEM),
+           "conv smem");
         for (const Conv& c : convs)
             if (c.oc > kSmallOC && (c.oc % 4 || c.ic % CBK))
                 throw std::runtime_error("vqgan: conv channel counts must be multiples of 4 (out) and 8 (in)");
         buf_floats = maxf;
-    }
-
-    // device buffers for n images (grown on demand)
-    void reserve(int n) {
-        if (n <= max_images) return;
-        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
-        graphs.clear();
-        for (float*& b : buf) { cudaFree(b); b = dalloc<float>(buf_floats * n); }
-        // split-K partials: the largest over the conv steps at n images
-        size_t pf = 0;
-        int maxc = 0;
-        for (const Step& s : prog) {
-            if (s.kind == Step::GnSilu) maxc = std::max(maxc, s.C);
-            if (s.kind != Step::ConvOp) continue;
-            const Conv& c = convs[s.conv];
-            const int M = n * s.H * s.W, kit = c.ks * c.ks * c.ic / CBK;
-            const int ns = conv_split(M, c.oc, kit);
-            if (ns > 1) pf = std::max(pf, (size_t)ns * M * c.oc);
-        }
-        cudaFree(part); part = dalloc<float>(pf);
-        part_floats = pf;
-        gn_chunks = 0;
-        for (const Step& s : prog)
-            if (s.kind == Step::GnSilu) gn_chunks = std::max(gn_chunks, chunks_for(n, s.H * s.W));
-        cudaFree(gn_part); gn_part = dalloc<double>((size_t)n * gn_chunks * maxc * 2);
-        cudaFree(gn_stat); gn_stat = dalloc<GnStat>((size_t)n * groups);
-        cudaFree(d_grid); d_grid = dalloc<int32_t>((size_t)n * n_tokens);
-        cudaFree(d_img); d_img = dalloc<float>((size_t)n * R * R * 3);
-        max_images = n;
     }
 
     int chunks_for(int n, int HW) const {
@@ -518,55 +861,140 @@ struct mgc_vqgan {
         return std::max(1, std::min(want, HW / 64));
     }
 
-    // Enqueue the decoder on `s` for n images: grid (device, [n][n_tokens]) -> out (device,
-    // [n][R][R][3]).  Returns the number of kernels launched.
+    // Device buffers for n images; binds every step to its buffers and tensor maps.
+    void reserve(int n) {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+        for (float*& b : buf) { cudaFree(b); b = nullptr; }
+        for (int i : {0, 2, 3}) buf[i] = dalloc<float>(buf_floats * n);
+        cudaFree(ph); ph = dalloc<bf16>(buf_floats * n);
+        cudaFree(pl); pl = dalloc<bf16>(buf_floats * n);
+        size_t pf = 0;
+        gn_chunks = 0;
+        size_t gn_need = 0;
+        float* b[4] = {buf[0], buf[1], buf[2], buf[3]};
+        for (Step& s : prog) {
+            if (s.kind == Step::SwapXH) { std::swap(b[0], b[3]); continue; }
+            s.p_src = s.src >= 0 ? b[s.src] : nullptr;
+            s.p_dst = s.dst >= 0 ? b[s.dst] : nullptr;
+            s.p_res = s.resid >= 0 ? b[s.resid] : nullptr;
+            if (s.kind != Step::ConvOp) continue;
+            const Conv& c = convs[s.conv];
+            s.tc = !simt_only && tc_shape_ok(c, s.H, s.W);
+            if (s.tc) {
+                const int BW = std::min(s.W, 128), BH = TC_BM / BW;
+                s.mh = make_act_map(ph, n, s.H, s.W, c.ic, BW, BH);
+                s.ml = make_act_map(pl, n, s.H, s.W, c.ic, BW, BH);
+            }
+        }
+        // split-K partials and GroupNorm partials: the largest over every image count <= n
+        for (int k = 1; k <= n; k++)
+            for (const Step& s : prog) {
+                if (s.kind == Step::GnSilu) {
+                    const int nch = chunks_for(k, s.H * s.W);
+                    gn_chunks = std::max(gn_chunks, nch);
+                    gn_need = std::max(gn_need, (size_t)k * nch * s.C * 2);
+                }
+                if (s.kind != Step::ConvOp) continue;
+                const Conv& c = convs[s.conv];
+                const int M = k * s.H * s.W;
+                int kit, ns;
+                if (s.tc) {
+                    kit = c.ks * c.ks * c.ic / TC_BK;
+                    ns = tc_split((M / TC_BM) * (c.oc / c.bn), kit);
+                } else {
+                    kit = c.ks * c.ks * c.ic / CBK;
+                    ns = simt_split(M, c.oc, kit);
+                }
+                const int kper = (kit + ns - 1) / ns, nsu = (kit + kper - 1) / kper;
+                if (nsu > 1) pf = std::max(pf, (size_t)nsu * M * c.oc);
+            }
+        cudaFree(part); part = dalloc<float>(pf);
+        cudaFree(gn_part); gn_part = dalloc<double>(gn_need);
+        cudaFree(gn_stat); gn_stat = dalloc<GnStat>((size_t)n * groups);
+        cudaFree(d_grid); d_grid = dalloc<int32_t>((size_t)n * n_tokens);
+        cudaFree(d_img); d_img = dalloc<float>((size_t)n * R * R * 3);
+        max_images = n;
+    }
+
+    // Enqueue the decoder on `s` for n <= max_images images: grid (device, [n][n_tokens]) ->
+    // out (device, [n][R][R][3]).  Returns the number of kernels launched.
     int enqueue(const int32_t* grid, int n, float* out, cudaStream_t s) {
         int nl = 0;
-        float* b[4] = {buf[0], buf[1], buf[2], buf[3]};
         for (const Step& stp : prog) {
             const int HW = stp.H * stp.W;
             switch (stp.kind) {
+            case Step::SwapXH:
+                break;
             case Step::Gather: {
                 const size_t n4 = (size_t)n * HW * E / 4;
-                launch_k(vq_gather_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, grid, codebook, n_codes, E, n4,
-                         b[stp.dst]);
+                launch_k(vq_gather_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, grid, (const float*)codebook,
+                         n_codes, E, n4, ph, pl);
                 nl++;
                 break;
             }
-            case Step::SwapXH:
-                std::swap(b[0], b[3]);
+            case Step::Split: {
+                const size_t n4 = (size_t)n * HW * stp.C / 4;
+                const int Hs = stp.up ? stp.H / 2 : stp.H, Ws = stp.up ? stp.W / 2 : stp.W;
+                launch_k(split_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, stp.p_src, Hs, Ws, stp.C,
+                         stp.up ? 1 : 0, n4, ph, pl);
+                nl++;
                 break;
+            }
             case Step::GnSilu: {
                 const Norm& nm = norms[stp.norm];
                 const int nch = chunks_for(n, HW), ppc = (HW + nch - 1) / nch;
-                launch_k(gn_partial_kernel, dim3(nch, n), kGnThreads, 0, s, b[stp.src], HW, nm.c, ppc, gn_part);
-                launch_k(gn_finalize_kernel, n, std::max(32, groups), 0, s, gn_part, nch, nm.c, groups, HW, 1e-5f,
-                         gn_stat);
+                launch_k(gn_partial_kernel, dim3(nch, n), kGnThreads, 0, s, stp.p_src, HW, nm.c, ppc, gn_part);
+                launch_k(gn_finalize_kernel, n, std::max(32, groups), 0, s, (const double*)gn_part, nch, nm.c, groups,
+                         HW, 1e-5f, gn_stat);
                 const size_t n4 = (size_t)n * HW * nm.c / 4;
-                launch_k(gn_apply_silu_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, b[stp.src], gn_stat, nm.g, nm.b,
-                         HW, nm.c, groups, n4, b[stp.dst]);
+                launch_k(gn_apply_silu_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, stp.p_src,
+                         (const GnStat*)gn_stat, (const float*)nm.g, (const float*)nm.b, HW, nm.c, groups, n4, ph, pl);
                 nl += 3;
                 break;
             }
             case Step::ConvOp: {
                 const Conv& c = convs[stp.conv];
-                ConvArgs a{};
-                a.x = b[stp.src]; a.w = c.w; a.bias = c.b; a.resid = stp.resid >= 0 ? b[stp.resid] : nullptr;
-                a.y = b[stp.dst]; a.part = part;
-                a.H = stp.H; a.W = stp.W; a.IC = c.ic; a.OC = c.oc; a.ks = c.ks; a.up = stp.up;
-                a.M = n * HW;
-                a.kiters = c.ks * c.ks * c.ic / CBK;
-                const int ns = conv_split(a.M, c.oc, a.kiters);
-                a.kper = (a.kiters + ns - 1) / ns;
-                const int nsu = (a.kiters + a.kper - 1) / a.kper;
-                dim3 gr((a.M + CBM - 1) / CBM, (c.oc + CBN - 1) / CBN, nsu);
-                if (stp.up) launch_k(conv_simt_kernel<true>, gr, 256, 0, s, a);
-                else launch_k(conv_simt_kernel<false>, gr, 256, 0, s, a);
+                const int M = n * HW;
+                int nsu = 1;
+                if (stp.tc) {
+                    TcArgs a{};
+                    a.wh = c.wh; a.wl = c.wl; a.bias = c.b; a.resid = stp.p_res; a.y = stp.p_dst; a.part = part;
+                    a.H = stp.H; a.W = stp.W; a.IC = c.ic; a.OC = c.oc; a.ks = c.ks; a.M = M;
+                    a.BW = std::min(stp.W, 128);
+                    a.BH = TC_BM / a.BW;
+                    a.tiles_x = stp.W / a.BW;
+                    a.tiles_per_img = a.tiles_x * (stp.H / a.BH);
+                    a.m_tiles = n * a.tiles_per_img;
+                    a.n_tiles = c.oc / c.bn;
+                    a.kblocks = c.ks * c.ks * c.ic / TC_BK;
+                    const int ns = tc_split(a.m_tiles * a.n_tiles, a.kblocks);
+                    a.kper = (a.kblocks + ns - 1) / ns;
+                    nsu = (a.kblocks + a.kper - 1) / a.kper;
+                    a.nsplit = nsu;
+                    a.n_units = a.m_tiles * a.n_tiles * nsu;
+                    const int grid_x = std::min(a.n_units, sm_count());
+                    if (c.bn == 256)
+                        launch_k(conv_tc_kernel<256>, grid_x, 192, TcCfg<256>::SMEM, s, stp.mh, stp.ml, a);
+                    else
+                        launch_k(conv_tc_kernel<128>, grid_x, 192, TcCfg<128>::SMEM, s, stp.mh, stp.ml, a);
+                } else {
+                    ConvArgs a{};
+                    a.xh = ph; a.xl = pl; a.w = c.w; a.bias = c.b; a.resid = stp.p_res;
+                    a.y = stp.p_dst; a.part = part;
+                    a.H = stp.H; a.W = stp.W; a.IC = c.ic; a.OC = c.oc; a.ks = c.ks; a.M = M;
+                    a.kiters = c.ks * c.ks * c.ic / CBK;
+                    const int ns = simt_split(M, c.oc, a.kiters);
+                    a.kper = (a.kiters + ns - 1) / ns;
+                    nsu = (a.kiters + a.kper - 1) / a.kper;
+                    dim3 gr((M + CBM - 1) / CBM, (c.oc + CBN - 1) / CBN, nsu);
+                    launch_k(conv_simt_kernel, gr, 256, 0, s, a);
+                }
                 nl++;
                 if (nsu > 1) {
-                    const size_t n4 = (size_t)a.M * c.oc / 4;
-                    launch_k(conv_splitk_reduce_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, part, nsu, n4, c.oc,
-                             c.b, a.resid, a.y);
+                    const size_t n4 = (size_t)M * c.oc / 4;
+                    launch_k(conv_splitk_reduce_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, (const float*)part, nsu,
+                             n4, c.oc, (const float*)c.b, stp.p_res, stp.p_dst);
                     nl++;
                 }
                 break;
@@ -575,8 +1003,8 @@ struct mgc_vqgan {
                 const Conv& c = convs[stp.conv];
                 const int M = n * HW;
                 const size_t smem = (size_t)c.ks * c.ks * c.ic * kSmallOC * 4;
-                launch_k(conv_small_oc_kernel, (unsigned)((M + 127) / 128), 128, smem, s, b[stp.src], c.w, c.b, out, M,
-                         stp.H, stp.W, c.ic, c.oc, c.ks);
+                launch_k(conv_small_oc_kernel, (unsigned)((M + 127) / 128), 128, smem, s, (const bf16*)ph,
+                         (const bf16*)pl, (const float*)c.w, (const float*)c.b, out, M, stp.H, stp.W, c.ic, c.oc, c.ks);
                 nl++;
                 break;
             }
@@ -594,11 +1022,13 @@ struct mgc_vqgan {
             cudaGraph_t gph = nullptr;
             ck(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "capture");
             launches = enqueue(d_grid, n, d_img, cap);
-            ck(cudaStreamEndCapture(cap, &gph), "end capture");
-            cudaGraphExec_t ex = nullptr;
-            ck(cudaGraphInstantiate(&ex, gph, 0), "instantiate");
-            cudaGraphDestroy(gph);
+            const cudaError_t e = cudaStreamEndCapture(cap, &gph);
             cudaStreamDestroy(cap);
+            ck(e, "end capture");
+            cudaGraphExec_t ex = nullptr;
+            const cudaError_t ei = cudaGraphInstantiate(&ex, gph, 0);
+            cudaGraphDestroy(gph);
+            ck(ei, "instantiate");
             it = graphs.emplace(n, ex).first;
         }
         ck(cudaGraphLaunch(it->second, s), "graph launch");

@@ -171,3 +171,23 @@ def test_reference_generate_drives_cuda_vqgan(tmp_path, oracle_mod):
     dec.close()
     if oracle_mod.ref_available():
         _gate(image, oracle_mod.ref_vqgan(path, grid, 64))
+
+
+def test_vqgan_tensor_core_and_simt_paths_agree(vq_models, monkeypatch):
+    """The same decode with every conv on the SIMT f32 path (MGC_VQGAN_SIMT=1) and with the
+    tcgen05 bf16x3 path: both within the reference gate of each other, and of the golden."""
+    from edge_maskgit_b200 import runtime as rt
+    models, _ = vq_models
+    path, spec = models["full"]
+    g = np.load(GOLD)
+    tc = rt.VqganDecoder(path)
+    img_tc = tc.decode(g["full_grid"])
+    tc.close()
+    monkeypatch.setenv("MGC_VQGAN_SIMT", "1")
+    sm = rt.VqganDecoder(path)
+    img_sm = sm.decode(g["full_grid"])
+    sm.close()
+    d, c = _gate(img_tc, img_sm)
+    assert d < 2e-3, d
+    for img in (img_tc, img_sm):
+        _gate(img.ravel()[g["full_index"]], g["full_samples"])
