@@ -549,11 +549,22 @@ def reference_vqgan_s() -> tuple[float, str]:
                         f"{dt:.2f} s, x{scale:.1f} by conv FLOPs to the 256x256 decoder")
 
 
+def bf16_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+VQ_OPS = ("conv_tc", "conv_simt", "conv_out", "splitk_reduce", "groupnorm", "split", "gather")
+
+
 def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, batch: int = 8) -> dict:
     """VQGAN decode of seeded token grids on each rank (replicas: each rank decodes its own
-    images, no collective).  Device timing: the decode graph on device buffers (CUDA events on
-    its stream); e2e: mgc_vqgan_decode with host grids in and the host HWC image out."""
-    import torch
+    images, no collective).  Device timing: the decode's CUDA graph replayed on device-resident
+    grids (CUDA events on the decoder's stream), for 1 image (the VqganFwd call) and for a
+    batch; per kernel class, a graph of that class's launches alone.  e2e: mgc_vqgan_decode,
+    host grid in and the host HWC image out, synchronous per image."""
     from edge_maskgit_b200 import runtime as rt
 
     if rank == 0:
@@ -563,44 +574,40 @@ def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, ba
     dec = rt.VqganDecoder(path, max_images=batch, device=local)
     R = dec.resolution
     grids = np.random.default_rng(100 + rank).integers(0, 1024, (batch, spec.n_tokens)).astype(np.int32)
-    g_dev = torch.from_numpy(grids).cuda()
-    out1 = torch.empty((1, R, R, 3), dtype=torch.float32, device="cuda")
-    outb = torch.empty((batch, R, R, 3), dtype=torch.float32, device="cuda")
-    host_img = np.empty((1, R, R, 3), np.float32)
-    res = {}
-    for n, out in ((1, out1), (batch, outb)):
-        for _ in range(warmup):
-            dec.decode_device(g_dev, out, n)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        _barrier(world)
-        e0.record()
-        for _ in range(steps):
-            dec.decode_device(g_dev, out, n)
-        e1.record()
-        torch.cuda.synchronize()
-        res[n] = _max_over_ranks([e0.elapsed_time(e1) / steps], world)[0]
-    launches = dec.launches()
-    for _ in range(warmup):
-        dec.decode(grids[0], out=host_img)
+    host_img = np.empty((batch, R, R, 3), np.float32)
+    dec.decode(grids, out=host_img)            # fills the device grids / buffers, captures the graphs
+    dec.decode(grids[0], out=host_img[:1])
     _barrier(world)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        dec.decode(grids[0], out=host_img)
-    e2e_ms = _max_over_ranks([(time.perf_counter() - t0) * 1e3 / steps], world)[0]
+    with ClockSampler(local) as clk:
+        ms1, nl1 = dec.time_op("all", 1, iters=steps)
+        msb, nlb = dec.time_op("all", batch, iters=steps)
+        ops = {op: dec.time_op(op, batch, iters=steps) for op in VQ_OPS}
+        for _ in range(warmup):
+            dec.decode(grids[0], out=host_img[:1])
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            dec.decode(grids[0], out=host_img[:1])
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / steps
+    ms1, msb, e2e_ms, tc_ms = _max_over_ranks([ms1, msb, e2e_ms, ops["conv_tc"][0]], world)
     dec.close()
     fl = vqgan_flops(spec)
-    ach = fl / (res[1] * 1e-3) / 1e12
-    return {"workload": "VQGAN decode, MaskGIT decoder (filters 128, mult 1,1,2,2,4, 16x16 -> 256x256), f32",
+    fl_out = 2.0 * 9 * spec.vqgan.filters * spec.vqgan.channel_multipliers[0] * 3 * R * R   # conv_out (SIMT)
+    peak, src = bf16_peak()
+    # the tensor-core convs issue 3 bf16 MMAs (hi*hi, hi*lo, lo*hi) per product
+    ach = 3 * (fl - fl_out) * batch / (tc_ms * 1e-3) / 1e12
+    return {"workload": "VQGAN decode, MaskGIT decoder (filters 128, mult 1,1,2,2,4, 16x16 -> 256x256)",
             "parallelism": f"replicas x{world}", "scaling": "weak",
-            "ms_per_image": res[1], "images_per_s": world * 1e3 / res[1],
-            f"ms_per_batch{batch}": res[batch], f"images_per_s_batch{batch}": world * batch * 1e3 / res[batch],
-            "e2e_ms_per_image": e2e_ms, "gpu_launches_per_decode": launches,
+            "ms_per_image": ms1, "images_per_s": world * 1e3 / ms1,
+            f"ms_per_batch{batch}": msb, f"images_per_s_batch{batch}": world * batch * 1e3 / msb,
+            "e2e_ms_per_image": e2e_ms, "gpu_launches_per_decode": nl1, f"gpu_launches_per_batch{batch}": nlb,
             "conv_gflop_per_image": fl / 1e9,
-            "roofline": {"bound": "fp32", "achieved": ach, "peak": FP32_NOMINAL_TFLOPS, "unit": "TFLOP/s",
-                         "frac": ach / FP32_NOMINAL_TFLOPS,
-                         "note": "whole decode at 1 image (conv FLOPs / decode time) against the nominal "
-                                 "FP32 FMA rate at max clock"}}
+            f"kernel_ms_per_batch{batch}": {op: {"ms": v[0], "launches": v[1]} for op, v in ops.items()},
+            "clocks": clk.summary(),
+            "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                         "kernel": f"conv_tc (tcgen05 bf16 hi/lo x3): a graph of the decode's tensor-core conv "
+                                   f"launches alone at {batch} images, {tc_ms:.3f} ms; MMA FLOPs = 3 x the conv "
+                                   f"FLOPs they compute ({(fl - fl_out) / 1e9:.1f} GFLOP per image)",
+                         "peak_source": f"{src} (MEASURED_PEAKS.json bf16_tflops, burst)"}}
 
 
 def run_vqgan_workload(args) -> None:
@@ -609,13 +616,15 @@ def run_vqgan_workload(args) -> None:
     if rank == 0:
         out = {"metric": "VQGAN images/s", "value": m["images_per_s"], "unit": "images/s", "n_gpus": world,
                "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_image"],
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+               "dtype": "f32 activations; convs bf16 hi/lo x3 on tensor cores, f32 accumulate",
                "data": "synthetic (seeded decoder weights and token grids)",
                "config": {"workload": m["workload"], "parallelism": m["parallelism"],
                           "l2": "activations 32 MB per image per layer at 256x256; weights 100 MB"},
                "e2e": {"value": world * 1e3 / m["e2e_ms_per_image"], "unit": "images/s",
                        "h2d_bytes_per_step": 256 * 4, "d2h_bytes_per_step": 256 * 256 * 3 * 4},
-               "gpu_launches": m["gpu_launches_per_decode"] * args.steps, "roofline": m["roofline"], "detail": m}
+               "gpu_launches": m["gpu_launches_per_decode"] * args.steps, "roofline": m["roofline"],
+               "clocks": m["clocks"], "detail": m}
         if world == 1 and not args.no_cpu_baseline:
             try:
                 s_, sample = reference_vqgan_s()

@@ -58,6 +58,7 @@ _SIGS = {
     "mgc_vqgan_decode": (I, [P, P, I, P]),
     "mgc_vqgan_decode_device": (I, [P, P, I, P, P]),
     "mgc_vqgan_launches": (I, [P]),
+    "mgc_vqgan_time_op": (I, [P, C.c_char_p, I, I, C.POINTER(F), C.POINTER(I)]),
     "mgc_vqgan_destroy": (None, [P]),
 }
 

@@ -24,9 +24,10 @@
 // implicit GEMM; MGC_VQGAN_SIMT=1 at create time forces that path for every conv.
 //
 // Numerics follow mg-cpu (src/mg-cpu/mg-cpu.cpp): GroupNorm statistics in double
-// (:124-147, variance as E[x^2] - mean^2 over per-chunk double sums), normalisation
-// (float)(x - mean) * inv, then xn = o * gamma + beta and xn / (1 + exp(-xn)) (:265-276) with
-// separately rounded multiply and add; convs accumulate in f32 in another order.
+// (:124-147, variance as E[x^2] - mean^2 over per-chunk double sums), inv = 1/sqrt((float)var +
+// eps) as there; the apply computes xn = (x - mean) * (gamma * inv) + beta in f32 with one fused
+// multiply-add (mg-cpu: (float)(x - mean) * inv, then * gamma + beta, :265-276; a few ulp apart)
+// and xn / (1 + exp(-xn)); convs accumulate in f32 in another order.
 #include "../../include/mgc.h"
 #include "gguf.h"
 #include "kernels.h"
@@ -207,42 +208,81 @@ __global__ void conv_splitk_reduce_kernel(const float* __restrict__ part, int ns
     reinterpret_cast<float4*>(y)[i] = v;
 }
 
-// Conv with few output channels (conv_out, OC = 3): one thread a pixel, weights in shared
-// memory as [tap][IC][4].
+// Conv with few output channels (conv_out: 3x3, OC <= 4).  A block computes a 32 x 32 pixel
+// tile of one image, 256 threads, 4 vertically adjacent pixels a thread.  Input channels go in
+// chunks of 8: the (34 x 34)-pixel haloed tile of the chunk is staged in shared memory as f32
+// (hi + lo, zeros outside the image, 9-float pixel stride: conflict-free), then each thread
+// runs the chunk's 9 taps x 8 channels on its 4 pixels with the weights ([tap][IC][4], read as
+// one broadcast float4) from shared memory.
 constexpr int kSmallOC = 4;
-__global__ void __launch_bounds__(128) conv_small_oc_kernel(const bf16* __restrict__ xh, const bf16* __restrict__ xl,
-                                                            const float* __restrict__ w, const float* __restrict__ bias,
-                                                            float* __restrict__ y, int M, int H, int W, int IC, int OC,
-                                                            int ks) {
-    extern __shared__ float ws[];   // [T][IC][4]
-    const int T = ks * ks;
-    for (int i = threadIdx.x; i < T * IC * kSmallOC; i += blockDim.x) {
+constexpr int kCoTile = 32, kCoHalo = kCoTile + 2, kCoCh = 8, kCoPix = kCoHalo * kCoHalo, kCoStride = kCoCh + 1;
+__global__ void __launch_bounds__(256) conv_small_oc_kernel(const bf16* __restrict__ xh, const bf16* __restrict__ xl,
+                                                            const float* __restrict__ w,
+                                                            const float* __restrict__ bias, float* __restrict__ y,
+                                                            int H, int W, int IC, int OC) {
+    extern __shared__ float sm[];
+    float* ws = sm;                           // [9][IC][4]
+    float* xs = sm + 9 * IC * kSmallOC;       // [kCoPix][kCoStride]
+    for (int i = threadIdx.x; i < 9 * IC * kSmallOC; i += blockDim.x) {
         const int o = i % kSmallOC, r = i / kSmallOC;
         ws[i] = o < OC ? w[(size_t)r * OC + o] : 0.f;
     }
-    __syncthreads();
-    const int m = blockIdx.x * blockDim.x + threadIdx.x;
-    if (m >= M) return;
-    const int HW = H * W, img = m / HW, rem = m - img * HW, py = rem / W, px = rem - py * W;
-    const int half = ks >> 1;
-    float acc[kSmallOC] = {0.f, 0.f, 0.f, 0.f};
-    for (int tap = 0; tap < T; tap++) {
-        const int yy = py + tap / ks - half, xx = px + tap % ks - half;
-        if (yy < 0 || yy >= H || xx < 0 || xx >= W) continue;
-        const size_t src = ((size_t)(img * H + yy) * W + xx) * IC;
-        const float4* wt = reinterpret_cast<const float4*>(ws + (size_t)tap * IC * kSmallOC);
-        for (int c4 = 0; c4 < IC / 4; c4++) {
-            const float4 v = load_pair4(xh, xl, src + c4 * 4);
-            const float xv[4] = {v.x, v.y, v.z, v.w};
+    const int img = blockIdx.z, x0 = blockIdx.x * kCoTile, y0 = blockIdx.y * kCoTile;
+    const int tx = threadIdx.x & 31, ty = (threadIdx.x >> 5) * 4;   // pixels (x0+tx, y0+ty .. +3)
+    float acc[4][kSmallOC];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float4 wv = wt[c4 * 4 + j];
-                acc[0] = fmaf(xv[j], wv.x, acc[0]); acc[1] = fmaf(xv[j], wv.y, acc[1]);
-                acc[2] = fmaf(xv[j], wv.z, acc[2]); acc[3] = fmaf(xv[j], wv.w, acc[3]);
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int o = 0; o < kSmallOC; o++) acc[i][o] = 0.f;
+    const size_t img_base = (size_t)img * H * W;
+    for (int c0 = 0; c0 < IC; c0 += kCoCh) {
+        __syncthreads();   // the previous chunk's reads are done (and, first time, the weights are in)
+        for (int p = threadIdx.x; p < kCoPix; p += blockDim.x) {
+            const int gy = y0 + p / kCoHalo - 1, gx = x0 + p % kCoHalo - 1;
+            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (gy >= 0 && gy < H && gx >= 0 && gx < W) {
+                const size_t off = (img_base + (size_t)gy * W + gx) * IC + c0;
+                const uint4 h = __ldg(reinterpret_cast<const uint4*>(xh + off));
+                const uint4 l = __ldg(reinterpret_cast<const uint4*>(xl + off));
+                const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float2 hf = bf2_to_f2(hw[q]), lf = bf2_to_f2(lw[q]);
+                    v[2 * q] = hf.x + lf.x;
+                    v[2 * q + 1] = hf.y + lf.y;
+                }
             }
+#pragma unroll
+            for (int c = 0; c < kCoCh; c++) xs[p * kCoStride + c] = v[c];
         }
+        __syncthreads();
+#pragma unroll
+        for (int kx = 0; kx < 3; kx++)
+#pragma unroll 2
+            for (int c = 0; c < kCoCh; c++) {
+                float col[6];
+#pragma unroll
+                for (int r = 0; r < 6; r++) col[r] = xs[((ty + r) * kCoHalo + tx + kx) * kCoStride + c];
+#pragma unroll
+                for (int ky = 0; ky < 3; ky++) {
+                    const float4 wv = *reinterpret_cast<const float4*>(ws + ((size_t)(ky * 3 + kx) * IC + c0 + c) * 4);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float xv = col[i + ky];
+                        acc[i][0] = fmaf(xv, wv.x, acc[i][0]); acc[i][1] = fmaf(xv, wv.y, acc[i][1]);
+                        acc[i][2] = fmaf(xv, wv.z, acc[i][2]); acc[i][3] = fmaf(xv, wv.w, acc[i][3]);
+                    }
+                }
+            }
     }
-    for (int o = 0; o < OC; o++) y[(size_t)m * OC + o] = acc[o] + (bias ? bias[o] : 0.f);
+    const int gx = x0 + tx;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int gy = y0 + ty + i;
+        if (gx >= W || gy >= H) continue;
+        float* o = y + (img_base + (size_t)gy * W + gx) * OC;
+        for (int k = 0; k < OC; k++) o[k] = acc[i][k] + (bias ? bias[k] : 0.f);
+    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -481,46 +521,63 @@ __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const float* __r
     }
 }
 
-struct GnStat { double mean; float inv; float pad; };
-
-__global__ void gn_finalize_kernel(const double* __restrict__ part, int nch, int C, int G, int HW, float eps,
-                                   GnStat* __restrict__ st) {
-    const int img = blockIdx.x, g = threadIdx.x;
-    if (g >= G) return;
-    const int cpg = C / G;
+// Pass 2: one block per (group, image); the chunk x channel partials are summed by a fixed
+// strided split and a fixed tree (deterministic).  Writes, per (image, channel), the group's
+// mean (rounded to f32) and a = gamma * inv, inv = 1 / sqrt(var + eps) as mg-cpu rounds it.
+constexpr int kGnFinThreads = 128;
+__global__ void __launch_bounds__(kGnFinThreads) gn_finalize_kernel(const double* __restrict__ part, int nch, int C,
+                                                                    int G, int HW, float eps,
+                                                                    const float* __restrict__ gamma,
+                                                                    float* __restrict__ mean_c, float* __restrict__ a_c) {
+    __shared__ double rs[kGnFinThreads], rss[kGnFinThreads];
+    const int g = blockIdx.x, img = blockIdx.y, cpg = C / G, n_items = nch * cpg;
     double s = 0, ss = 0;
-    for (int k = 0; k < nch; k++)
-        for (int c = g * cpg; c < (g + 1) * cpg; c++) {
-            const double* p = part + (((size_t)img * nch + k) * C + c) * 2;
-            s += p[0]; ss += p[1];
-        }
+    for (int i = threadIdx.x; i < n_items; i += kGnFinThreads) {
+        const int k = i / cpg, c = g * cpg + i % cpg;
+        const double* p = part + (((size_t)img * nch + k) * C + c) * 2;
+        s += p[0]; ss += p[1];
+    }
+    rs[threadIdx.x] = s; rss[threadIdx.x] = ss;
+    __syncthreads();
+    for (int w = kGnFinThreads / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) { rs[threadIdx.x] += rs[threadIdx.x + w]; rss[threadIdx.x] += rss[threadIdx.x + w]; }
+        __syncthreads();
+    }
     const double cnt = (double)HW * cpg;
-    const double mean = s / cnt;
-    const double var = fmax(ss / cnt - mean * mean, 0.0);
-    st[img * G + g] = GnStat{mean, 1.0f / sqrtf((float)var + eps), 0.f};
+    const double mean = rs[0] / cnt;
+    const double var = fmax(rss[0] / cnt - mean * mean, 0.0);
+    const float inv = 1.0f / sqrtf((float)var + eps);
+    for (int j = threadIdx.x; j < cpg; j += kGnFinThreads) {
+        const int c = g * cpg + j;
+        mean_c[(size_t)img * C + c] = (float)mean;
+        a_c[(size_t)img * C + c] = __fmul_rn(inv, gamma[c]);
+    }
 }
 
-__global__ void gn_apply_silu_kernel(const float* __restrict__ x, const GnStat* __restrict__ st,
-                                     const float* __restrict__ gamma, const float* __restrict__ beta, int HW, int C,
-                                     int G, size_t n4, bf16* __restrict__ yh, bf16* __restrict__ yl) {
+// Pass 3: y = silu((x - mean) * a + beta), 8 channels a thread, written as the (hi, lo) pair.
+__global__ void gn_apply_silu_kernel(const float* __restrict__ x, const float* __restrict__ mean_c,
+                                     const float* __restrict__ a_c, const float* __restrict__ beta, int HW, int C,
+                                     size_t n8, bf16* __restrict__ yh, bf16* __restrict__ yl) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n4) return;
-    const size_t e = i * 4;
+    if (i >= n8) return;
+    const size_t e = i * 8;
     const int c0 = (int)(e % C);
-    const int img = (int)(e / ((size_t)HW * C));
-    const int cpg = C / G;
-    const float4 v = reinterpret_cast<const float4*>(x)[i];
-    const float xv[4] = {v.x, v.y, v.z, v.w};
-    float o[4];
+    const size_t img = e / ((size_t)HW * C);
+    const float4* xp = reinterpret_cast<const float4*>(x + e);
+    const float4 v0 = __ldg(xp), v1 = __ldg(xp + 1);
+    const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    const float* mc = mean_c + img * C + c0;
+    const float* ac = a_c + img * C + c0;
+    __align__(16) bf16 h[8], l[8];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int c = c0 + j;
-        const GnStat s = st[img * G + c / cpg];
-        const float nrm = __fmul_rn((float)((double)xv[j] - s.mean), s.inv);
-        const float xn = __fadd_rn(__fmul_rn(nrm, gamma[c]), beta[c]);
-        o[j] = xn / (1.0f + expf(-xn));
+    for (int j = 0; j < 8; j++) {
+        const float xn = fmaf(xv[j] - mc[j], ac[j], beta[c0 + j]);
+        const float o = xn / (1.0f + expf(-xn));
+        h[j] = __float2bfloat16_rn(o);
+        l[j] = __float2bfloat16_rn(o - __bfloat162float(h[j]));
     }
-    split_store4(yh, yl, e, o);
+    *reinterpret_cast<uint4*>(yh + e) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(yl + e) = *reinterpret_cast<const uint4*>(l);
 }
 
 // f32 NHWC -> (hi, lo) pair, optionally nearest-upsampled 2x (mg-cpu.cpp:190-196): output
@@ -664,7 +721,8 @@ struct mgc_vqgan {
     float* part = nullptr;       // split-K partials
     int gn_chunks = 0;
     double* gn_part = nullptr;
-    GnStat* gn_stat = nullptr;
+    float* gn_mean = nullptr;    // [n][C] per-channel group mean
+    float* gn_a = nullptr;       // [n][C] gamma * inv
     int32_t* d_grid = nullptr;
     float* d_img = nullptr;
     std::map<int, cudaGraphExec_t> graphs;   // per image count
@@ -676,7 +734,7 @@ struct mgc_vqgan {
         for (auto& n : norms) { cudaFree(n.g); cudaFree(n.b); }
         for (float* b : buf) cudaFree(b);
         cudaFree(ph); cudaFree(pl);
-        cudaFree(codebook); cudaFree(part); cudaFree(gn_part); cudaFree(gn_stat); cudaFree(d_grid); cudaFree(d_img);
+        cudaFree(codebook); cudaFree(part); cudaFree(gn_part); cudaFree(gn_mean); cudaFree(gn_a); cudaFree(d_grid); cudaFree(d_img);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -781,7 +839,7 @@ struct mgc_vqgan {
             const GgufTensor& b = g.req(name + ".bias");
             if (w.type != 0 || b.type != 0 || w.ne[0] != c || b.ne[0] != c)
                 throw std::runtime_error("vqgan: bad GroupNorm " + name);
-            if (c % groups || c % 4 || kGnThreads % (c / 4)) throw std::runtime_error("vqgan: unsupported channel count");
+            if (c % groups || c % 8 || kGnThreads % (c / 4)) throw std::runtime_error("vqgan: unsupported channel count");
             Norm n;
             n.c = c;
             n.g = dalloc<float>(c);
@@ -839,12 +897,11 @@ struct mgc_vqgan {
         }
         step(Step::GnSilu, 0, -1, -1, -1, add_norm("vqgan.decoder.norm_out", cur), H, W, cur, false);
         const GgufTensor& co = g.req("vqgan.decoder.conv_out.weight");
-        if (co.ne[3] > kSmallOC) throw std::runtime_error("vqgan: conv_out must have at most 4 output channels");
+        if (co.ne[3] > kSmallOC || co.ne[0] != 3) throw std::runtime_error("vqgan: conv_out must be 3x3 with at most 4 outputs");
         step(Step::ConvOut, -1, -1, -1, add_conv("vqgan.decoder.conv_out", cur, (int)co.ne[3], 3, true), -1, H, W, cur,
              false);
-        const size_t co_smem = (size_t)9 * cur * kSmallOC * 4;
-        if (co_smem > 200 * 1024) throw std::runtime_error("vqgan: conv_out input has too many channels");
-        ck(cudaFuncSetAttribute(conv_small_oc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)co_smem),
+        if (co_smem(cur) > 200 * 1024 || cur % kCoCh) throw std::runtime_error("vqgan: unsupported conv_out input channels");
+        ck(cudaFuncSetAttribute(conv_small_oc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)co_smem(cur)),
            "conv_out smem");
         ck(cudaFuncSetAttribute(conv_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<128>::SMEM),
            "conv smem");
@@ -855,6 +912,8 @@ struct mgc_vqgan {
                 throw std::runtime_error("vqgan: conv channel counts must be multiples of 4 (out) and 8 (in)");
         buf_floats = maxf;
     }
+
+    static size_t co_smem(int ic) { return ((size_t)9 * ic * kSmallOC + (size_t)kCoPix * kCoStride) * 4; }
 
     int chunks_for(int n, int HW) const {
         const int want = std::max(1, (2 * sm_count() + n - 1) / n);
@@ -911,7 +970,11 @@ struct mgc_vqgan {
             }
         cudaFree(part); part = dalloc<float>(pf);
         cudaFree(gn_part); gn_part = dalloc<double>(gn_need);
-        cudaFree(gn_stat); gn_stat = dalloc<GnStat>((size_t)n * groups);
+        int maxc = 0;
+        for (const Step& s : prog)
+            if (s.kind == Step::GnSilu) maxc = std::max(maxc, s.C);
+        cudaFree(gn_mean); gn_mean = dalloc<float>((size_t)n * maxc);
+        cudaFree(gn_a); gn_a = dalloc<float>((size_t)n * maxc);
         cudaFree(d_grid); d_grid = dalloc<int32_t>((size_t)n * n_tokens);
         cudaFree(d_img); d_img = dalloc<float>((size_t)n * R * R * 3);
         max_images = n;
@@ -919,7 +982,9 @@ struct mgc_vqgan {
 
     // Enqueue the decoder on `s` for n <= max_images images: grid (device, [n][n_tokens]) ->
     // out (device, [n][R][R][3]).  Returns the number of kernels launched.
-    int enqueue(const int32_t* grid, int n, float* out, cudaStream_t s) {
+    enum OpBit { kGather = 1, kGn = 2, kSplit = 4, kConvTc = 8, kConvSimt = 16, kReduce = 32, kConvOut = 64,
+                 kAll = 127 };
+    int enqueue(const int32_t* grid, int n, float* out, cudaStream_t s, int mask = kAll) {
         int nl = 0;
         for (const Step& stp : prog) {
             const int HW = stp.H * stp.W;
@@ -927,6 +992,7 @@ struct mgc_vqgan {
             case Step::SwapXH:
                 break;
             case Step::Gather: {
+                if (!(mask & kGather)) break;
                 const size_t n4 = (size_t)n * HW * E / 4;
                 launch_k(vq_gather_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, grid, (const float*)codebook,
                          n_codes, E, n4, ph, pl);
@@ -934,6 +1000,7 @@ struct mgc_vqgan {
                 break;
             }
             case Step::Split: {
+                if (!(mask & kSplit)) break;
                 const size_t n4 = (size_t)n * HW * stp.C / 4;
                 const int Hs = stp.up ? stp.H / 2 : stp.H, Ws = stp.up ? stp.W / 2 : stp.W;
                 launch_k(split_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, stp.p_src, Hs, Ws, stp.C,
@@ -942,14 +1009,15 @@ struct mgc_vqgan {
                 break;
             }
             case Step::GnSilu: {
+                if (!(mask & kGn)) break;
                 const Norm& nm = norms[stp.norm];
                 const int nch = chunks_for(n, HW), ppc = (HW + nch - 1) / nch;
                 launch_k(gn_partial_kernel, dim3(nch, n), kGnThreads, 0, s, stp.p_src, HW, nm.c, ppc, gn_part);
-                launch_k(gn_finalize_kernel, n, std::max(32, groups), 0, s, (const double*)gn_part, nch, nm.c, groups,
-                         HW, 1e-5f, gn_stat);
-                const size_t n4 = (size_t)n * HW * nm.c / 4;
-                launch_k(gn_apply_silu_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, stp.p_src,
-                         (const GnStat*)gn_stat, (const float*)nm.g, (const float*)nm.b, HW, nm.c, groups, n4, ph, pl);
+                launch_k(gn_finalize_kernel, dim3(groups, n), kGnFinThreads, 0, s, (const double*)gn_part, nch, nm.c,
+                         groups, HW, 1e-5f, (const float*)nm.g, gn_mean, gn_a);
+                const size_t n8 = (size_t)n * HW * nm.c / 8;
+                launch_k(gn_apply_silu_kernel, (unsigned)((n8 + 255) / 256), 256, 0, s, stp.p_src,
+                         (const float*)gn_mean, (const float*)gn_a, (const float*)nm.b, HW, nm.c, n8, ph, pl);
                 nl += 3;
                 break;
             }
@@ -957,7 +1025,14 @@ struct mgc_vqgan {
                 const Conv& c = convs[stp.conv];
                 const int M = n * HW;
                 int nsu = 1;
-                if (stp.tc) {
+                const bool run_conv = mask & (stp.tc ? kConvTc : kConvSimt);
+                if (!run_conv) {
+                    // (only the split count is needed, for the reduce below)
+                    const int kit = stp.tc ? c.ks * c.ks * c.ic / TC_BK : c.ks * c.ks * c.ic / CBK;
+                    const int ns = stp.tc ? tc_split((M / TC_BM) * (c.oc / c.bn), kit) : simt_split(M, c.oc, kit);
+                    const int kper = (kit + ns - 1) / ns;
+                    nsu = (kit + kper - 1) / kper;
+                } else if (stp.tc) {
                     TcArgs a{};
                     a.wh = c.wh; a.wl = c.wl; a.bias = c.b; a.resid = stp.p_res; a.y = stp.p_dst; a.part = part;
                     a.H = stp.H; a.W = stp.W; a.IC = c.ic; a.OC = c.oc; a.ks = c.ks; a.M = M;
@@ -990,8 +1065,8 @@ struct mgc_vqgan {
                     dim3 gr((M + CBM - 1) / CBM, (c.oc + CBN - 1) / CBN, nsu);
                     launch_k(conv_simt_kernel, gr, 256, 0, s, a);
                 }
-                nl++;
-                if (nsu > 1) {
+                if (run_conv) nl++;
+                if (nsu > 1 && (mask & kReduce)) {
                     const size_t n4 = (size_t)M * c.oc / 4;
                     launch_k(conv_splitk_reduce_kernel, (unsigned)((n4 + 255) / 256), 256, 0, s, (const float*)part, nsu,
                              n4, c.oc, (const float*)c.b, stp.p_res, stp.p_dst);
@@ -1000,17 +1075,48 @@ struct mgc_vqgan {
                 break;
             }
             case Step::ConvOut: {
+                if (!(mask & kConvOut)) break;
                 const Conv& c = convs[stp.conv];
-                const int M = n * HW;
-                const size_t smem = (size_t)c.ks * c.ks * c.ic * kSmallOC * 4;
-                launch_k(conv_small_oc_kernel, (unsigned)((M + 127) / 128), 128, smem, s, (const bf16*)ph,
-                         (const bf16*)pl, (const float*)c.w, (const float*)c.b, out, M, stp.H, stp.W, c.ic, c.oc, c.ks);
+                dim3 gr((stp.W + kCoTile - 1) / kCoTile, (stp.H + kCoTile - 1) / kCoTile, n);
+                launch_k(conv_small_oc_kernel, gr, 256, co_smem(c.ic), s, (const bf16*)ph, (const bf16*)pl,
+                         (const float*)c.w, (const float*)c.b, out, stp.H, stp.W, c.ic, c.oc);
                 nl++;
                 break;
             }
             }
         }
         return nl;
+    }
+
+    // Mean milliseconds of one replay of a graph holding only the launches of `mask` for n images
+    // (on the decoder's buffers, whatever they hold), replayed `iters` times between CUDA events.
+    float time_mask(int mask, int n, int iters, int* nl) {
+        cudaStream_t cap = nullptr;
+        ck(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), "stream");
+        cudaGraph_t gph = nullptr;
+        ck(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal), "capture");
+        *nl = enqueue(d_grid, n, d_img, cap, mask);
+        const cudaError_t e = cudaStreamEndCapture(cap, &gph);
+        cudaStreamDestroy(cap);
+        ck(e, "end capture");
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t ei = cudaGraphInstantiate(&ex, gph, 0);
+        cudaGraphDestroy(gph);
+        ck(ei, "instantiate");
+        cudaEvent_t e0, e1;
+        ck(cudaEventCreate(&e0), "event");
+        ck(cudaEventCreate(&e1), "event");
+        ck(cudaGraphLaunch(ex, st), "graph launch");   // warm-up
+        ck(cudaEventRecord(e0, st), "event");
+        for (int i = 0; i < iters; i++) ck(cudaGraphLaunch(ex, st), "graph launch");
+        ck(cudaEventRecord(e1, st), "event");
+        ck(cudaEventSynchronize(e1), "sync");
+        float ms = 0.f;
+        ck(cudaEventElapsedTime(&ms, e0, e1), "elapsed");
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        cudaGraphExecDestroy(ex);
+        return ms / iters;
     }
 
     // Decode d_grid -> d_img through a CUDA graph captured once per image count.
@@ -1094,6 +1200,24 @@ int mgc_vqgan_decode_device(mgc_vqgan* v, const int32_t* grid_dev, int n_images,
         ck(cudaSetDevice(v->device), "cudaSetDevice");
         v->launches = v->enqueue(grid_dev, n_images, image_dev, (cudaStream_t)stream);
         ck(cudaPeekAtLastError(), "decode launch");
+    });
+}
+
+int mgc_vqgan_time_op(mgc_vqgan* v, const char* op, int n_images, int iters, float* ms_per_replay, int* launches) {
+    return vq_guard([&] {
+        if (!v || !op || !ms_per_replay) throw std::runtime_error("mgc_vqgan_time_op: null argument");
+        if (n_images <= 0 || n_images > v->max_images || iters <= 0)
+            throw std::runtime_error("mgc_vqgan_time_op: n_images must be in [1, max_images], iters positive");
+        static const std::map<std::string, int> ops = {
+            {"gather", mgc_vqgan::kGather}, {"groupnorm", mgc_vqgan::kGn}, {"split", mgc_vqgan::kSplit},
+            {"conv_tc", mgc_vqgan::kConvTc}, {"conv_simt", mgc_vqgan::kConvSimt},
+            {"splitk_reduce", mgc_vqgan::kReduce}, {"conv_out", mgc_vqgan::kConvOut}, {"all", mgc_vqgan::kAll}};
+        auto it = ops.find(op);
+        if (it == ops.end()) throw std::runtime_error(std::string("mgc_vqgan_time_op: unknown op ") + op);
+        ck(cudaSetDevice(v->device), "cudaSetDevice");
+        int nl = 0;
+        *ms_per_replay = v->time_mask(it->second, n_images, iters, &nl);
+        if (launches) *launches = nl;
     });
 }
 

@@ -334,6 +334,12 @@ class VqganDecoder:
     def launches(self) -> int:
         return lib.mgc_vqgan_launches(self._h)
 
+    def time_op(self, op: str, n_images: int = 1, iters: int = 20) -> tuple[float, int]:
+        """(ms per replay, launches) of a graph of one kernel class of the decode."""
+        ms, n = C.c_float(), C.c_int()
+        check(lib.mgc_vqgan_time_op(self._h, op.encode(), n_images, iters, C.byref(ms), C.byref(n)), "vqgan_time_op")
+        return ms.value, n.value
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib.mgc_vqgan_destroy(self._h)

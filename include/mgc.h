@@ -193,6 +193,13 @@ int mgc_vqgan_decode_device(mgc_vqgan* v, const int32_t* grid_dev, int n_images,
                             void* stream);
 /* Kernels the last decode launched (all this library's own). */
 int mgc_vqgan_launches(const mgc_vqgan* v);
+/* Times one kernel class of the decode as it runs inside it: a CUDA graph of that class's
+ * launches only for n_images (op: "conv_tc", "conv_simt", "conv_out", "splitk_reduce",
+ * "groupnorm", "split", "gather" or "all"), on the decoder's own buffers, replayed `iters`
+ * times between CUDA events on its stream; *ms_per_replay = mean ms, *launches (optional) =
+ * kernels per replay. */
+int mgc_vqgan_time_op(mgc_vqgan* v, const char* op, int n_images, int iters, float* ms_per_replay,
+                      int* launches);
 void mgc_vqgan_destroy(mgc_vqgan* v);
 
 #ifdef __cplusplus

