@@ -582,6 +582,7 @@ def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, ba
         ms1, nl1 = dec.time_op("all", 1, iters=steps)
         msb, nlb = dec.time_op("all", batch, iters=steps)
         ops = {op: dec.time_op(op, batch, iters=steps) for op in VQ_OPS}
+        ops1 = {op: dec.time_op(op, 1, iters=steps) for op in VQ_OPS}
         for _ in range(warmup):
             dec.decode(grids[0], out=host_img[:1])
         t0 = time.perf_counter()
@@ -602,6 +603,7 @@ def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, ba
             "e2e_ms_per_image": e2e_ms, "gpu_launches_per_decode": nl1, f"gpu_launches_per_batch{batch}": nlb,
             "conv_gflop_per_image": fl / 1e9,
             f"kernel_ms_per_batch{batch}": {op: {"ms": v[0], "launches": v[1]} for op, v in ops.items()},
+            "kernel_ms_per_image": {op: {"ms": v[0], "launches": v[1]} for op, v in ops1.items()},
             "clocks": clk.summary(),
             "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                          "kernel": f"conv_tc (tcgen05 bf16 hi/lo x3): a graph of the decode's tensor-core conv "

@@ -319,10 +319,26 @@ struct TcArgs {
     const float* resid;
     float* y;
     float* part;
+    double* stats;        // GroupNorm partials of the output or null: [img][tiles_per_img * 4][OC][2]
     int H, W, IC, OC, ks, M;
     int BW, BH, tiles_x, tiles_per_img;
     int m_tiles, n_tiles, kblocks, kper, nsplit, n_units;
 };
+
+// Column sums of a warp's 32 x 32 register block: lane l holds row l's 32 values in a[]; after
+// 31 shuffles lane l holds the sum over the 32 rows of column l in a[0] (fixed order).
+__device__ __forceinline__ void warp_colsum32(float (&a)[32], int lane) {
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1) {
+        const bool up = lane & w;
+#pragma unroll
+        for (int j = 0; j < w; j++) {
+            const float send = up ? a[j] : a[j + w];
+            const float keep = up ? a[j + w] : a[j];
+            a[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+        }
+    }
+}
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar) {
@@ -454,6 +470,7 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
                 tmem_ld_wait();
                 const int col = nt * BN + c * 32;
                 float* o = dst + m * p.OC + col;
+                float sa[32], sq[32];
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     float4 f = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
@@ -469,6 +486,16 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
                         }
                     }
                     *reinterpret_cast<float4*>(o + j) = f;
+                    sa[j] = f.x; sa[j + 1] = f.y; sa[j + 2] = f.z; sa[j + 3] = f.w;
+                }
+                if (p.stats) {   // this warp's 32 pixels: per-channel sum and sum of squares
+#pragma unroll
+                    for (int j = 0; j < 32; j++) sq[j] = sa[j] * sa[j];
+                    warp_colsum32(sa, lane);
+                    warp_colsum32(sq, lane);
+                    double* st = p.stats + ((((size_t)img * p.tiles_per_img + r) * 4 + q) * p.OC + col + lane) * 2;
+                    st[0] = (double)sa[0];
+                    st[1] = (double)sq[0];
                 }
             }
             tc_fence_before();
@@ -697,6 +724,7 @@ struct Step {
     float* p_dst = nullptr;
     const float* p_res = nullptr;
     bool tc = false;
+    bool feeds_gn = false;   // the next step (past swaps) is a GroupNorm of this conv's output
     CUtensorMap mh{}, ml{};
 };
 
@@ -907,6 +935,12 @@ struct mgc_vqgan {
            "conv smem");
         ck(cudaFuncSetAttribute(conv_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<256>::SMEM),
            "conv smem");
+        for (size_t i = 0; i < prog.size(); i++) {
+            if (prog[i].kind != Step::ConvOp) continue;
+            size_t j = i + 1;
+            while (j < prog.size() && prog[j].kind == Step::SwapXH) j++;
+            prog[i].feeds_gn = j < prog.size() && prog[j].kind == Step::GnSilu;
+        }
         for (const Conv& c : convs)
             if (c.oc > kSmallOC && (c.oc % 4 || c.ic % CBK))
                 throw std::runtime_error("vqgan: conv channel counts must be multiples of 4 (out) and 8 (in)");
@@ -967,6 +1001,8 @@ struct mgc_vqgan {
                 }
                 const int kper = (kit + ns - 1) / ns, nsu = (kit + kper - 1) / kper;
                 if (nsu > 1) pf = std::max(pf, (size_t)nsu * M * c.oc);
+                if (s.tc && nsu == 1 && s.feeds_gn)   // epilogue GroupNorm partials: 4 per 128-pixel tile
+                    gn_need = std::max(gn_need, (size_t)M / TC_BM * 4 * c.oc * 2);
             }
         cudaFree(part); part = dalloc<float>(pf);
         cudaFree(gn_part); gn_part = dalloc<double>(gn_need);
@@ -986,8 +1022,10 @@ struct mgc_vqgan {
                  kAll = 127 };
     int enqueue(const int32_t* grid, int n, float* out, cudaStream_t s, int mask = kAll) {
         int nl = 0;
+        int fused_nch = 0;   // > 0: the preceding conv wrote the GroupNorm partials (that many chunks)
         for (const Step& stp : prog) {
             const int HW = stp.H * stp.W;
+            if (stp.kind != Step::SwapXH && stp.kind != Step::GnSilu) fused_nch = 0;
             switch (stp.kind) {
             case Step::SwapXH:
                 break;
@@ -1011,14 +1049,20 @@ struct mgc_vqgan {
             case Step::GnSilu: {
                 if (!(mask & kGn)) break;
                 const Norm& nm = norms[stp.norm];
-                const int nch = chunks_for(n, HW), ppc = (HW + nch - 1) / nch;
-                launch_k(gn_partial_kernel, dim3(nch, n), kGnThreads, 0, s, stp.p_src, HW, nm.c, ppc, gn_part);
+                int nch = fused_nch;
+                fused_nch = 0;
+                if (!nch) {
+                    nch = chunks_for(n, HW);
+                    const int ppc = (HW + nch - 1) / nch;
+                    launch_k(gn_partial_kernel, dim3(nch, n), kGnThreads, 0, s, stp.p_src, HW, nm.c, ppc, gn_part);
+                    nl++;
+                }
                 launch_k(gn_finalize_kernel, dim3(groups, n), kGnFinThreads, 0, s, (const double*)gn_part, nch, nm.c,
                          groups, HW, 1e-5f, (const float*)nm.g, gn_mean, gn_a);
                 const size_t n8 = (size_t)n * HW * nm.c / 8;
                 launch_k(gn_apply_silu_kernel, (unsigned)((n8 + 255) / 256), 256, 0, s, stp.p_src,
                          (const float*)gn_mean, (const float*)gn_a, (const float*)nm.b, HW, nm.c, n8, ph, pl);
-                nl += 3;
+                nl += 2;
                 break;
             }
             case Step::ConvOp: {
@@ -1032,6 +1076,10 @@ struct mgc_vqgan {
                     const int ns = stp.tc ? tc_split((M / TC_BM) * (c.oc / c.bn), kit) : simt_split(M, c.oc, kit);
                     const int kper = (kit + ns - 1) / ns;
                     nsu = (kit + kper - 1) / kper;
+                    if (stp.tc && nsu == 1 && stp.feeds_gn && (mask & kGn)) {
+                        const int BW = std::min(stp.W, 128);
+                        fused_nch = (stp.W / BW) * (stp.H / (TC_BM / BW)) * 4;
+                    }
                 } else if (stp.tc) {
                     TcArgs a{};
                     a.wh = c.wh; a.wl = c.wl; a.bias = c.b; a.resid = stp.p_res; a.y = stp.p_dst; a.part = part;
@@ -1048,6 +1096,10 @@ struct mgc_vqgan {
                     nsu = (a.kblocks + a.kper - 1) / a.kper;
                     a.nsplit = nsu;
                     a.n_units = a.m_tiles * a.n_tiles * nsu;
+                    if (nsu == 1 && stp.feeds_gn && (mask & kGn)) {   // the GroupNorm partials come from the epilogue
+                        a.stats = gn_part;
+                        fused_nch = a.tiles_per_img * 4;
+                    }
                     const int grid_x = std::min(a.n_units, sm_count());
                     if (c.bn == 256)
                         launch_k(conv_tc_kernel<256>, grid_x, 192, TcCfg<256>::SMEM, s, stp.mh, stp.ml, a);
