@@ -57,6 +57,8 @@ _SIGS = {
     "mgc_vqgan_info": (I, [P, P, P, P]),
     "mgc_vqgan_decode": (I, [P, P, I, P]),
     "mgc_vqgan_decode_device": (I, [P, P, I, P, P]),
+    "mgc_vqgan_decode_rgb8": (I, [P, P, I, P]),
+    "mgc_generate_images": (I, [P, P, I, P, P, I, F, P, P]),
     "mgc_vqgan_launches": (I, [P]),
     "mgc_vqgan_time_op": (I, [P, C.c_char_p, I, I, C.POINTER(F), C.POINTER(I)]),
     "mgc_vqgan_destroy": (None, [P]),

@@ -41,6 +41,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -645,6 +646,14 @@ __global__ void vq_gather_kernel(const int32_t* __restrict__ grid, const float* 
     split_store4(yh, yl, i * 4, o);
 }
 
+// The bytes of mg::Image (mg-generate.cpp:141-144): v = min(max(x, 0), 1) * 255 + 0.5, truncated.
+__global__ void rgb8_kernel(const float* __restrict__ img, size_t n, uint8_t* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float v = __fadd_rn(__fmul_rn(fminf(fmaxf(img[i], 0.f), 1.f), 255.f), 0.5f);
+    out[i] = (uint8_t)__float2uint_rz(v);
+}
+
 // ------------------------------------------------------------------------------------------
 // Host side.
 void ck(cudaError_t e, const char* what) {
@@ -753,6 +762,7 @@ struct mgc_vqgan {
     float* gn_a = nullptr;       // [n][C] gamma * inv
     int32_t* d_grid = nullptr;
     float* d_img = nullptr;
+    uint8_t* d_rgb = nullptr;
     std::map<int, cudaGraphExec_t> graphs;   // per image count
     int launches = 0;                         // kernels one decode launches
 
@@ -763,6 +773,7 @@ struct mgc_vqgan {
         for (float* b : buf) cudaFree(b);
         cudaFree(ph); cudaFree(pl);
         cudaFree(codebook); cudaFree(part); cudaFree(gn_part); cudaFree(gn_mean); cudaFree(gn_a); cudaFree(d_grid); cudaFree(d_img);
+        cudaFree(d_rgb);
         if (st) cudaStreamDestroy(st);
     }
 
@@ -1013,6 +1024,7 @@ struct mgc_vqgan {
         cudaFree(gn_a); gn_a = dalloc<float>((size_t)n * maxc);
         cudaFree(d_grid); d_grid = dalloc<int32_t>((size_t)n * n_tokens);
         cudaFree(d_img); d_img = dalloc<float>((size_t)n * R * R * 3);
+        cudaFree(d_rgb); d_rgb = dalloc<uint8_t>((size_t)n * R * R * 3);
         max_images = n;
     }
 
@@ -1242,6 +1254,45 @@ int mgc_vqgan_decode(mgc_vqgan* v, const int32_t* grid, int n_images, float* ima
         ck(cudaMemcpyAsync(image_hwc, v->d_img, no * 4, cudaMemcpyDeviceToHost, v->st), "copy image");
         ck(cudaStreamSynchronize(v->st), "decode");
     });
+}
+
+int mgc_vqgan_decode_rgb8(mgc_vqgan* v, const int32_t* grid, int n_images, uint8_t* rgb) {
+    return vq_guard([&] {
+        if (!v || !grid || !rgb) throw std::runtime_error("mgc_vqgan_decode_rgb8: null argument");
+        if (n_images <= 0 || n_images > v->max_images)
+            throw std::runtime_error("mgc_vqgan_decode_rgb8: n_images must be in [1, max_images]");
+        const size_t nt = (size_t)n_images * v->n_tokens;
+        for (size_t i = 0; i < nt; i++)
+            if (grid[i] < 0 || grid[i] >= v->n_codes) throw std::runtime_error("mgc_vqgan_decode_rgb8: token id out of range");
+        ck(cudaSetDevice(v->device), "cudaSetDevice");
+        ck(cudaMemcpyAsync(v->d_grid, grid, nt * 4, cudaMemcpyHostToDevice, v->st), "copy grid");
+        v->run(n_images, v->st);
+        const size_t no = (size_t)n_images * v->R * v->R * 3;
+        launch_k(rgb8_kernel, (unsigned)((no + 255) / 256), 256, 0, v->st, (const float*)v->d_img, no, v->d_rgb);
+        ck(cudaMemcpyAsync(rgb, v->d_rgb, no, cudaMemcpyDeviceToHost, v->st), "copy image");
+        ck(cudaStreamSynchronize(v->st), "decode");
+    });
+}
+
+int mgc_generate_images(mgc_runtime* rt, mgc_vqgan* v, int B, const int32_t* class_ids, const uint64_t* seeds,
+                        int steps, float temperature, uint8_t* rgb, int32_t* tokens_out) {
+    if (!v || !rt || B <= 0 || !rgb) { set_last_error("mgc_generate_images: bad arguments"); return -1; }
+    const int S = v->n_tokens + 1;
+    std::vector<int32_t> tokens((size_t)B * S);
+    if (mgc_generate(rt, B, class_ids, seeds, steps, temperature, tokens.data()) != 0) return -1;
+    if (tokens_out) std::memcpy(tokens_out, tokens.data(), tokens.size() * sizeof(int32_t));
+    // the final grids (class token dropped, mg-generate.cpp:131-140), decoded in batches
+    std::vector<int32_t> grids((size_t)B * v->n_tokens);
+    for (int i = 0; i < B; i++)
+        std::memcpy(grids.data() + (size_t)i * v->n_tokens, tokens.data() + (size_t)i * S + 1,
+                    sizeof(int32_t) * v->n_tokens);
+    const size_t img_bytes = (size_t)v->R * v->R * 3;
+    for (int i0 = 0; i0 < B; i0 += v->max_images) {
+        const int n = std::min(v->max_images, B - i0);
+        if (mgc_vqgan_decode_rgb8(v, grids.data() + (size_t)i0 * v->n_tokens, n, rgb + (size_t)i0 * img_bytes) != 0)
+            return -1;
+    }
+    return 0;
 }
 
 int mgc_vqgan_decode_device(mgc_vqgan* v, const int32_t* grid_dev, int n_images, float* image_dev, void* stream) {

@@ -289,6 +289,19 @@ class CudaRuntime:
         check(lib.mgc_generate(self._h, B, _ptr(cls), _ptr(sd), steps, temperature, _ptr(out)), "generate")
         return out
 
+    def generate_images(self, vq: "VqganDecoder", class_ids, seeds, steps: int = 8,
+                        temperature: float = 4.5) -> tuple[np.ndarray, np.ndarray]:
+        """mg::generate end to end (mgc_generate_images): uint8 images [B][R][R][3] and the
+        final token sequences [B][n_tokens + 1]."""
+        cls = np.ascontiguousarray(class_ids, np.int32)
+        sd = np.ascontiguousarray(seeds, np.uint64)
+        B, R = len(cls), vq.resolution
+        rgb = np.empty((B, R, R, 3), np.uint8)
+        tok = np.empty((B, self.hparams.n_tokens + 1), np.int32)
+        check(lib.mgc_generate_images(self._h, vq._h, B, _ptr(cls), _ptr(sd), steps, temperature, _ptr(rgb),
+                                      _ptr(tok)), "generate_images")
+        return rgb, tok
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib.mgc_runtime_destroy(self._h)
@@ -324,6 +337,16 @@ class VqganDecoder:
         if out is None:
             out = np.empty((g.shape[0], R, R, 3), np.float32)
         check(lib.mgc_vqgan_decode(self._h, _ptr(g), g.shape[0], _ptr(out)), "vqgan_decode")
+        return out[0] if single else out
+
+    def decode_rgb8(self, grid) -> np.ndarray:
+        """The bytes of the reference's mg::Image (clamp, * 255 + 0.5, truncate): uint8 HWC."""
+        g = np.ascontiguousarray(grid, np.int32)
+        single = g.ndim == 1
+        g = g.reshape(-1, self.n_tokens)
+        R = self.resolution
+        out = np.empty((g.shape[0], R, R, 3), np.uint8)
+        check(lib.mgc_vqgan_decode_rgb8(self._h, _ptr(g), g.shape[0], _ptr(out)), "vqgan_decode_rgb8")
         return out[0] if single else out
 
     def decode_device(self, grid_dev, out_dev, n_images: int) -> None:

@@ -187,6 +187,15 @@ int mgc_vqgan_info(const mgc_vqgan* v, int* n_tokens, int* resolution, int* code
  * host image [n_images][R][R][3] f32, unclamped (mg-generate.cpp:141-144 clamps when it makes
  * bytes).  Synchronous.  Grid cell p = y * sqrt(n_tokens) + x. */
 int mgc_vqgan_decode(mgc_vqgan* v, const int32_t* grid, int n_images, float* image_hwc);
+/* The same, returned as the bytes of the reference's mg::Image (mg-generate.cpp:141-144:
+ * clamp to [0, 1], * 255 + 0.5, truncated), host rgb [n_images][R][R][3] uint8. */
+int mgc_vqgan_decode_rgb8(mgc_vqgan* v, const int32_t* grid, int n_images, uint8_t* rgb);
+/* The whole of mg::generate (src/mg-generate.cpp:39-171) for B images: the decode loop of
+ * mgc_generate on rt, then each final grid (class token dropped) through the VQGAN decoder in
+ * batches of v's max_images, as mgc_vqgan_decode_rgb8.  rgb host [B][R][R][3] uint8;
+ * tokens_out (optional) host [B][n_tokens + 1] as mgc_generate. */
+int mgc_generate_images(mgc_runtime* rt, mgc_vqgan* v, int B, const int32_t* class_ids, const uint64_t* seeds,
+                        int steps, float temperature, uint8_t* rgb, int32_t* tokens_out);
 /* The same on device buffers, enqueued on `stream` (null = legacy default stream) without a
  * sync; ids outside the codebook decode as a zero latent. */
 int mgc_vqgan_decode_device(mgc_vqgan* v, const int32_t* grid_dev, int n_images, float* image_dev,

@@ -5,10 +5,11 @@
 // tests run it and compare its grid with mgc_generate's.  It shows that the C ABI (through
 // include/mgc.hpp) links into, and drives, the reference program unchanged.
 //
-//   mg_generate_cuda MODEL.gguf CLASS SEED STEPS OUT.bin [IMAGE.bin]
+//   mg_generate_cuda MODEL.gguf CLASS SEED STEPS OUT.bin [IMAGE.bin [RGB.bin]]
 //     OUT.bin   = the n_tokens grid (int32)
 //     IMAGE.bin = the decoded image, HWC f32 [R][R][3], from the CUDA VQGAN decoder as the
 //                 VqganFwd callback (given only for a GGUF that carries the decoder)
+//     RGB.bin   = the bytes of the mg::Image that generate() returns
 #include "mg-generate.hpp"
 #include "mg-model.hpp"
 #include "mg-tensor.hpp"
@@ -22,8 +23,8 @@
 #include <vector>
 
 int main(int argc, char** argv) {
-    if (argc != 6 && argc != 7) {
-        std::fprintf(stderr, "usage: %s MODEL.gguf CLASS SEED STEPS OUT.bin [IMAGE.bin]\n", argv[0]);
+    if (argc < 6 || argc > 8) {
+        std::fprintf(stderr, "usage: %s MODEL.gguf CLASS SEED STEPS OUT.bin [IMAGE.bin [RGB.bin]]\n", argv[0]);
         return 2;
     }
     try {
@@ -37,7 +38,7 @@ int main(int argc, char** argv) {
         std::vector<int32_t> grid(n_tok);
         // and, with IMAGE.bin, the VQGAN decoder's VqganFwd
         std::unique_ptr<mgc::Vqgan> vq;
-        if (argc == 7) vq.reset(new mgc::Vqgan(argv[1], 1, 0));
+        if (argc >= 7) vq.reset(new mgc::Vqgan(argv[1], 1, 0));
         std::vector<float> image;
         mg::VqganFwd vq_fwd = vq ? vq->vqgan_fwd() : mg::VqganFwd();
         mg::VqganFwd vfwd = [&](const int32_t* g, float* hwc) {
@@ -52,7 +53,7 @@ int main(int argc, char** argv) {
         cfg.seed = std::strtoull(argv[3], nullptr, 10);
         cfg.steps = std::atoi(argv[4]);
         mg::GenStats stats;
-        mg::generate(*model, cfg, false, fwd, vfwd, &stats, nullptr);
+        const mg::Image img = mg::generate(*model, cfg, false, fwd, vfwd, &stats, nullptr);
         FILE* f = std::fopen(argv[5], "wb");
         if (!f || std::fwrite(grid.data(), sizeof(int32_t), grid.size(), f) != grid.size()) {
             std::fprintf(stderr, "cannot write %s\n", argv[5]);
@@ -66,6 +67,14 @@ int main(int argc, char** argv) {
                 return 1;
             }
             std::fclose(fi);
+        }
+        if (argc == 8) {
+            FILE* fr = std::fopen(argv[7], "wb");
+            if (!fr || std::fwrite(img.rgb.data(), 1, img.rgb.size(), fr) != img.rgb.size()) {
+                std::fprintf(stderr, "cannot write %s\n", argv[7]);
+                return 1;
+            }
+            std::fclose(fr);
         }
         std::printf("transformer_ms %.3f steps %d\n", stats.transformer_ms, stats.steps);
         return 0;

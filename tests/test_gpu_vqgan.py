@@ -158,20 +158,34 @@ def test_reference_generate_drives_cuda_vqgan(tmp_path, oracle_mod):
     spec = synth.ModelSpec(n_layer=2, n_tokens=16, quant="gq8",
                            vqgan=synth.VqganSpec(filters=32, embedding_dim=32))
     path = synth.make_model(tmp_path / "m.gguf", spec)
-    p = subprocess.run([str(exe), str(path), "207", "42", "8", str(tmp_path / "g.bin"), str(tmp_path / "i.bin")],
-                       capture_output=True, text=True, timeout=600)
+    p = subprocess.run([str(exe), str(path), "207", "42", "8", str(tmp_path / "g.bin"), str(tmp_path / "i.bin"),
+                        str(tmp_path / "rgb.bin")], capture_output=True, text=True, timeout=600)
     assert p.returncode == 0, p.stderr
     grid = np.fromfile(tmp_path / "g.bin", np.int32)
     image = np.fromfile(tmp_path / "i.bin", np.float32).reshape(64, 64, 3)
-    r = rt.CudaRuntime(path, max_rows=17)
+    rgb_ref_loop = np.fromfile(tmp_path / "rgb.bin", np.uint8).reshape(64, 64, 3)
+    r = rt.CudaRuntime(path, max_rows=17 * 2)
     toks = r.generate([207], [42], steps=8, temperature=4.5)
-    r.close()
     assert np.array_equal(grid, toks[0, 1:])
-    dec = rt.VqganDecoder(path)
+    dec = rt.VqganDecoder(path, max_images=1)
     assert np.array_equal(image, dec.decode(grid))
+    # mg::generate end to end in the library: the same tokens and the same bytes as the
+    # reference's generate() (its own float -> byte conversion) driving the CUDA callbacks;
+    # two images in batches of one exercise the chunked decode
+    rgb, tok2 = r.generate_images(dec, [207, 207], [42, 42], steps=8, temperature=4.5)
+    assert np.array_equal(tok2[0, 1:], grid) and np.array_equal(tok2[1], tok2[0])
+    assert np.array_equal(rgb[0], rgb_ref_loop) and np.array_equal(rgb[1], rgb_ref_loop)
+    assert np.array_equal(dec.decode_rgb8(grid), rgb_ref_loop)
     dec.close()
+    r.close()
     if oracle_mod.ref_available():
-        _gate(image, oracle_mod.ref_vqgan(path, grid, 64))
+        ref_img = oracle_mod.ref_vqgan(path, grid, 64)
+        _gate(image, ref_img)
+        # bytes from the reference's CPU decoder: equal but where a value sits on a rounding edge
+        ref_rgb = (np.minimum(np.maximum(ref_img, np.float32(0)), np.float32(1)) * np.float32(255)
+                   + np.float32(0.5)).astype(np.uint8)
+        diff = np.abs(ref_rgb.astype(int) - rgb_ref_loop.astype(int))
+        assert diff.max() <= 1 and (diff == 0).mean() > 0.99
 
 
 def test_vqgan_tensor_core_and_simt_paths_agree(vq_models, monkeypatch):
