@@ -24,6 +24,7 @@ F = C.c_float
 _SIGS = {
     "mgc_last_error": (C.c_char_p, []),
     "mgc_device_error": (I, []),
+    "mgc_selftest_wait_timeout": (I, [I, P]),
     "mgc_pack_q8_0": (I, [P, I64, I64, P]),
     "mgc_pack_q4_k": (I, [P, I64, I64, P]),
     "mgc_dequant": (I, [I, P, I64, I64, P]),

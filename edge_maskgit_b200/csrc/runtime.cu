@@ -40,6 +40,19 @@ __global__ void spin_kernel(long long cycles) {
 }
 void launch_spin(long long cycles, cudaStream_t st) { spin_kernel<<<1, 1, 0, st>>>(cycles); }
 
+// Self-test of the bounded-wait path every pipelined kernel uses: waits on an mbarrier that
+// nothing arrives on.  mbar_wait gives up after its cycle limit (~2 s), records `code` in the
+// device error word and returns, so the kernel ends and the context stays usable.
+__global__ void wait_timeout_selftest_kernel(int code) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x != 0) return;
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    mbar_wait(&bar, 0, (volatile int*)&abort_flag, code);
+}
+
 void set_max_shared_carveout(const void* kernel) {
     static std::mutex mu;
     static std::set<std::pair<const void*, int>> done;
@@ -140,6 +153,15 @@ void mgc::set_last_error(const char* msg) { g_err = msg; }
 extern "C" {
 
 const char* mgc_last_error(void) { return g_err.c_str(); }
+
+int mgc_selftest_wait_timeout(int code, void* stream) {
+    return guard([&] {
+        if (code <= 0) throw Err("mgc_selftest_wait_timeout: code must be positive");
+        wait_timeout_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(code);
+        CK(cudaPeekAtLastError());
+        CK(cudaStreamSynchronize((cudaStream_t)stream));
+    });
+}
 
 int mgc_device_error(void) {
     int v = 0;

@@ -1206,6 +1206,18 @@ struct mgc_vqgan {
 };
 
 namespace {
+// After a synchronous decode: a bounded wait inside a conv that timed out left a code in the
+// device error word (the kernel returned early); report it and clear the word.
+void check_vq_dev_error() {
+    int v = 0;
+    ck(cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)), "device error word");
+    if (v != 0) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int));
+        throw std::runtime_error("vqgan: a kernel gave up waiting (device error code " + std::to_string(v) + ")");
+    }
+}
+
 template <class F>
 int vq_guard(F&& f) {
     try { f(); return 0; }
@@ -1253,6 +1265,7 @@ int mgc_vqgan_decode(mgc_vqgan* v, const int32_t* grid, int n_images, float* ima
         const size_t no = (size_t)n_images * v->R * v->R * 3;
         ck(cudaMemcpyAsync(image_hwc, v->d_img, no * 4, cudaMemcpyDeviceToHost, v->st), "copy image");
         ck(cudaStreamSynchronize(v->st), "decode");
+        check_vq_dev_error();
     });
 }
 
@@ -1271,6 +1284,7 @@ int mgc_vqgan_decode_rgb8(mgc_vqgan* v, const int32_t* grid, int n_images, uint8
         launch_k(rgb8_kernel, (unsigned)((no + 255) / 256), 256, 0, v->st, (const float*)v->d_img, no, v->d_rgb);
         ck(cudaMemcpyAsync(rgb, v->d_rgb, no, cudaMemcpyDeviceToHost, v->st), "copy image");
         ck(cudaStreamSynchronize(v->st), "decode");
+        check_vq_dev_error();
     });
 }
 

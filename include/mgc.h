@@ -27,6 +27,10 @@ const char* mgc_last_error(void);
 /* Reads and clears the device-side error word written by bounded waits inside kernels
  * (0 = none).  A non-zero value means a kernel gave up waiting and returned early. */
 int mgc_device_error(void);
+/* Self-test of that path: one kernel waits on an mbarrier nothing arrives on, gives up after
+ * the wait limit (~2 s), records `code` (> 0) in the device error word and returns; the call
+ * syncs `stream`.  mgc_device_error() then returns `code`, and the context stays usable. */
+int mgc_selftest_wait_timeout(int code, void* stream);
 
 /* ------------------------------------------------------------------ weight packing (host)
  * Replaces tools/convert_to_gguf.py quant_q8_0 (:109-124) and quant_q4_k (:68-106):
@@ -185,7 +189,8 @@ int mgc_vqgan_create(const char* gguf_path, int max_images, int device, mgc_vqga
 int mgc_vqgan_info(const mgc_vqgan* v, int* n_tokens, int* resolution, int* codebook_size);
 /* Host grid [n_images][n_tokens] (ids in [0, codebook_size), else -1 and nothing runs) ->
  * host image [n_images][R][R][3] f32, unclamped (mg-generate.cpp:141-144 clamps when it makes
- * bytes).  Synchronous.  Grid cell p = y * sqrt(n_tokens) + x. */
+ * bytes).  Synchronous.  Grid cell p = y * sqrt(n_tokens) + x.  Returns -1 if a kernel gave up
+ * a bounded wait (the device error word, read and cleared). */
 int mgc_vqgan_decode(mgc_vqgan* v, const int32_t* grid, int n_images, float* image_hwc);
 /* The same, returned as the bytes of the reference's mg::Image (mg-generate.cpp:141-144:
  * clamp to [0, 1], * 255 + 0.5, truncated), host rgb [n_images][R][R][3] uint8. */

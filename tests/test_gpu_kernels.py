@@ -202,6 +202,23 @@ def test_no_device_error_left(dev):
     assert rt.device_error() == 0
 
 
+def test_bounded_wait_times_out_and_context_survives(dev, oracle_mod):
+    """A wait that nothing completes (an mbarrier nobody arrives on) gives up after its limit,
+    leaves its code in the device error word and returns; later kernels run normally."""
+    import ctypes as C
+    from edge_maskgit_b200 import runtime as rt
+    from edge_maskgit_b200._lib import lib
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+    assert lib.mgc_selftest_wait_timeout(77, C.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    assert rt.device_error() == 77
+    assert rt.device_error() == 0   # read and cleared
+    x = np.random.default_rng(1).standard_normal((33, 256)).astype(np.float32)
+    qx, dx, _ = rt.quantize_act(_t(x, dev))
+    oq, od, _ = oracle_mod.quantize_act(x)
+    assert np.array_equal(qx.cpu().numpy(), oq) and np.array_equal(dx.cpu().numpy(), od)
+
+
 @pytest.mark.parametrize("wtype", [8, 12])
 @pytest.mark.parametrize("act", [0, 1])
 def test_qgemm_large_m_epilogue(dev, oracle_mod, wtype, act):
