@@ -620,7 +620,7 @@ int attn_prepare() {
 
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
                       size_t scratch_floats, cudaStream_t st, const ActQ* qo, bool qo_c, bool* quantized,
-                      bool prepped) {
+                      bool prepped, long split_ctas) {
     if (quantized) *quantized = false;
     if (Dh != fa::D) return -2;
     int dev = 0;
@@ -631,7 +631,7 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     if (!scratch || scratch_floats < prep_n) return -3;
     // Split the key range over CTAs when (query tiles x heads x images) leaves SMs idle.
     const int qt = (S + fa::BM - 1) / fa::BM, ntiles = (S + fa::BC - 1) / fa::BC;
-    const long ctas = (long)qt * H * B;
+    const long ctas = split_ctas > 0 ? split_ctas : (long)qt * H * B;
     int nsplit = 1;
     if (scratch_floats >= attn_scratch_floats(B, S, H))
         while (nsplit < kAttnMaxSplit && nsplit < ntiles && ctas * (nsplit + 1) <= 2 * 148) nsplit++;

@@ -149,6 +149,8 @@ void launch_gemm_f32(const float* w, const float* x, int M, int N, int K, const 
 // fp16-K/V flash attention, qkv [B*S][3E] -> out [B*S][E]
 // scratch holds the f16 tiles of the prep pass (attn_prep_floats(), required) followed by the
 // key-split partials (splitting is used when scratch_floats >= attn_scratch_floats()).
+// split_ctas > 0: decide the key split as for a launch of that many CTAs (query tiles x heads x
+// images) -- a tensor-parallel rank passes the single-GPU count so its heads split the same way.
 constexpr int kAttnMaxSplit = 4;
 size_t attn_prep_floats(int B, int S, int H);
 size_t attn_scratch_floats(int B, int S, int H);
@@ -156,7 +158,8 @@ size_t attn_scratch_floats(int B, int S, int H);
 // into qo (*quantized = true); otherwise the caller quantizes.
 int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale, float* out, float* scratch,
                       size_t scratch_floats, cudaStream_t st, const ActQ* qo = nullptr, bool qo_c = false,
-                      bool* quantized = nullptr, bool prepped = false);
+                      bool* quantized = nullptr, bool prepped = false,
+                      long split_ctas = 0);
 // where launch_flash_attn expects the prep tiles inside `scratch` (fill them with a fused
 // QKV-GEMM epilogue, then launch with prepped = true)
 AttnPrepOut attn_prep_out(float* scratch, int B, int S, int H);

@@ -465,8 +465,11 @@ void linear(mgc_runtime* rt, const QWeight& w, const float* xin, const ActQ& a, 
 //   tiles at its own column offset) -> all-gather of those int8 tiles in place -> ffn_down ->
 //   all-gather -> LayerNorm.  output_proj and its LayerNorm run replicated; the MLM head is
 //   split by vocabulary rows and its logits all-gathered.
+// Column-split tensor-parallel forward (one stream; the NCCL all-gathers are captured into the
+// step graph).  The attention's key split is chosen from the single-GPU launch shape, so every
+// head is reduced in the same order as on one GPU.
 void enqueue_forward_tp(mgc_runtime* rt, const int32_t* tokens, int B, int S, float* logits) {
-    const int R = B * S, E = rt->E, G = rt->tp_world, g = rt->tp_rank, Eg = rt->Eg, Fg = rt->Fg, Vg = rt->Vg;
+    const int R = B * S, E = rt->E, g = rt->tp_rank, Eg = rt->Eg, Fg = rt->Fg, Vg = rt->Vg;
     cudaStream_t st = rt->st;
     const bool qc = rt->any_q4k;
     const long long slice = (long long)R * Eg;   // floats per rank block of gbuf
@@ -483,6 +486,7 @@ void enqueue_forward_tp(mgc_runtime* rt, const int32_t* tokens, int B, int S, fl
     const int launches0 = g_launch_count;
     launch_embed_ln(rt->tok, rt->V, rt->pos, E, tokens, B, S, rt->g0, rt->b0, rt->eps, rt->x, &rt->aE, qc, st);
     const float scale = 1.0f / std::sqrt((float)rt->Dh);
+    const long attn_ctas = (long)((S + 127) / 128) * rt->n_head * B;   // the single-GPU launch
     // ffn_up writes chunks [g*Fg/128, (g+1)*Fg/128) of the full activation tiles: one contiguous run
     const size_t f_slice = (size_t)(Fg / 128) * (rt->Mpad / 128) * kActTile;
     for (int l = 0; l < rt->n_layer; l++) {
@@ -490,7 +494,7 @@ void enqueue_forward_tp(mgc_runtime* rt, const int32_t* tokens, int B, int S, fl
         const AttnPrepOut ap = attn_prep_out(rt->attn_scratch, B, S, rt->Hl);
         q(L.qkv, rt->aE, L.bqkv, 0, nullptr, 0, nullptr, nullptr, 0, &ap);
         if (launch_flash_attn(nullptr, B, S, rt->Hl, rt->Dh, scale, rt->att, rt->attn_scratch, rt->attn_scratch_n, st,
-                              nullptr, false, nullptr, true) != 0)
+                              nullptr, false, nullptr, true, attn_ctas) != 0)
             throw Err("flash attention launch failed");
         gather(rt->att, rt->gbuf, sizeof(float) * (size_t)slice);
         if (!launch_quant_blocked(rt->gbuf, Eg, slice, R, E, rt->aE, qc, st)) throw Err("gathered quantizer failed");
@@ -513,7 +517,6 @@ void enqueue_forward_tp(mgc_runtime* rt, const int32_t* tokens, int B, int S, fl
     launch_ungather_cols(rt->lgbuf, R, Vg, rt->V, logits, st);
     CK(cudaPeekAtLastError());
     rt->last_launches = g_launch_count - launches0;
-    (void)G;
 }
 
 // Enqueue one transformer forward (build_transformer, mg-transformer.cpp:32-111) on rt->st.
