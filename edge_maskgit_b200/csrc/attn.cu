@@ -63,6 +63,11 @@ __global__ void __launch_bounds__(128) attn_prep(const float* __restrict__ qkv, 
 // max of the scaled scores.
 // FULL: every key of the thread's chunks is valid (all but a key range's last tile), so the
 // per-key masking compiles away.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {   // one three-input max (sm_100)
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 template <int NCH, bool FULL = false>
 __device__ __forceinline__ float tile_row_max(const uint32_t (&r)[NCH][32], int part, int nch, int nvalid, float c1) {
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -70,9 +75,15 @@ __device__ __forceinline__ float tile_row_max(const uint32_t (&r)[NCH][32], int 
     for (int cc = 0; cc < NCH; cc++) {
         const int ch = NCH * part + cc;
         if (!FULL && ch >= nch) break;
+        if (FULL) {   // two new scores per instruction (the max is exact: same result in any order)
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (FULL || ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
+            for (int j = 0; j < 32; j += 2)
+                mx[(j >> 1) & 3] = fmax3(mx[(j >> 1) & 3], __uint_as_float(r[cc][j]), __uint_as_float(r[cc][j + 1]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+                if (ch * 32 + j < nvalid) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(r[cc][j]));
+        }
     }
     return __fmul_rn(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), c1);
 }
