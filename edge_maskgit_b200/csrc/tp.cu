@@ -6,6 +6,7 @@
 // does) the loader returns that copy, otherwise the system library.  Only the five entry points
 // below are used; their C signatures are NCCL's public API (nccl.h).
 #include "kernels.h"
+#include "ptx.cuh"
 #include "tp.h"
 
 #include <dlfcn.h>
@@ -76,6 +77,7 @@ void tp_comm_destroy(ncclComm_t comm) {
 
 // [G][R][Vg] vocabulary slices -> [R][V] row-major logits (columns >= V dropped)
 __global__ void ungather_cols_kernel(const float* __restrict__ src, int R, int Vg, int V, float* __restrict__ dst) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)R * V) return;
     const int r = (int)(i / V), v = (int)(i % V), g = v / Vg;

@@ -94,6 +94,7 @@ struct ConvArgs {
 constexpr int CBM = 128, CBN = 128, CBK = 8, CPAD = 4;
 
 __global__ void __launch_bounds__(256, 2) conv_simt_kernel(ConvArgs a) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     __shared__ __align__(16) float As[2][CBK][CBM + CPAD];
     __shared__ __align__(16) float Bs[2][CBK][CBN];
     const int tid = threadIdx.x;
@@ -190,6 +191,7 @@ __global__ void __launch_bounds__(256, 2) conv_simt_kernel(ConvArgs a) {
 __global__ void conv_splitk_reduce_kernel(const float* __restrict__ part, int nsplit, size_t n4, int OC,
                                           const float* __restrict__ bias, const float* __restrict__ resid,
                                           float* __restrict__ y) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const float4* p = reinterpret_cast<const float4*>(part);
@@ -221,6 +223,7 @@ __global__ void __launch_bounds__(256) conv_small_oc_kernel(const bf16* __restri
                                                             const float* __restrict__ w,
                                                             const float* __restrict__ bias, float* __restrict__ y,
                                                             int H, int W, int IC, int OC) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     extern __shared__ float sm[];
     float* ws = sm;                           // [9][IC][4]
     float* xs = sm + 9 * IC * kSmallOC;       // [kCoPix][kCoStride]
@@ -370,6 +373,7 @@ __global__ void __launch_bounds__(192, 1) conv_tc_kernel(const __grid_constant__
         mbar_fence_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+    griddep_wait();   // activations / residual come from the preceding kernel (no-op without PDL)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -520,6 +524,7 @@ constexpr int kGnThreads = 256;
 
 __global__ void __launch_bounds__(kGnThreads) gn_partial_kernel(const float* __restrict__ x, int HW, int C,
                                                                 int pix_per_chunk, double* __restrict__ part) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     __shared__ double red[kGnThreads * 8];
     const int chunk = blockIdx.x, img = blockIdx.y, nch = gridDim.x;
     const int C4 = C / 4, rows = kGnThreads / C4;   // C4 divides kGnThreads (host checks)
@@ -557,6 +562,7 @@ __global__ void __launch_bounds__(kGnFinThreads) gn_finalize_kernel(const double
                                                                     int G, int HW, float eps,
                                                                     const float* __restrict__ gamma,
                                                                     float* __restrict__ mean_c, float* __restrict__ a_c) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     __shared__ double rs[kGnFinThreads], rss[kGnFinThreads];
     const int g = blockIdx.x, img = blockIdx.y, cpg = C / G, n_items = nch * cpg;
     double s = 0, ss = 0;
@@ -586,6 +592,7 @@ __global__ void __launch_bounds__(kGnFinThreads) gn_finalize_kernel(const double
 __global__ void gn_apply_silu_kernel(const float* __restrict__ x, const float* __restrict__ mean_c,
                                      const float* __restrict__ a_c, const float* __restrict__ beta, int HW, int C,
                                      size_t n8, bf16* __restrict__ yh, bf16* __restrict__ yl) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n8) return;
     const size_t e = i * 8;
@@ -612,6 +619,7 @@ __global__ void gn_apply_silu_kernel(const float* __restrict__ x, const float* _
 // pixel (y, x) reads input (y / 2, x / 2).  H, W: the input's size.
 __global__ void split_kernel(const float* __restrict__ x, int H, int W, int C, int up, size_t n4,
                              bf16* __restrict__ yh, bf16* __restrict__ yl) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const int C4 = C / 4;
@@ -634,6 +642,7 @@ __global__ void split_kernel(const float* __restrict__ x, int H, int W, int C, i
 // [0, codebook) decode as zeros.
 __global__ void vq_gather_kernel(const int32_t* __restrict__ grid, const float* __restrict__ cb, int n_codes, int E,
                                  size_t n4, bf16* __restrict__ yh, bf16* __restrict__ yl) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const int E4 = E / 4;
@@ -648,6 +657,7 @@ __global__ void vq_gather_kernel(const int32_t* __restrict__ grid, const float* 
 
 // The bytes of mg::Image (mg-generate.cpp:141-144): v = min(max(x, 0), 1) * 255 + 0.5, truncated.
 __global__ void rgb8_kernel(const float* __restrict__ img, size_t n, uint8_t* __restrict__ out) {
+    griddep_wait();   // inputs come from the preceding kernel (no-op without PDL)
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float v = __fadd_rn(__fmul_rn(fminf(fmaxf(img[i], 0.f), 1.f), 255.f), 0.5f);
