@@ -20,7 +20,10 @@
 //   and sum through shared memory) -> P split as P_hi = f16(p), P_lo = f16(p - P_hi) (keeps
 //   ~22 bits, like the reference's f32 P) -> O_tile = P_hi V + P_lo V in TMEM -> o = alpha o +
 //   O_tile in registers.
+#include <cstdlib>
+
 #include "kernels.h"
+#include "qgemm_common.cuh"
 #include "ptx.cuh"
 #include "rowquant.cuh"
 #include "attnprep.cuh"
@@ -619,6 +622,7 @@ size_t attn_scratch_floats(int B, int S, int H) {
 
 static bool g_attn_ready[64] = {};
 
+
 int attn_prepare() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
@@ -644,8 +648,13 @@ int launch_flash_attn(const float* qkv, int B, int S, int H, int Dh, float scale
     const int qt = (S + fa::BM - 1) / fa::BM, ntiles = (S + fa::BC - 1) / fa::BC;
     const long ctas = split_ctas > 0 ? split_ctas : (long)qt * H * B;
     int nsplit = 1;
+    static const int max_split = [] {   // MGC_ATTN_MAXSPLIT caps the key split (measurement knob)
+        const char* e = std::getenv("MGC_ATTN_MAXSPLIT");
+        const int v = e ? std::atoi(e) : kAttnMaxSplit;
+        return v < 1 ? 1 : v > kAttnMaxSplit ? kAttnMaxSplit : v;
+    }();
     if (scratch_floats >= attn_scratch_floats(B, S, H))
-        while (nsplit < kAttnMaxSplit && nsplit < ntiles && ctas * (nsplit + 1) <= 2 * 148) nsplit++;
+        while (nsplit < max_split && nsplit < ntiles && ctas * (nsplit + 1) <= 2 * sm_count()) nsplit++;
     const int tiles_per = (ntiles + nsplit - 1) / nsplit;
     nsplit = (ntiles + tiles_per - 1) / tiles_per;   // no empty split
     const int R = B * S;
