@@ -24,7 +24,8 @@
 // implicit GEMM; MGC_VQGAN_SIMT=1 at create time forces that path for every conv.
 //
 // Numerics follow mg-cpu (src/mg-cpu/mg-cpu.cpp): GroupNorm statistics in double
-// (:124-147, variance as E[x^2] - mean^2 over per-chunk double sums), inv = 1/sqrt((float)var +
+// (:124-147, variance as E[x^2] - mean^2 over per-chunk double sums; where the tensor-core conv
+// epilogue supplies them, each chunk is a warp's 32 pixels summed in f32 first), inv = 1/sqrt((float)var +
 // eps) as there; the apply computes xn = (x - mean) * (gamma * inv) + beta in f32 with one fused
 // multiply-add (mg-cpu: (float)(x - mean) * inv, then * gamma + beta, :265-276; a few ulp apart)
 // and xn / (1 + exp(-xn)); convs accumulate in f32 in another order.
