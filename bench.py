@@ -612,6 +612,12 @@ def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, ba
     peak, src = bf16_peak()
     # the tensor-core convs issue 3 bf16 MMAs (hi*hi, hi*lo, lo*hi) per product
     ach = 3 * (fl - fl_out) * batch / (tc_ms * 1e-3) / 1e12
+    traffic = None   # DRAM bytes of the 31 conv launches of an 8-image decode (ncu, profiles/)
+    tf = ROOT / "profiles" / "vqgan_conv_tc_traffic.txt"
+    if tf.exists() and batch == 8:
+        for line in tf.read_text().splitlines():
+            if line.startswith("bytes_per_decode_batch8:"):
+                traffic = float(line.split(":")[1])
     return {"workload": "VQGAN decode, MaskGIT decoder (filters 128, mult 1,1,2,2,4, 16x16 -> 256x256)",
             "parallelism": f"replicas x{world}", "scaling": "weak",
             "ms_per_image": ms1, "images_per_s": world * 1e3 / ms1,
@@ -622,6 +628,7 @@ def vqgan_measure(steps: int, warmup: int, world: int, rank: int, local: int, ba
             "kernel_ms_per_image": {op: {"ms": v[0], "launches": v[1]} for op, v in ops1.items()},
             "clocks": clk.summary(),
             "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                         "traffic": traffic, "traffic_unit": "DRAM bytes per graph replay (the 31 conv launches)",
                          "kernel": f"conv_tc (tcgen05 bf16 hi/lo x3): a graph of the decode's tensor-core conv "
                                    f"launches alone at {batch} images, {tc_ms:.3f} ms; MMA FLOPs = 3 x the conv "
                                    f"FLOPs they compute ({(fl - fl_out) / 1e9:.1f} GFLOP per image)",
